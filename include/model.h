@@ -1,0 +1,29 @@
+/*
+ * model.h — model lifecycle and forward pass (reference include/model.h:6-8).
+ *
+ * vx_model_create   loads a GGUF file (Q4_0 / Q8_0 / F32 tensors, llama
+ *                   architecture) and uploads it to the current CUDA device.
+ * vx_model_forward  appends n_tokens to the model's KV cache at
+ *                   model->cache_len, advances cache_len by n_tokens and writes
+ *                   the logits of the LAST token into the caller's host buffer
+ *                   (n_vocab floats; entries the LM head does not cover hold
+ *                   -1e30, reference src/model.c:604).
+ */
+#ifndef VX_MODEL_H
+#define VX_MODEL_H
+
+#include "veltrix.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+vx_error vx_model_create(const char *path, vx_model **model);
+void vx_model_destroy(vx_model *model);
+vx_error vx_model_forward(vx_model *model, const int *tokens, int n_tokens, float *logits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,86 @@
+"""GPU parity: quantised GEMV (tcgen05 kernel and the exact CUDA-core kernel)
+against the CPU oracle, through the C-ABI (vxc_qgemv / vxc_qgemv_simt).
+
+Tolerance: both kernels accumulate in fp32 from exact integer weights and a
+22-bit activation split (tensor-core path) or fp32 activations (CUDA-core
+path); they differ from the reference only in summation order, so
+max|y_gpu - y_oracle| <= 2e-5 * max|y_oracle| (K <= 11008).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from _paths import oracle
+from qgen import q4_0_blocks, q8_0_blocks
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-5
+
+
+def run_case(torch, qt, rows, cols, M, simt, seed=0):
+    import vxb200
+    rng = np.random.default_rng(seed)
+    blk = (q4_0_blocks if qt == 2 else q8_0_blocks)(rows, cols, rng)
+    x = rng.standard_normal((M, cols)).astype(np.float32)
+    O = oracle()
+    yo = np.zeros((M, rows), np.float32)
+    O.vxo_qgemv(qt, blk.ctypes.data, x.ctypes.data, yo.ctypes.data, M, rows, cols)
+    W = vxb200.QMat(qt, blk, rows, cols)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.full((M, rows), float("nan"), device="cuda")
+    wsb = max(W.workspace_bytes(M), 4)
+    ws = torch.empty(wsb // 4 + 1, device="cuda")
+    W.gemv(xd.data_ptr(), M, yd.data_ptr(), ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream, simt=simt)
+    torch.cuda.synchronize()
+    code = ctypes.c_uint(0)
+    assert vxb200.lib().vxc_check_device_error(ctypes.byref(code)) == 0, code.value
+    y = yd.cpu().numpy()
+    W.close()
+    err = np.max(np.abs(y - yo))
+    return err, np.max(np.abs(yo))
+
+
+@pytest.mark.parametrize("simt", [False, True])
+@pytest.mark.parametrize("qt", [2, 8])
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (11008, 4096)])
+@pytest.mark.parametrize("M", [1, 2, 5, 8])
+def test_config2_shapes(cuda, qt, rows, cols, M, simt):
+    err, mx = run_case(cuda, qt, rows, cols, M, simt)
+    assert err <= TOL * mx, (err, mx)
+
+
+@pytest.mark.parametrize("qt", [2, 8])
+@pytest.mark.parametrize("rows,cols,M", [(100, 256, 3), (130, 64, 1), (4096, 11008, 5), (257, 2048, 17),
+                                         (384, 4096, 40), (512, 1024, 64), (640, 512, 100), (32000, 256, 5)])
+def test_edge_shapes(cuda, qt, rows, cols, M):
+    """Ragged row tiles, the smallest K, M beyond one N tile and beyond 64."""
+    err, mx = run_case(cuda, qt, rows, cols, M, simt=False, seed=rows + M)
+    assert err <= TOL * mx, (err, mx)
+
+
+def test_zero_and_large_activations(cuda):
+    """All-zero rows must give exact zeros; rows spanning 1e-30..1e30 exercise
+    the per-row power-of-two prescale of the activation split."""
+    import vxb200
+    torch = cuda
+    rng = np.random.default_rng(9)
+    rows, cols, M = 256, 512, 4
+    blk = q4_0_blocks(rows, cols, rng)
+    x = rng.standard_normal((M, cols)).astype(np.float32)
+    x[0] = 0
+    x[1] *= 1e30
+    x[2] *= 1e-30
+    O = oracle()
+    yo = np.zeros((M, rows), np.float32)
+    O.vxo_qgemv(2, blk.ctypes.data, x.ctypes.data, yo.ctypes.data, M, rows, cols)
+    W = vxb200.QMat(2, blk, rows, cols)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty((M, rows), device="cuda")
+    wsb = max(W.workspace_bytes(M), 4)
+    ws = torch.empty(wsb // 4 + 1, device="cuda")
+    W.gemv(xd.data_ptr(), M, yd.data_ptr(), ws.data_ptr(), wsb)
+    y = yd.cpu().numpy()
+    assert np.all(y[0] == 0)
+    for m in (1, 2, 3):
+        assert np.max(np.abs(y[m] - yo[m])) <= TOL * np.max(np.abs(yo[m]))

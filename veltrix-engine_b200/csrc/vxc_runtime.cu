@@ -1,0 +1,80 @@
+// vxc_runtime.cu — device selection, error reporting.
+#include "vxc_common.cuh"
+#include "vxc_internal.h"
+
+#include <stdarg.h>
+#include <stdio.h>
+
+static thread_local char t_err[512] = "";
+static unsigned int *g_err_ptr[64];   // per device
+
+void vxc_set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof t_err, fmt, ap);
+    va_end(ap);
+}
+
+extern "C" const char *vxc_error_string(void) { return t_err; }
+
+extern "C" int vxc_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n;
+}
+
+int vxc_require_device(void) {
+    int dev = -1;
+    if (vxc_device_count() <= 0 || cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        vxc_set_error("no CUDA device available (the B200 back end has no CPU fallback)");
+        return -7;
+    }
+    if (dev < 0 || dev >= 64) return -7;
+    if (!g_err_ptr[dev]) {
+        unsigned int *p = NULL;
+        if (cudaMalloc((void **)&p, sizeof(unsigned int)) != cudaSuccess ||
+            cudaMemset(p, 0, sizeof(unsigned int)) != cudaSuccess) {
+            vxc_set_error("cannot allocate the device error word");
+            return -3;
+        }
+        g_err_ptr[dev] = p;
+    }
+    return 0;
+}
+
+unsigned int *vxc_device_error_ptr(void) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return (dev >= 0 && dev < 64) ? g_err_ptr[dev] : NULL;
+}
+
+extern "C" int vxc_device_init(int device) {
+    if (vxc_device_count() <= 0) {
+        vxc_set_error("no CUDA device available (the B200 back end has no CPU fallback)");
+        return -7;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        vxc_set_error("cudaSetDevice(%d) failed", device);
+        return -7;
+    }
+    cudaDeviceProp p;
+    cudaGetDeviceProperties(&p, device);
+    if (p.major < 10) {
+        vxc_set_error("device %d is sm_%d%d; this library is built for sm_100a", device, p.major, p.minor);
+        return -7;
+    }
+    return vxc_require_device();
+}
+
+extern "C" int vxc_check_device_error(unsigned int *code_out) {
+    int rc = vxc_require_device();
+    if (rc) return rc;
+    unsigned int h = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&h, vxc_device_error_ptr(), sizeof h, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(vxc_device_error_ptr(), 0, sizeof h);
+    if (e != cudaSuccess) { vxc_set_error("vxc_check_device_error: %s", cudaGetErrorString(e)); return -3; }
+    if (code_out) *code_out = h;
+    return h ? -3 : 0;
+}
