@@ -29,6 +29,8 @@ extern "C" {
  * counterpart: the reference is CPU-only, src/model.c:377-382 sets threads.) */
 int vxc_device_init(int device);
 int vxc_device_count(void);
+/* Index of the calling thread's current CUDA device, or -1 without one. */
+int vxc_device_current(void);
 const char *vxc_error_string(void);
 /* Read and clear the device-side error word that kernels set instead of
  * trapping (timeouts, out-of-range token ids).  Synchronises the device. */
@@ -65,6 +67,67 @@ int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, void *workspac
  * cores); kept as an independent second implementation for tests. */
 int vxc_qgemv_simt(const vxc_qmat *w, const float *x, int M, float *y, void *workspace,
                    size_t workspace_bytes, void *stream);
+
+/* ---- device model ---------------------------------------------------------- */
+
+/* A host tensor in GGUF layout: type 0 = F32, 2 = Q4_0, 8 = Q8_0; `rows` x
+ * `cols` with cols the contiguous (ne0) dimension.  data == NULL = absent. */
+typedef struct {
+    int type;
+    int rows, cols;
+    const void *data;
+} vxc_tensor_view;
+
+typedef struct {
+    vxc_tensor_view attn_norm, wq, wk, wv, wo, ffn_norm, wg, wu, wd;
+} vxc_layer_views;
+
+/* Llama-family hyper-parameters (reference vx_model_config,
+ * include/veltrix.h:80-102; rope_theta as read by src/gguf.c:533). */
+typedef struct {
+    int n_layers, n_heads, n_kv_heads, n_embd, n_head_dim, n_ff, n_vocab;
+    int max_pos;          /* largest position the RoPE table covers */
+    float rope_theta;
+} vxc_net_config;
+
+typedef struct vxc_net vxc_net;
+typedef struct vxc_seqs vxc_seqs;
+
+/* Upload a model (weights stay resident; QKV and gate/up are fused per
+ * layer).  Replaces the reference's load + consolidate step
+ * (src/model.c:18-111) for the device. */
+int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd, const vxc_tensor_view *out_norm,
+                   const vxc_tensor_view *output, const vxc_layer_views *layers, vxc_net **out);
+void vxc_net_destroy(vxc_net *net);
+int vxc_net_config_get(const vxc_net *net, vxc_net_config *cfg);
+/* Device bytes of weights read by one forward pass (all matrices + norms). */
+size_t vxc_net_weight_bytes(const vxc_net *net);
+
+/* KV cache for n_slots independent sequences of up to max_ctx positions
+ * (fp32, [layer][slot][pos][kv_dim] — reference src/model.c:404-411 keeps
+ * one [layer][n_ctx][kv_dim] cache per model) plus work buffers for up to
+ * max_rows rows per forward call. */
+int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int max_rows, vxc_seqs **out);
+void vxc_seqs_destroy(vxc_seqs *s);
+
+/* Batched forward (reference vx_model_forward, src/model.c:391-628, for many
+ * tokens and sequences at once).  Rows come in n_groups groups of
+ * rows_per_group consecutive tokens; group g belongs to sequence slot
+ * d_slot[g] and its row t sits at position d_pos[g] + t.  K/V of every row
+ * are written into the slot's cache before attention, so each row attends to
+ * positions 0..its own position (causal within the group).  Logits are
+ * produced for the rows listed in d_logit_rows (n_logit_rows of them) into
+ * d_logits[n_logit_rows][n_vocab].  All d_* pointers are device memory;
+ * nothing is copied to the host, so the call can be captured in a CUDA graph.
+ * Rows with an out-of-range token or position raise the device error word. */
+int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
+                int rows_per_group, const int *d_logit_rows, int n_logit_rows, float *d_logits, void *stream);
+
+/* Host-buffer form of vxc_forward for one sequence (the drop-in path of
+ * vx_model_forward): n_tokens host tokens at positions pos0.. of `slot`;
+ * the logits of the last token go to h_logits (n_vocab floats).  Processes
+ * the tokens in chunks of max_rows and synchronises. */
+int vxc_forward_host(vxc_seqs *s, int slot, int pos0, const int *h_tokens, int n_tokens, float *h_logits);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,33 @@
+/*
+ * veltrix_synth.h — synthetic GGUF checkpoints for tests and benchmarks.
+ *
+ * No counterpart in the reference's library API; it follows the fixture
+ * writer of the reference's tests/test_e2e.c:20-160 (llama architecture,
+ * GGUF v3) but places tensor offsets relative to the data section, as the
+ * loader expects (src/gguf.c:231-233).  Weights are N(0, 0.02) from
+ * Philox4x32-10 keyed by (seed, tensor index, element index), quantised with
+ * the reference's Q4_0 rule (src/quantize.c:88-114) or the GGML Q8_0 rule;
+ * norm weights are 1.0.
+ */
+#ifndef VELTRIX_SYNTH_H
+#define VELTRIX_SYNTH_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    int n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab;
+    float rope_theta;
+    int wtype;   /* 2 = Q4_0, 8 = Q8_0 for every 2-D tensor */
+} vx_synth_config;
+
+/* Writes `path`; returns 0 or a vx_error code. */
+int vx_synth_write_gguf(const char *path, const vx_synth_config *cfg, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,71 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+declared in include/*.h, and the public struct layout matches the
+reference's include/veltrix.h (callers read/write vx_model fields)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from _paths import ROOT
+
+HEADERS = ["veltrix.h", "model.h", "speculative.h", "veltrix_cuda.h", "veltrix_synth.h"]
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        p = os.path.join(ROOT, "include", h)
+        if not os.path.exists(p):
+            continue
+        src = open(p).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        src = re.sub(r"//[^\n]*", "", src)
+        for m in re.finditer(r"^[A-Za-z_][\w\s\*]*?\b(vx\w+)\s*\(", src, flags=re.M):
+            if "typedef" in m.group(0):
+                continue
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    import vxb200
+    L = vxb200.lib()
+    names = declared_functions()
+    assert len(names) > 20
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_binding_prototypes_cover_headers():
+    import vxb200
+    missing = [n for n in declared_functions() if n not in vxb200.PROTOTYPES]
+    assert not missing, missing
+
+
+def test_vx_model_layout_matches_c(tmp_path):
+    """offsetof(vx_model, cache_len/config.n_ctx) in C == the ctypes mirror."""
+    import vxb200
+    src = tmp_path / "o.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "veltrix.h"\n'
+                   'int main(){printf("%zu %zu %zu\\n", offsetof(vx_model, cache_len), '
+                   'offsetof(vx_model, config.n_ctx), sizeof(vx_model_config));return 0;}\n')
+    exe = tmp_path / "o"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    a, b, c = map(int, subprocess.run([str(exe)], capture_output=True, text=True).stdout.split())
+    assert a == vxb200.ModelHead.cache_len.offset
+    assert b == vxb200.ModelConfig.n_ctx.offset
+    assert c == ctypes.sizeof(vxb200.ModelConfig)
+
+
+def test_no_device_fails_loudly():
+    """Without a CUDA device every entry point fails: no CPU fallback."""
+    import vxb200
+    L = vxb200.lib()
+    if L.vxc_device_count() > 0:
+        pytest.skip("a CUDA device is present")
+    assert L.vxc_device_init(0) != 0
+    assert b"no CUDA device" in L.vxc_error_string()
+    h = ctypes.c_void_p()
+    assert L.vx_model_create(b"/nonexistent.gguf", ctypes.byref(h)) != 0

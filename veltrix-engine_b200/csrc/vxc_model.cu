@@ -1,0 +1,687 @@
+// vxc_model.cu — device-resident Llama-family forward pass over many rows and
+// sequences (reference src/model.c:391-628, scalar semantics).
+//
+// Per layer, for M = n_groups * rows_per_group rows:
+//   h   = rmsnorm(x) * attn_norm                      (src/model.c:518, src/tensor.c:132-140)
+//   qkv = [Wq;Wk;Wv] h                                 fused GEMV (src/model.c:522-536)
+//   rope(q,k) at each row's position; k,v -> cache    (src/tensor.c:249-270, src/model.c:291-296)
+//   att = softmax(q k^T / sqrt(hd)) v, causal          (src/model.c:299-338)
+//   x  += Wo att                                       (out-of-place fix of src/model.c:543-546)
+//   h   = rmsnorm(x) * ffn_norm
+//   [g;u] = [Wg;Wu] h ; s = silu(g) ; f = |s|<0.01 ? 0 : s*u   (src/model.c:580-585)
+//   x  += Wd f                                         (src/model.c:587-589)
+// logits = Wout rmsnorm(x) * out_norm for the requested rows (src/model.c:598-615).
+//
+// RoPE uses a host-built (cos, sin) table computed exactly as the reference
+// does (freq = 1/powf(theta, 2i/hd), val = pos*freq, cosf/sinf), and the
+// rotation is written with explicitly rounded ops, so it matches the
+// reference bit-for-bit.  The KV cache is fp32 ([layer][slot][pos][kv_dim]).
+#include "vxc_common.cuh"
+#include "vxc_qmat.cuh"
+#include "vxc_internal.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <vector>
+
+struct vxc_layer_dev {
+    float *attn_norm, *ffn_norm;   // never NULL (ones when the GGUF has none)
+    vxc_qmat *wqkv, *wo, *wgu, *wd;
+};
+
+struct vxc_net {
+    vxc_net_config cfg;
+    int embd_type;
+    uint8_t *embd;           // raw GGUF rows
+    size_t embd_row_bytes;
+    int embd_rows, embd_cols;
+    float *out_norm;         // NULL when absent (no final norm, src/model.c:600)
+    vxc_qmat *out;           // LM head
+    vxc_layer_dev *layers;
+    float2 *rope;            // [max_pos][hd/2]
+    size_t weight_bytes;
+};
+
+struct vxc_seqs {
+    const vxc_net *net;
+    int n_slots, max_ctx, max_rows;
+    float *k, *v;            // [L][slots][ctx][kvd]
+    float *x, *h, *qkv, *att, *gu, *hf, *o;
+    void *gemv_ws;
+    size_t gemv_ws_bytes;
+    float *attn_part;
+    int attn_sl, attn_splits;
+};
+
+#define ATTN_QC 16      // queries per attention CTA
+#define ATTN_T 32       // key positions per smem tile
+
+// ---------------------------------------------------------------------------
+// kernels
+// ---------------------------------------------------------------------------
+__global__ void k_embed(const uint8_t *__restrict__ embd, int type, size_t row_bytes, int vocab, int E,
+                        const int *__restrict__ tokens, float *__restrict__ x, unsigned int *err) {
+    const int m = blockIdx.x;
+    const int tok = tokens[m];
+    float *xr = x + (size_t)m * E;
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0) vxc_flag_error(err, VXC_DERR_BAD_TOKEN);
+        for (int i = threadIdx.x; i < E; i += blockDim.x) xr[i] = 0.0f;
+        return;
+    }
+    const uint8_t *row = embd + (size_t)tok * row_bytes;
+    if (type == 0) {
+        const float *f = reinterpret_cast<const float *>(row);
+        for (int i = threadIdx.x; i < E; i += blockDim.x) xr[i] = f[i];
+        return;
+    }
+    // one thread per element: block b = i/32 (src/quantize.c:578-591, :642-651)
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+        int b = i >> 5, j = i & 31;
+        if (type == 2) {
+            const uint8_t *blk = row + (size_t)b * 18;
+            float d = vxc_h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+            uint8_t byte = blk[2 + (j >> 1)];
+            int q = (j & 1) ? (byte >> 4) : (byte & 0x0F);
+            xr[i] = (float)(q - 8) * d;
+        } else {
+            const uint8_t *blk = row + (size_t)b * 34;
+            float d = vxc_h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+            xr[i] = (float)(int8_t)blk[2 + j] * d;
+        }
+    }
+}
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += red[i];
+    return t;
+}
+
+// out[m] = w * (x[src] * (1/sqrt(sum(x^2)/E + 1e-5)))  (src/tensor.c:132-140)
+__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, int E,
+                          const int *__restrict__ rows, float *__restrict__ out) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    const int src = rows ? rows[m] : m;
+    const float *xr = x + (size_t)src * E;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < E; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    ss = block_sum(ss, red);
+    float rms = sqrtf(ss / (float)E + 1e-5f);
+    float *o = out + (size_t)m * E;
+    if (rms < 1e-10f) {
+        for (int i = threadIdx.x; i < E; i += blockDim.x) o[i] = 0.0f;
+        return;
+    }
+    float inv = 1.0f / rms;
+    for (int i = threadIdx.x; i < E; i += blockDim.x) o[i] = __fmul_rn(w[i], __fmul_rn(xr[i], inv));
+}
+
+// RoPE on q (in place) and k, then k, v -> cache at the row's position.
+__global__ void k_rope_kv(float *__restrict__ qkv, int T, const int *__restrict__ d_slot,
+                          const int *__restrict__ d_pos, const float2 *__restrict__ rope, int max_pos, int H,
+                          int KH, int hd, float *__restrict__ kc, float *__restrict__ vc, int n_slots,
+                          int max_ctx, unsigned int *err) {
+    const int m = blockIdx.x;
+    const int g = m / T, t = m % T;
+    const int slot = d_slot[g];
+    const int pos = d_pos[g] + t;
+    const int E = H * hd, kvd = KH * hd;
+    float *row = qkv + (size_t)m * (E + 2 * kvd);
+    if (pos < 0 || pos >= max_ctx || pos >= max_pos || slot < 0 || slot >= n_slots) {
+        if (threadIdx.x == 0) vxc_flag_error(err, VXC_DERR_CTX_FULL);
+        return;
+    }
+    const int np = hd / 2;
+    const float2 *cs = rope + (size_t)pos * np;
+    float *kdst = kc + ((size_t)slot * max_ctx + pos) * kvd;
+    float *vdst = vc + ((size_t)slot * max_ctx + pos) * kvd;
+    for (int i = threadIdx.x; i < (H + KH) * np; i += blockDim.x) {
+        int head = i / np, p = i % np;
+        float2 c = cs[p];
+        float *v = head < H ? row + (size_t)head * hd + 2 * p : row + E + (size_t)(head - H) * hd + 2 * p;
+        float a = v[0], b = v[1];
+        // a*cr - b*ci ; a*ci + b*cr with the reference's separate roundings
+        float r0 = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+        float r1 = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+        if (head < H) {
+            v[0] = r0;
+            v[1] = r1;
+        } else {
+            int off = (head - H) * hd + 2 * p;
+            kdst[off] = r0;
+            kdst[off + 1] = r1;
+        }
+    }
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) vdst[i] = row[E + kvd + i];
+}
+
+// Decode/verify attention, split over the context.  CTA = (group g, kv head,
+// query chunk) x split.  Queries are the rows of group g times the q heads of
+// the kv head (GQA mapping kv_h = h*KH/H, src/model.c:303).  Each CTA writes
+// per query: running max m, sum l of exp(s - m), and o = sum exp(s - m) v.
+__global__ void __launch_bounds__(128) k_attn_partial(const float *__restrict__ qkv, int T,
+                                                      const int *__restrict__ d_slot,
+                                                      const int *__restrict__ d_pos, int H, int KH, int hd,
+                                                      const float *__restrict__ kc, const float *__restrict__ vc,
+                                                      int max_ctx, int SL, int nqc, float *__restrict__ part) {
+    extern __shared__ float sm[];
+    const int G = H / KH;
+    const int nq = T * G;
+    const int bx = blockIdx.x;
+    const int qc = bx % nqc;
+    const int kvh = (bx / nqc) % KH;
+    const int g = bx / (nqc * KH);
+    const int split = blockIdx.y;
+    const int nsplit = gridDim.y;
+    const int q0 = qc * ATTN_QC;
+    const int nql = min(ATTN_QC, nq - q0);
+    const int E = H * hd, kvd = KH * hd;
+    const int slot = d_slot[g];
+    const int base = d_pos[g];
+    const int p0 = split * SL;
+    const int pend = min(p0 + SL, base + T);        // exclusive, causal bound of the group
+    const int tid = threadIdx.x;
+    const int hdp = hd + 1;
+    float *qs = sm;                                 // [QC][hd]
+    float *ks = qs + ATTN_QC * hd;                  // [T][hd+1]
+    float *sc = ks + ATTN_T * hdp;                  // [QC][SL]
+    const float scale = 1.0f / sqrtf((float)hd);
+    // part layout: [g][kvh][q][split][hd + 2]
+    auto part_ptr = [&](int q) {
+        return part + ((((size_t)g * KH + kvh) * (size_t)nq + q) * nsplit + split) * (hd + 2);
+    };
+    if (nql <= 0) return;
+    if (p0 >= pend) {
+        for (int i = tid; i < nql; i += blockDim.x) {
+            float *pp = part_ptr(q0 + i);
+            pp[0] = -INFINITY;
+            pp[1] = 0.0f;
+        }
+        return;
+    }
+    const int npos = pend - p0;
+    for (int i = tid; i < nql * hd; i += blockDim.x) {
+        int ql = i / hd, d = i % hd;
+        int q = q0 + ql;
+        int t = q / G, j = q % G;
+        int h = kvh * G + j;
+        qs[ql * hd + d] = qkv[(size_t)(g * T + t) * (E + 2 * kvd) + (size_t)h * hd + d];
+    }
+    const float *kbase = kc + (size_t)slot * max_ctx * kvd + (size_t)kvh * hd;
+    const float *vbase = vc + (size_t)slot * max_ctx * kvd + (size_t)kvh * hd;
+    // scores
+    for (int t0 = 0; t0 < npos; t0 += ATTN_T) {
+        const int nt = min(ATTN_T, npos - t0);
+        __syncthreads();
+        for (int i = tid; i < nt * hd; i += blockDim.x) {
+            int r = i / hd, d = i % hd;
+            ks[r * hdp + d] = kbase[(size_t)(p0 + t0 + r) * kvd + d];
+        }
+        __syncthreads();
+        for (int i = tid; i < nql * ATTN_T; i += blockDim.x) {
+            int ql = i / ATTN_T, r = i % ATTN_T;
+            if (r >= nt) continue;
+            int t = (q0 + ql) / G;
+            int pos = p0 + t0 + r;
+            float s = -INFINITY;
+            if (pos <= base + t) {
+                const float *qv = qs + ql * hd, *kv = ks + r * hdp;
+                float a = 0.0f;
+                for (int d = 0; d < hd; d++) a = fmaf(qv[d], kv[d], a);
+                s = a * scale;
+            }
+            sc[ql * SL + t0 + r] = s;
+        }
+    }
+    __syncthreads();
+    // per-query max and exp-sum over this split (one warp per query)
+    const int w = tid >> 5, l = tid & 31;
+    __shared__ float qmax[ATTN_QC], qsum[ATTN_QC];
+    for (int ql = w; ql < nql; ql += 4) {
+        float mx = -INFINITY;
+        for (int i = l; i < npos; i += 32) mx = fmaxf(mx, sc[ql * SL + i]);
+        mx = warp_max(mx);
+        float su = 0.0f;
+        for (int i = l; i < npos; i += 32) {
+            float s = sc[ql * SL + i];
+            float e = (s == -INFINITY) ? 0.0f : expf(s - mx);
+            sc[ql * SL + i] = e;
+            su += e;
+        }
+        su = warp_sum(su);
+        if (l == 0) { qmax[ql] = mx; qsum[ql] = su; }
+    }
+    // o = sum e * v
+    float acc[ATTN_QC];
+#pragma unroll
+    for (int i = 0; i < ATTN_QC; i++) acc[i] = 0.0f;
+    for (int t0 = 0; t0 < npos; t0 += ATTN_T) {
+        const int nt = min(ATTN_T, npos - t0);
+        __syncthreads();
+        for (int i = tid; i < nt * hd; i += blockDim.x) {
+            int r = i / hd, d = i % hd;
+            ks[r * hdp + d] = vbase[(size_t)(p0 + t0 + r) * kvd + d];
+        }
+        __syncthreads();
+        for (int d = tid; d < hd; d += blockDim.x) {
+            // hd <= 128 = blockDim.x: one pass
+#pragma unroll
+            for (int ql = 0; ql < ATTN_QC; ql++) {
+                if (ql < nql) {
+                    float a = acc[ql];
+                    for (int r = 0; r < nt; r++) a = fmaf(sc[ql * SL + t0 + r], ks[r * hdp + d], a);
+                    acc[ql] = a;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    for (int d = tid; d < hd; d += blockDim.x) {
+#pragma unroll
+        for (int ql = 0; ql < ATTN_QC; ql++)
+            if (ql < nql) part_ptr(q0 + ql)[2 + d] = acc[ql];
+    }
+    if (tid < nql) {
+        float *pp = part_ptr(q0 + tid);
+        pp[0] = qmax[tid];
+        pp[1] = qsum[tid];
+    }
+}
+
+// out = (sum_i e^{m_i-M} o_i) / (sum_i e^{m_i-M} l_i + 1e-10)  (vx_softmax's +1e-10, src/tensor.c:168)
+__global__ void k_attn_combine(const float *__restrict__ part, int T, int H, int KH, int hd, int nsplit,
+                               float *__restrict__ att) {
+    const int G = H / KH, nq = T * G;
+    const int idx = blockIdx.x;             // (g, kvh, q)
+    const int q = idx % nq;
+    const int kvh = (idx / nq) % KH;
+    const int g = idx / (nq * KH);
+    const float *pp = part + (size_t)idx * nsplit * (hd + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; s++) M = fmaxf(M, pp[(size_t)s * (hd + 2)]);
+    float Ls = 0.0f;
+    for (int s = 0; s < nsplit; s++) {
+        float ms = pp[(size_t)s * (hd + 2)];
+        if (ms != -INFINITY) Ls += expf(ms - M) * pp[(size_t)s * (hd + 2) + 1];
+    }
+    const float inv = 1.0f / (Ls + 1e-10f);
+    const int t = q / G, h = kvh * G + q % G;
+    float *dst = att + (size_t)(g * T + t) * (H * hd) + (size_t)h * hd;
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float o = 0.0f;
+        for (int s = 0; s < nsplit; s++) {
+            float ms = pp[(size_t)s * (hd + 2)];
+            if (ms != -INFINITY) o += expf(ms - M) * pp[(size_t)s * (hd + 2) + 2 + d];
+        }
+        dst[d] = o * inv;
+    }
+}
+
+// f = |silu(g)| < 0.01 ? 0 : silu(g) * u   (src/model.c:580-585, src/tensor.c:71-88, :277)
+__global__ void k_swiglu(const float *__restrict__ gu, int M, int F, float *__restrict__ hf) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)M * F) return;
+    size_t m = i / F, j = i % F;
+    float g = gu[m * 2 * F + j];
+    float u = gu[m * 2 * F + F + j];
+    float s = g / (1.0f + expf(-g));
+    hf[i] = (fabsf(s) < 0.01f) ? __fmul_rn(s, 0.0f) : __fmul_rn(s, u);
+}
+
+__global__ void k_add(float *__restrict__ x, const float *__restrict__ o, size_t n) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __fadd_rn(x[i], o[i]);
+}
+
+__global__ void k_fill(float *__restrict__ p, size_t n, float v) {
+    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+// ---------------------------------------------------------------------------
+// host: upload
+// ---------------------------------------------------------------------------
+static size_t row_bytes_of(int type, int cols) {
+    if (type == 2) return (size_t)(cols / 32) * 18;
+    if (type == 8) return (size_t)(cols / 32) * 34;
+    return (size_t)cols * 4;
+}
+
+static int upload_f32_or_ones(const vxc_tensor_view *t, int n, float **out) {
+    std::vector<float> h(n, 1.0f);
+    if (t && t->data && t->type == 0 && t->rows * t->cols >= n) memcpy(h.data(), t->data, (size_t)n * 4);
+    VXC_CUDA_OK(cudaMalloc((void **)out, (size_t)n * 4));
+    VXC_CUDA_OK(cudaMemcpy(*out, h.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+    return 0;
+}
+
+// Concatenate matrices by rows (same type and cols) and upload as one qmat.
+static int upload_fused(const vxc_tensor_view *const *parts, int n, vxc_qmat **out) {
+    int type = parts[0]->type, cols = parts[0]->cols, rows = 0;
+    for (int i = 0; i < n; i++) {
+        if (!parts[i]->data || parts[i]->type != type || parts[i]->cols != cols) {
+            vxc_set_error("fused matrix parts differ in type/shape or are missing");
+            return -7;
+        }
+        rows += parts[i]->rows;
+    }
+    if (type != 2 && type != 8) {
+        vxc_set_error("weight type %d not supported on the device (Q4_0 / Q8_0 only)", type);
+        return -7;
+    }
+    size_t rb = row_bytes_of(type, cols);
+    std::vector<uint8_t> buf;
+    const void *src = parts[0]->data;
+    if (n > 1) {
+        buf.resize(rb * rows);
+        size_t off = 0;
+        for (int i = 0; i < n; i++) {
+            memcpy(buf.data() + off, parts[i]->data, rb * parts[i]->rows);
+            off += rb * parts[i]->rows;
+        }
+        src = buf.data();
+    }
+    return vxc_qmat_create(type, src, rows, cols, out);
+}
+
+static size_t qmat_bytes(const vxc_qmat *w) { return w ? w->qs_bytes + w->sc_bytes : 0; }
+
+extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
+                              const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
+                              const vxc_layer_views *layers, vxc_net **out) {
+    int rc = vxc_require_device();
+    if (rc) return rc;
+    if (!cfg || !tok_embd || !tok_embd->data || !layers || !out || cfg->n_layers <= 0 || cfg->n_heads <= 0 ||
+        cfg->n_kv_heads <= 0 || cfg->n_heads % cfg->n_kv_heads || cfg->n_head_dim % 2 || cfg->n_head_dim > 128 ||
+        cfg->n_embd != cfg->n_heads * cfg->n_head_dim || cfg->n_embd % 32 || cfg->n_ff % 32) {
+        vxc_set_error("vxc_net_create: unsupported configuration");
+        return -4;
+    }
+    vxc_net *n = (vxc_net *)calloc(1, sizeof(vxc_net));
+    n->cfg = *cfg;
+    const int E = cfg->n_embd, L = cfg->n_layers;
+    // embedding rows (raw)
+    n->embd_type = tok_embd->type;
+    n->embd_rows = tok_embd->rows;
+    n->embd_cols = tok_embd->cols;
+    n->embd_row_bytes = row_bytes_of(tok_embd->type, tok_embd->cols);
+    size_t eb = n->embd_row_bytes * tok_embd->rows;
+    if (cudaMalloc((void **)&n->embd, eb) != cudaSuccess ||
+        cudaMemcpy(n->embd, tok_embd->data, eb, cudaMemcpyHostToDevice) != cudaSuccess) {
+        vxc_set_error("vxc_net_create: embedding upload failed");
+        vxc_net_destroy(n);
+        return -3;
+    }
+    if (out_norm && out_norm->data) {
+        if ((rc = upload_f32_or_ones(out_norm, E, &n->out_norm))) { vxc_net_destroy(n); return rc; }
+    }
+    const vxc_tensor_view *ow = (output && output->data) ? output : tok_embd;   // src/format.c:238
+    {
+        const vxc_tensor_view *p[1] = {ow};
+        if ((rc = upload_fused(p, 1, &n->out))) { vxc_net_destroy(n); return rc; }
+    }
+    n->layers = (vxc_layer_dev *)calloc((size_t)L, sizeof(vxc_layer_dev));
+    size_t wb = qmat_bytes(n->out) + (size_t)E * 4;
+    for (int l = 0; l < L; l++) {
+        const vxc_layer_views *lv = &layers[l];
+        vxc_layer_dev *d = &n->layers[l];
+        if ((rc = upload_f32_or_ones(&lv->attn_norm, E, &d->attn_norm)) ||
+            (rc = upload_f32_or_ones(&lv->ffn_norm, E, &d->ffn_norm))) { vxc_net_destroy(n); return rc; }
+        const vxc_tensor_view *qkv[3] = {&lv->wq, &lv->wk, &lv->wv};
+        const vxc_tensor_view *o[1] = {&lv->wo};
+        const vxc_tensor_view *gu[2] = {&lv->wg, &lv->wu};
+        const vxc_tensor_view *dn[1] = {&lv->wd};
+        if ((rc = upload_fused(qkv, 3, &d->wqkv)) || (rc = upload_fused(o, 1, &d->wo)) ||
+            (rc = upload_fused(gu, 2, &d->wgu)) || (rc = upload_fused(dn, 1, &d->wd))) {
+            vxc_net_destroy(n);
+            return rc;
+        }
+        wb += qmat_bytes(d->wqkv) + qmat_bytes(d->wo) + qmat_bytes(d->wgu) + qmat_bytes(d->wd) + 2ull * E * 4;
+    }
+    n->weight_bytes = wb;
+    // RoPE table exactly as src/tensor.c:180-187 computes it per call
+    const int hd = cfg->n_head_dim, np = hd / 2, P = cfg->max_pos > 0 ? cfg->max_pos : 4096;
+    n->cfg.max_pos = P;
+    std::vector<float2> tab((size_t)P * np);
+    std::vector<float> freq(np);
+    for (int i = 0; i < np; i++) freq[i] = 1.0f / powf(cfg->rope_theta, (float)(i * 2) / hd);
+    for (int p = 0; p < P; p++)
+        for (int i = 0; i < np; i++) {
+            float val = p * freq[i];
+            tab[(size_t)p * np + i] = make_float2(cosf(val), sinf(val));
+        }
+    if (cudaMalloc((void **)&n->rope, tab.size() * sizeof(float2)) != cudaSuccess ||
+        cudaMemcpy(n->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess) {
+        vxc_set_error("vxc_net_create: rope table upload failed");
+        vxc_net_destroy(n);
+        return -3;
+    }
+    *out = n;
+    return 0;
+}
+
+extern "C" void vxc_net_destroy(vxc_net *n) {
+    if (!n) return;
+    if (n->embd) cudaFree(n->embd);
+    if (n->out_norm) cudaFree(n->out_norm);
+    vxc_qmat_destroy(n->out);
+    if (n->layers) {
+        for (int l = 0; l < n->cfg.n_layers; l++) {
+            vxc_layer_dev *d = &n->layers[l];
+            if (d->attn_norm) cudaFree(d->attn_norm);
+            if (d->ffn_norm) cudaFree(d->ffn_norm);
+            vxc_qmat_destroy(d->wqkv);
+            vxc_qmat_destroy(d->wo);
+            vxc_qmat_destroy(d->wgu);
+            vxc_qmat_destroy(d->wd);
+        }
+        free(n->layers);
+    }
+    if (n->rope) cudaFree(n->rope);
+    free(n);
+}
+
+extern "C" int vxc_net_config_get(const vxc_net *n, vxc_net_config *cfg) {
+    if (!n || !cfg) return -4;
+    *cfg = n->cfg;
+    return 0;
+}
+
+extern "C" size_t vxc_net_weight_bytes(const vxc_net *n) { return n ? n->weight_bytes : 0; }
+
+// ---------------------------------------------------------------------------
+// host: sequences + forward
+// ---------------------------------------------------------------------------
+static size_t attn_smem(int hd, int SL) {
+    return ((size_t)ATTN_QC * hd + (size_t)ATTN_T * (hd + 1) + (size_t)ATTN_QC * SL) * sizeof(float);
+}
+
+extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int max_rows, vxc_seqs **out) {
+    if (!net || !out || n_slots <= 0 || max_ctx <= 0 || max_rows <= 0) { vxc_set_error("vxc_seqs_create: bad args"); return -4; }
+    int rc = vxc_require_device();
+    if (rc) return rc;
+    const vxc_net_config &c = net->cfg;
+    if (max_ctx > c.max_pos) { vxc_set_error("vxc_seqs_create: max_ctx %d > rope table %d", max_ctx, c.max_pos); return -4; }
+    vxc_seqs *s = (vxc_seqs *)calloc(1, sizeof(vxc_seqs));
+    s->net = net;
+    s->n_slots = n_slots;
+    s->max_ctx = max_ctx;
+    s->max_rows = max_rows;
+    const int E = c.n_embd, kvd = c.n_kv_heads * c.n_head_dim, F = c.n_ff, hd = c.n_head_dim;
+    size_t kvn = (size_t)c.n_layers * n_slots * max_ctx * kvd;
+    // attention split length: at most 16 splits, tiles of 32 positions
+    int SL = (max_ctx + 15) / 16;
+    SL = ((SL + ATTN_T - 1) / ATTN_T) * ATTN_T;
+    if (SL < 256) SL = 256;
+    s->attn_sl = SL;
+    s->attn_splits = (max_ctx + SL - 1) / SL;
+    size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 2);
+    size_t ws = 0;
+    for (int l = 0; l < c.n_layers; l++) {
+        const vxc_layer_dev *d = &net->layers[l];
+        const vxc_qmat *mats[4] = {d->wqkv, d->wo, d->wgu, d->wd};
+        for (int i = 0; i < 4; i++) {
+            size_t b = vxc_qgemv_workspace_bytes(mats[i], max_rows < 64 ? max_rows : 64);
+            for (int m = 1; m <= (max_rows < 64 ? max_rows : 64); m++) {
+                size_t bm = vxc_qgemv_workspace_bytes(mats[i], m);
+                if (bm > b) b = bm;
+            }
+            if (b > ws) ws = b;
+        }
+    }
+    for (int m = 1; m <= (max_rows < 64 ? max_rows : 64); m++) {
+        size_t bm = vxc_qgemv_workspace_bytes(net->out, m);
+        if (bm > ws) ws = bm;
+    }
+    s->gemv_ws_bytes = ws;
+    cudaError_t e = cudaSuccess;
+#define ALLOC(p, n) if (e == cudaSuccess) e = cudaMalloc((void **)&(p), (n))
+    ALLOC(s->k, kvn * 4);
+    ALLOC(s->v, kvn * 4);
+    ALLOC(s->x, (size_t)max_rows * E * 4);
+    ALLOC(s->h, (size_t)max_rows * E * 4);
+    ALLOC(s->qkv, (size_t)max_rows * (E + 2 * kvd) * 4);
+    ALLOC(s->att, (size_t)max_rows * E * 4);
+    ALLOC(s->gu, (size_t)max_rows * 2 * F * 4);
+    ALLOC(s->hf, (size_t)max_rows * F * 4);
+    ALLOC(s->o, (size_t)max_rows * E * 4);
+    ALLOC(s->attn_part, part * 4);
+    if (ws) ALLOC(s->gemv_ws, ws);
+#undef ALLOC
+    if (e == cudaSuccess) e = cudaMemset(s->k, 0, kvn * 4);
+    if (e == cudaSuccess) e = cudaMemset(s->v, 0, kvn * 4);
+    if (e == cudaSuccess && attn_smem(hd, SL) > 48 * 1024)
+        e = cudaFuncSetAttribute(k_attn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(hd, SL));
+    if (e != cudaSuccess) {
+        vxc_set_error("vxc_seqs_create: %s", cudaGetErrorString(e));
+        vxc_seqs_destroy(s);
+        return -3;
+    }
+    *out = s;
+    return 0;
+}
+
+extern "C" void vxc_seqs_destroy(vxc_seqs *s) {
+    if (!s) return;
+    float *ptrs[] = {s->k, s->v, s->x, s->h, s->qkv, s->att, s->gu, s->hf, s->o, s->attn_part};
+    for (float *p : ptrs)
+        if (p) cudaFree(p);
+    if (s->gemv_ws) cudaFree(s->gemv_ws);
+    free(s);
+}
+
+static inline unsigned nblk(size_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
+                           int rows_per_group, const int *d_logit_rows, int n_logit_rows, float *d_logits,
+                           void *stream) {
+    if (!s || !d_tokens || !d_slot || !d_pos || n_groups <= 0 || rows_per_group <= 0) {
+        vxc_set_error("vxc_forward: bad arguments");
+        return -4;
+    }
+    const int M = n_groups * rows_per_group, T = rows_per_group;
+    if (M > s->max_rows || n_logit_rows > s->max_rows || (n_logit_rows > 0 && (!d_logit_rows || !d_logits))) {
+        vxc_set_error("vxc_forward: %d rows exceed max_rows %d", M, s->max_rows);
+        return -4;
+    }
+    const vxc_net *n = s->net;
+    const vxc_net_config &c = n->cfg;
+    const int E = c.n_embd, H = c.n_heads, KH = c.n_kv_heads, hd = c.n_head_dim, F = c.n_ff;
+    const int kvd = KH * hd;
+    cudaStream_t st = (cudaStream_t)stream;
+    unsigned int *err = vxc_device_error_ptr();
+    int rc;
+    k_embed<<<M, 256, 0, st>>>(n->embd, n->embd_type, n->embd_row_bytes, n->embd_rows, E, d_tokens, s->x, err);
+    const int G = H / KH, nq = T * G, nqc = (nq + ATTN_QC - 1) / ATTN_QC;
+    const size_t asm_bytes = attn_smem(hd, s->attn_sl);
+    for (int l = 0; l < c.n_layers; l++) {
+        const vxc_layer_dev *d = &n->layers[l];
+        float *kc = s->k + (size_t)l * s->n_slots * s->max_ctx * kvd;
+        float *vc = s->v + (size_t)l * s->n_slots * s->max_ctx * kvd;
+        k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->attn_norm, E, NULL, s->h);
+        if ((rc = vxc_qgemv(d->wqkv, s->h, M, s->qkv, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
+        k_rope_kv<<<M, 128, 0, st>>>(s->qkv, T, d_slot, d_pos, n->rope, c.max_pos, H, KH, hd, kc, vc, s->n_slots,
+                                     s->max_ctx, err);
+        k_attn_partial<<<dim3(n_groups * KH * nqc, s->attn_splits), 128, asm_bytes, st>>>(
+            s->qkv, T, d_slot, d_pos, H, KH, hd, kc, vc, s->max_ctx, s->attn_sl, nqc, s->attn_part);
+        k_attn_combine<<<n_groups * KH * nq, 128, 0, st>>>(s->attn_part, T, H, KH, hd, s->attn_splits, s->att);
+        if ((rc = vxc_qgemv(d->wo, s->att, M, s->o, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
+        k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E);
+        k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->ffn_norm, E, NULL, s->h);
+        if ((rc = vxc_qgemv(d->wgu, s->h, M, s->gu, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
+        k_swiglu<<<nblk((size_t)M * F, 256), 256, 0, st>>>(s->gu, M, F, s->hf);
+        if ((rc = vxc_qgemv(d->wd, s->hf, M, s->o, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
+        k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E);
+    }
+    if (n_logit_rows > 0) {
+        const int V = c.n_vocab, R = n->out->rows;
+        if (n->out_norm)
+            k_rmsnorm<<<n_logit_rows, 256, 0, st>>>(s->x, n->out_norm, E, d_logit_rows, s->h);
+        else
+            return vxc_set_error("vxc_forward: models without output_norm are not supported"), -7;
+        if (R < V) k_fill<<<nblk((size_t)n_logit_rows * V, 256), 256, 0, st>>>(d_logits, (size_t)n_logit_rows * V, -1e30f);
+        if (R == V) {
+            if ((rc = vxc_qgemv(n->out, s->h, n_logit_rows, d_logits, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
+        } else {
+            vxc_set_error("vxc_forward: LM head rows %d != vocab %d not supported", R, V);
+            return -7;
+        }
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { vxc_set_error("vxc_forward: %s", cudaGetErrorString(e)); return -3; }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// host-buffer single-sequence path (vx_model_forward)
+// ---------------------------------------------------------------------------
+extern "C" int vxc_forward_host(vxc_seqs *s, int slot, int pos0, const int *h_tokens, int n_tokens,
+                                float *h_logits) {
+    if (!s || !h_tokens || n_tokens <= 0 || slot < 0 || slot >= s->n_slots || pos0 < 0) {
+        vxc_set_error("vxc_forward_host: bad arguments");
+        return -4;
+    }
+    if (pos0 + n_tokens > s->max_ctx) {
+        vxc_set_error("vxc_forward_host: positions %d..%d exceed the context of %d", pos0, pos0 + n_tokens - 1,
+                      s->max_ctx);
+        return -4;
+    }
+    const int V = s->net->cfg.n_vocab;
+    int *d_i = NULL;
+    float *d_l = NULL;
+    const int chunk = s->max_rows;
+    VXC_CUDA_OK(cudaMalloc((void **)&d_i, (size_t)(chunk + 3) * sizeof(int)));
+    if (cudaMalloc((void **)&d_l, (size_t)V * sizeof(float)) != cudaSuccess) {
+        cudaFree(d_i);
+        vxc_set_error("vxc_forward_host: out of device memory");
+        return -3;
+    }
+    int rc = 0;
+    for (int done = 0; done < n_tokens && rc == 0; done += chunk) {
+        int n = n_tokens - done < chunk ? n_tokens - done : chunk;
+        int meta[3] = {slot, pos0 + done, n - 1};
+        if (cudaMemcpy(d_i, h_tokens + done, (size_t)n * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(d_i + chunk, meta, sizeof meta, cudaMemcpyHostToDevice) != cudaSuccess) {
+            rc = -3;
+            break;
+        }
+        const bool last = done + n >= n_tokens;
+        rc = vxc_forward(s, d_i, d_i + chunk, d_i + chunk + 1, 1, n, last ? d_i + chunk + 2 : NULL, last ? 1 : 0,
+                         last ? d_l : NULL, NULL);
+    }
+    if (rc == 0 && h_logits && cudaMemcpy(h_logits, d_l, (size_t)V * sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = -3;
+    if (rc == 0) rc = vxc_check_device_error(NULL);
+    cudaFree(d_i);
+    cudaFree(d_l);
+    return rc;
+}

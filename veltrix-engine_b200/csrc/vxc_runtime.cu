@@ -78,3 +78,9 @@ extern "C" int vxc_check_device_error(unsigned int *code_out) {
     if (code_out) *code_out = h;
     return h ? -3 : 0;
 }
+
+extern "C" int vxc_device_current(void) {
+    int d = -1;
+    if (vxc_device_count() <= 0 || cudaGetDevice(&d) != cudaSuccess) { cudaGetLastError(); return -1; }
+    return d;
+}

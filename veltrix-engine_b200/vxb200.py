@@ -29,7 +29,101 @@ PROTOTYPES = {
     "vxc_qgemv_workspace_bytes": (ctypes.c_size_t, [_vp, ctypes.c_int]),
     "vxc_qgemv": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]),
     "vxc_qgemv_simt": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]),
+    "vxc_device_current": (ctypes.c_int, []),
+    "vxc_net_create": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_vp)]),
+    "vxc_net_destroy": (None, [_vp]),
+    "vxc_net_config_get": (ctypes.c_int, [_vp, _vp]),
+    "vxc_net_weight_bytes": (ctypes.c_size_t, [_vp]),
+    "vxc_seqs_create": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
+    "vxc_seqs_destroy": (None, [_vp]),
+    "vxc_forward": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp]),
+    "vxc_forward_host": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp]),
+    # model.h / veltrix.h
+    "vx_model_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "vx_model_destroy": (None, [_vp]),
+    "vx_model_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    "vx_model_kv_truncate": (None, [_vp, ctypes.c_int]),
+    "vx_set_compute_level": (None, [ctypes.c_int]),
+    "vx_enable_metalearn": (None, [ctypes.c_bool]),
+    "vx_set_n_threads": (None, [ctypes.c_int]),
+    "vx_set_forward_timing_enabled": (None, [ctypes.c_int]),
+    "vx_print_forward_timing": (None, []),
+    # veltrix_synth.h
+    "vx_synth_write_gguf": (ctypes.c_int, [ctypes.c_char_p, _vp, ctypes.c_uint64]),
 }
+
+
+class SynthConfig(ctypes.Structure):
+    _fields_ = [("n_embd", ctypes.c_int), ("n_layers", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("n_kv_heads", ctypes.c_int), ("n_ff", ctypes.c_int), ("n_vocab", ctypes.c_int),
+                ("rope_theta", ctypes.c_float), ("wtype", ctypes.c_int)]
+
+
+class ModelConfig(ctypes.Structure):
+    """vx_model_config (include/veltrix.h)."""
+    _fields_ = [("n_layers", ctypes.c_int), ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int),
+                ("n_embd", ctypes.c_int), ("n_head_dim", ctypes.c_int), ("n_ff", ctypes.c_int),
+                ("n_vocab", ctypes.c_int), ("n_ctx", ctypes.c_int), ("rope_theta", ctypes.c_float),
+                ("rope_freq_base", ctypes.c_float), ("n_threads", ctypes.c_int), ("arch", ctypes.c_int),
+                ("mlp_type", ctypes.c_int), ("norm_type", ctypes.c_int), ("rope_partial_dims", ctypes.c_int),
+                ("has_q_bias", ctypes.c_bool), ("has_k_bias", ctypes.c_bool), ("has_v_bias", ctypes.c_bool),
+                ("has_post_attn_norm", ctypes.c_bool), ("has_post_ffn_norm", ctypes.c_bool),
+                ("has_ffn_bias", ctypes.c_bool)]
+
+
+class ModelHead(ctypes.Structure):
+    """Leading fields of struct vx_model up to cache_len (include/veltrix.h)."""
+    _fields_ = [("config", ModelConfig), ("tensors", ctypes.c_void_p), ("n_tensors", ctypes.c_int)] + \
+               [("p%d" % i, ctypes.c_void_p) for i in range(27)] + [("cache_len", ctypes.c_int)]
+
+
+def write_synth(path, n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab, wtype, seed, rope_theta=10000.0):
+    c = SynthConfig(n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab, rope_theta, wtype)
+    check(lib().vx_synth_write_gguf(path.encode(), ctypes.byref(c), seed), "vx_synth_write_gguf")
+
+
+class Model:
+    """vx_model handle of the B200 back end (include/model.h)."""
+
+    def __init__(self, path):
+        h = _vp()
+        rc = lib().vx_model_create(path.encode(), ctypes.byref(h))
+        if rc != 0:
+            raise VxError(f"vx_model_create({path}) = {rc}: {lib().vxc_error_string()}")
+        self.h = h
+        self.head = ctypes.cast(h, ctypes.POINTER(ModelHead)).contents
+
+    @property
+    def n_vocab(self):
+        return self.head.config.n_vocab
+
+    @property
+    def cache_len(self):
+        return self.head.cache_len
+
+    @cache_len.setter
+    def cache_len(self, v):
+        self.head.cache_len = v
+
+    def forward(self, tokens):
+        import numpy as np
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(self.n_vocab, np.float32)
+        rc = lib().vx_model_forward(self.h, toks.ctypes.data, toks.size, out.ctypes.data)
+        if rc != 0:
+            raise VxError(f"vx_model_forward = {rc}: {lib().vxc_error_string()}")
+        return out
+
+    def close(self):
+        if self.h:
+            lib().vx_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 _lib = None
 
