@@ -129,6 +129,65 @@ int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *
  * the tokens in chunks of max_rows and synchronises. */
 int vxc_forward_host(vxc_seqs *s, int slot, int pos0, const int *h_tokens, int n_tokens, float *h_logits);
 
+/* ---- sampling ----------------------------------------------------------------
+ * Canonical sampler shared with the CPU oracle (bit-exact given the same fp32
+ * logits): T <= 0 is greedy (first maximum, reference src/speculative.c:93-98);
+ * otherwise W_v = trunc(exp((l_v - max)/T) * 2^32) with a fixed exp, and a
+ * token is drawn as the first v whose prefix sum of W exceeds
+ * floor(sum(W) * u24 / 2^24), u24 = Philox4x32-10(seed; pos, seq, purpose) >> 8.
+ */
+
+/* One token per row of logits[n_rows][V] (device) into tokens[n_rows]
+ * (device), row r using Philox counter (pos[r], seq[r], purpose).
+ * Replaces sample_top_p / sample_greedy (src/speculative.c:35-98) with
+ * top_p = 1. */
+int vxc_sample_rows(const float *logits, int n_rows, int V, float temp, uint64_t seed, const int *d_pos,
+                    const int *d_seq, unsigned int purpose, int *d_tokens, void *stream);
+
+/* Scratch bytes vxc_accept needs for n_seq sequences of k draft tokens. */
+size_t vxc_accept_workspace_bytes(int n_seq, int k);
+
+/* Fused acceptance for n_seq sequences (reference verify_draft,
+ * src/speculative.c:178-236, restated as standard speculative sampling):
+ * P = target logits (row i of sequence s at P + s*p_seq + i*p_pos, i <= k),
+ * Q = draft logits (row i at Q + s*q_seq + i*q_pos, i < k), draft tokens
+ * d[s*k + i].  Draft token i of sequence s sits at absolute position
+ * pos0[s] + i and uses Philox counters (pos0[s]+i, seq_id[s], ACCEPT /
+ * RESAMPLE).  Outputs n_acc[s] in 0..k and next[s] (the correction token,
+ * or the bonus token drawn from row k when all k are accepted).  One kernel
+ * launch; all pointers are device memory. */
+int vxc_accept(const float *P, long long p_seq, long long p_pos, const float *Q, long long q_seq,
+               long long q_pos, const int *d, int n_seq, int k, int V, float temp, uint64_t seed,
+               const int *seq_id, const int *pos0, int *n_acc, int *next, void *workspace,
+               size_t workspace_bytes, void *stream);
+
+/* ---- device speculative-decoding engine --------------------------------------- */
+
+typedef struct vxc_spec vxc_spec;
+
+typedef struct {
+    long long rounds;      /* draft+verify rounds run */
+    long long drafted;     /* draft tokens proposed (sum over sequences) */
+    long long accepted;    /* draft tokens accepted */
+    long long emitted;     /* tokens written to the outputs */
+    double prefill_ms;     /* device time of the prompt pass */
+    double decode_ms;      /* device time of the round loop */
+} vxc_spec_stats;
+
+/* Engine for up to n_seq concurrent sequences of max_ctx positions, k draft
+ * tokens per round; keeps KV caches for both models. */
+int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int n_seq, int k, int max_ctx, vxc_spec **out);
+void vxc_spec_destroy(vxc_spec *e);
+
+/* Generate up to max_new tokens for each of n_seq sequences (host buffers:
+ * prompts concatenated, prompt_len[n_seq], seq_id[n_seq] = Philox sequence
+ * ids; out[n_seq][max_new], counts[n_seq]).  Replaces
+ * vx_speculative_generate (src/speculative.c:238-294) for a batch; the
+ * whole round loop (k draft steps, one (k+1)-row verify, fused acceptance,
+ * commit) runs on the device as one CUDA graph per round. */
+int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *prompt_len, const int *seq_id, int n_seq,
+                      int max_new, float temp, uint64_t seed, int *out, int *counts, vxc_spec_stats *stats);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,106 @@
+"""Configuration 1 end to end on the device: speculative decoding through the
+public API (vx_speculative_*), tiny Q8_0 target and draft, 32-token prompt,
+k = 4, 128 new tokens.
+
+- Greedy: the output must equal the reference's target-only greedy stream
+  (tests/golden, produced by the reference build) wherever the reference's
+  top-2 margin exceeds 1e-3.
+- Sampled (T = 0.8): the oracle's O-spec run on the same checkpoints with the
+  same seed; sampling is bit-exact given identical logits and the logits agree
+  to ~1e-6, so the streams are expected to be identical.
+- Batch: each sequence of a batch equals its single-sequence run.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from _paths import oracle
+import fixtures
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+f32p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+
+
+@pytest.fixture(scope="module")
+def models(cuda):
+    import vxb200
+    t = vxb200.Model(fixtures.path("tiny_target"))
+    d = vxb200.Model(fixtures.path("tiny_draft"))
+    yield t, d
+    t.close()
+    d.close()
+
+
+def test_greedy_equals_reference_greedy(models):
+    import vxb200
+    t, d = models
+    g = np.load(os.path.join(GOLD, "tiny_target.npz"))
+    sp = vxb200.Speculative(d, t, 4, temp=0.0)
+    out = sp.generate(g["prompt"], 64)
+    assert len(out) == 64
+    ref = g["greedy"]
+    for i in range(64):
+        if out[i] != ref[i]:
+            assert g["margins"][i] <= 1e-3, (i, out[i], ref[i])
+            break
+    st = sp.stats()
+    assert st.emitted == 64 and st.rounds >= 1 and st.accepted <= st.drafted
+    sp.close()
+
+
+def test_sampled_matches_oracle_spec(models):
+    import vxb200
+    t, d = models
+    O = oracle()
+    ot = O.vxo_model_load(fixtures.path("tiny_target").encode(), 0)
+    od = O.vxo_model_load(fixtures.path("tiny_draft").encode(), 0)
+    rng = np.random.default_rng(12345)
+    prompt = rng.integers(0, 4096, 32).astype(np.int32)
+    n = 128
+    want = np.zeros(n, np.int32)
+    rounds = ctypes.c_int()
+    O.vxo_spec_generate(ot, od, f32p(prompt), len(prompt), 4, 0.8, 1234, 0, f32p(want), n, ctypes.byref(rounds))
+    sp = vxb200.Speculative(d, t, 4, temp=0.8, seed=1234)
+    got = sp.generate(prompt, n)
+    assert len(got) == n
+    agree = int(np.argmax(got != want)) if np.any(got != want) else n
+    assert agree == n, f"streams diverge at token {agree}"
+    O.vxo_model_free(ot)
+    O.vxo_model_free(od)
+    sp.close()
+
+
+def test_batch_equals_single(models):
+    import vxb200
+    t, d = models
+    rng = np.random.default_rng(7)
+    prompts = [rng.integers(0, 4096, n).astype(np.int32) for n in (32, 17, 2)]
+    sp = vxb200.Speculative(d, t, 4, temp=0.8, seed=99)
+    batch = sp.generate_batch(prompts, 40)
+    for i, p in enumerate(prompts):
+        single = vxb200.Speculative(d, t, 4, temp=0.8, seed=99, seq_id_base=i)
+        one = single.generate(p, 40)
+        assert np.array_equal(one, batch[i]), i
+        single.close()
+    sp.close()
+
+
+def test_stream_single_token_prompt(models):
+    """vx_speculative_generate_stream: a one-token prompt (src/speculative.c:296-300)."""
+    import vxb200
+    t, d = models
+    sp = vxb200.Speculative(d, t, 3, temp=0.0)
+    out = np.zeros(20, np.int32)
+    n = vxb200.lib().vx_speculative_generate_stream(sp.h, 7, out.ctypes.data, 20)
+    assert n == 20
+    # greedy speculative == greedy target decoding from the same prompt
+    t.cache_len = 0
+    lg = t.forward(np.array([7]))
+    for i in range(20):
+        tok = int(np.argmax(lg))
+        assert tok == out[i], i
+        lg = t.forward(np.array([tok]))
+    sp.close()

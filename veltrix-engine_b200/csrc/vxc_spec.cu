@@ -1,0 +1,688 @@
+// vxc_spec.cu — sampling, fused acceptance and the device-resident
+// speculative-decoding round loop.
+//
+// Semantics (the corrected form of reference src/speculative.c:148-294; the
+// CPU oracle oracle/vxo_spec.c restates the same procedure):
+//   round, for every active sequence with committed tokens c[0..L):
+//     draft step 0   rows (c[L-2], c[L-1]) at positions L-2, L-1 -> q_0
+//     draft step i   row d_i at position L+i-1 -> q_i            (i = 1..k-1)
+//     d_{i+1}        sampled from q_i with Philox (pos L+i, DRAFT)
+//     verify         rows (c[L-1], d_1..d_k) at positions L-1..L+k-1 -> p_0..p_k
+//     accept         first rejection i: sample max(0, p_i - q_i); all accepted:
+//                    bonus from p_k                (fused kernel k_accept)
+//     commit         c += d_1..d_a, next ; L += a + 1
+// KV invariants: target holds 0..L-2 at round start (the verify rewrites
+// L-1..); draft holds 0..L-3 (step 0 rewrites L-2, L-1).  Positions past a
+// rejection hold stale K/V that the next round overwrites before reading.
+// All sampling decisions use exact integer weights (vxc_weight), so they match
+// the oracle bit-for-bit given the same logits.
+#include "vxc_common.cuh"
+#include "vxc_internal.h"
+
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <vector>
+
+typedef unsigned long long u64;
+typedef unsigned __int128 u128;
+
+#define SMP_THREADS 512
+
+// ---------------------------------------------------------------------------
+// block-wide helpers (blockDim.x == SMP_THREADS)
+// ---------------------------------------------------------------------------
+struct MaxIdx {
+    float v;
+    int i;
+};
+
+__device__ __forceinline__ MaxIdx better(MaxIdx a, MaxIdx b) {
+    // larger value wins; on ties the lower index (first maximum)
+    if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+    return a;
+}
+
+__device__ MaxIdx block_argmax(const float *__restrict__ row, int V, MaxIdx *red) {
+    MaxIdx m = {-INFINITY, 0x7fffffff};
+    for (int v = threadIdx.x; v < V; v += blockDim.x) m = better(m, MaxIdx{row[v], v});
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        MaxIdx t;
+        t.v = __shfl_xor_sync(0xffffffffu, m.v, o);
+        t.i = __shfl_xor_sync(0xffffffffu, m.i, o);
+        m = better(m, t);
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = m;
+    __syncthreads();
+    MaxIdx r = red[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) r = better(r, red[i]);
+    __syncthreads();
+    return r;
+}
+
+__device__ u64 block_sum_u64(u64 v, u64 *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    u64 r = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) r += red[i];
+    __syncthreads();
+    return r;
+}
+
+// Exclusive prefix of per-thread values in thread order.
+__device__ u64 block_excl_scan_u64(u64 v, u64 *red) {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    u64 inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        u64 t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (l >= o) inc += t;
+    }
+    __syncthreads();
+    if (l == 31) red[w] = inc;
+    __syncthreads();
+    u64 base = 0;
+    for (int i = 0; i < w; i++) base += red[i];
+    __syncthreads();
+    return base + inc - v;
+}
+
+// Chunked search: thread t owns elements [t*C, (t+1)*C).  Returns the first
+// v with inclusive prefix sum of wt(v) > thr (or V-1 if none).
+template <class WF>
+__device__ int block_draw(int V, u64 thr, WF wt, u64 *red, int *res) {
+    const int C = (V + blockDim.x - 1) / blockDim.x;
+    const int a = threadIdx.x * C, b = min(V, a + C);
+    u64 s = 0;
+    for (int v = a; v < b; v++) s += wt(v);
+    u64 ex = block_excl_scan_u64(s, red);
+    if (threadIdx.x == 0) *res = V - 1;
+    __syncthreads();
+    if (a < b && ex <= thr && thr < ex + s) {
+        u64 acc = ex;
+        for (int v = a; v < b; v++) {
+            acc += wt(v);
+            if (acc > thr) { *res = v; break; }
+        }
+    }
+    __syncthreads();
+    int r = *res;
+    __syncthreads();
+    return r;
+}
+
+__device__ __forceinline__ u64 draw_threshold(u64 S, uint32_t word) {
+    return (u64)(((u128)S * (word >> 8)) >> 24);
+}
+
+// ---------------------------------------------------------------------------
+// per-row sampler
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(SMP_THREADS) k_sample_rows(const float *__restrict__ logits, int V, float temp,
+                                                             u64 seed, const int *__restrict__ pos,
+                                                             const int *__restrict__ seq, unsigned purpose,
+                                                             int *__restrict__ out) {
+    __shared__ MaxIdx red_m[32];
+    __shared__ u64 red_u[32];
+    __shared__ int res;
+    const int r = blockIdx.x;
+    const float *row = logits + (size_t)r * V;
+    MaxIdx mx = block_argmax(row, V, red_m);
+    if (!(temp > 0.0f)) {
+        if (threadIdx.x == 0) out[r] = mx.i;
+        return;
+    }
+    const float invT = 1.0f / temp;
+    auto wt = [&](int v) -> u64 { return vxc_weight(row[v], mx.v, invT); };
+    u64 s = 0;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) s += wt(v);
+    u64 S = block_sum_u64(s, red_u);
+    uint32_t word = vxc_philox_u32(seed, (uint32_t)pos[r], (uint32_t)seq[r], purpose);
+    int t = block_draw(V, draw_threshold(S, word), wt, red_u, &res);
+    if (threadIdx.x == 0) out[r] = t;
+}
+
+extern "C" int vxc_sample_rows(const float *logits, int n_rows, int V, float temp, uint64_t seed, const int *d_pos,
+                               const int *d_seq, unsigned int purpose, int *d_tokens, void *stream) {
+    if (!logits || n_rows <= 0 || V <= 0 || !d_pos || !d_seq || !d_tokens) {
+        vxc_set_error("vxc_sample_rows: bad arguments");
+        return -4;
+    }
+    k_sample_rows<<<n_rows, SMP_THREADS, 0, (cudaStream_t)stream>>>(logits, V, temp, seed, d_pos, d_seq, purpose,
+                                                                    d_tokens);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { vxc_set_error("vxc_sample_rows: %s", cudaGetErrorString(e)); return -3; }
+    return 0;
+}
+
+// ---------------------------------------------------------------------------
+// fused acceptance
+// ---------------------------------------------------------------------------
+struct AccStat {
+    float maxp, maxq;
+    int argp, pad;
+    u64 Sp, Sq, Wpd, Wqd;
+};
+
+__global__ void __launch_bounds__(SMP_THREADS) k_accept(const float *__restrict__ P, long long p_seq, long long p_pos,
+                                                        const float *__restrict__ Q, long long q_seq, long long q_pos,
+                                                        const int *__restrict__ d, int k, int V, float temp, u64 seed,
+                                                        const int *__restrict__ seq_id, const int *__restrict__ pos0,
+                                                        int *__restrict__ n_acc, int *__restrict__ next,
+                                                        AccStat *st, unsigned int *__restrict__ cnt) {
+    __shared__ MaxIdx red_m[32];
+    __shared__ u64 red_u[32];
+    __shared__ int res;
+    __shared__ int is_last;
+    const int s = blockIdx.x, i = blockIdx.y;
+    const bool greedy = !(temp > 0.0f);
+    const float invT = greedy ? 0.0f : 1.0f / temp;
+    // ---- phase 1: statistics of row i ----
+    {
+        const float *pr = P + s * p_seq + i * p_pos;
+        MaxIdx mp = block_argmax(pr, V, red_m);
+        AccStat a;
+        a.maxp = mp.v;
+        a.argp = mp.i;
+        a.maxq = 0.0f;
+        a.Sp = a.Sq = a.Wpd = a.Wqd = 0;
+        if (!greedy) {
+            u64 sp = 0;
+            for (int v = threadIdx.x; v < V; v += blockDim.x) sp += vxc_weight(pr[v], mp.v, invT);
+            a.Sp = block_sum_u64(sp, red_u);
+            if (i < k) {
+                const float *qr = Q + s * q_seq + i * q_pos;
+                MaxIdx mq = block_argmax(qr, V, red_m);
+                a.maxq = mq.v;
+                u64 sq = 0;
+                for (int v = threadIdx.x; v < V; v += blockDim.x) sq += vxc_weight(qr[v], mq.v, invT);
+                a.Sq = block_sum_u64(sq, red_u);
+                int t = d[s * k + i];
+                if (t >= 0 && t < V) {
+                    a.Wpd = vxc_weight(pr[t], mp.v, invT);
+                    a.Wqd = vxc_weight(qr[t], mq.v, invT);
+                }
+            }
+        }
+        if (threadIdx.x == 0) {
+            st[s * (k + 1) + i] = a;
+            __threadfence();
+            unsigned prev = atomicAdd(&cnt[s], 1u);
+            is_last = (prev == (unsigned)k);
+        }
+        __syncthreads();
+        if (!is_last) return;
+    }
+    // ---- phase 2 (last CTA of sequence s): decision and resample ----
+    __threadfence();
+    if (threadIdx.x == 0) cnt[s] = 0;   // re-arm for the next launch
+    // other CTAs wrote these; read them through L2, not a stale L1 line
+    const AccStat *S_ = st + s * (k + 1);
+    __syncthreads();
+    const int p0 = pos0[s], sid = seq_id[s];
+    int acc = k, nxt = -1, rej = -1;
+    for (int j = 0; j < k; j++) {
+        AccStat a = S_[j];
+        int t = d[s * k + j];
+        bool ok;
+        if (greedy) {
+            ok = (t == a.argp);
+        } else {
+            u64 u = vxc_philox_u32(seed, (uint32_t)(p0 + j), (uint32_t)sid, VXC_PURPOSE_ACCEPT) >> 8;
+            ok = (t >= 0 && t < V) && ((u128)u * a.Wqd * a.Sp < (((u128)a.Wpd * a.Sq) << 24));
+        }
+        if (!ok) { acc = j; rej = j; break; }
+    }
+    if (greedy) {
+        nxt = S_[acc].argp;
+    } else if (rej >= 0) {
+        const AccStat a = S_[rej];
+        const float *pr = P + s * p_seq + rej * p_pos;
+        const float *qr = Q + s * q_seq + rej * q_pos;
+        auto rw = [&](int v) -> u64 {
+            u128 x = (u128)vxc_weight(pr[v], a.maxp, invT) * a.Sq;
+            u128 y = (u128)vxc_weight(qr[v], a.maxq, invT) * a.Sp;
+            return x > y ? (u64)((x - y) >> 36) : 0ull;
+        };
+        u64 sr = 0;
+        for (int v = threadIdx.x; v < V; v += blockDim.x) sr += rw(v);
+        u64 SR = block_sum_u64(sr, red_u);
+        if (SR == 0) {
+            nxt = a.argp;
+        } else {
+            uint32_t w = vxc_philox_u32(seed, (uint32_t)(p0 + rej), (uint32_t)sid, VXC_PURPOSE_RESAMPLE);
+            nxt = block_draw(V, draw_threshold(SR, w), rw, red_u, &res);
+        }
+    } else {
+        const AccStat a = S_[k];
+        const float *pr = P + s * p_seq + k * p_pos;
+        auto pw = [&](int v) -> u64 { return vxc_weight(pr[v], a.maxp, invT); };
+        uint32_t w = vxc_philox_u32(seed, (uint32_t)(p0 + k), (uint32_t)sid, VXC_PURPOSE_RESAMPLE);
+        nxt = block_draw(V, draw_threshold(a.Sp, w), pw, red_u, &res);
+    }
+    if (threadIdx.x == 0) {
+        n_acc[s] = acc;
+        next[s] = nxt;
+    }
+}
+
+static size_t accept_ws(int n_seq, int k) {
+    size_t a = (size_t)n_seq * (k + 1) * sizeof(AccStat);
+    a = (a + 255) & ~(size_t)255;
+    return a + (size_t)n_seq * sizeof(unsigned int);
+}
+
+extern "C" size_t vxc_accept_workspace_bytes(int n_seq, int k) { return accept_ws(n_seq, k); }
+
+// The counters at the end of the workspace must be zero on the first launch;
+// the kernel re-arms them itself.
+static int launch_accept(const float *P, long long p_seq, long long p_pos, const float *Q, long long q_seq,
+                         long long q_pos, const int *d, int n_seq, int k, int V, float temp, uint64_t seed,
+                         const int *seq_id, const int *pos0, int *n_acc, int *next, void *ws, cudaStream_t st) {
+    size_t a = ((size_t)n_seq * (k + 1) * sizeof(AccStat) + 255) & ~(size_t)255;
+    k_accept<<<dim3(n_seq, k + 1), SMP_THREADS, 0, st>>>(P, p_seq, p_pos, Q, q_seq, q_pos, d, k, V, temp, seed,
+                                                         seq_id, pos0, n_acc, next, (AccStat *)ws,
+                                                         (unsigned int *)((char *)ws + a));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { vxc_set_error("vxc_accept: %s", cudaGetErrorString(e)); return -3; }
+    return 0;
+}
+
+extern "C" int vxc_accept(const float *P, long long p_seq, long long p_pos, const float *Q, long long q_seq,
+                          long long q_pos, const int *d, int n_seq, int k, int V, float temp, uint64_t seed,
+                          const int *seq_id, const int *pos0, int *n_acc, int *next, void *workspace,
+                          size_t workspace_bytes, void *stream) {
+    if (!P || !Q || !d || n_seq <= 0 || k <= 0 || V <= 0 || !seq_id || !pos0 || !n_acc || !next) {
+        vxc_set_error("vxc_accept: bad arguments");
+        return -4;
+    }
+    if (!workspace || workspace_bytes < accept_ws(n_seq, k)) {
+        vxc_set_error("vxc_accept: workspace of %zu bytes needed", accept_ws(n_seq, k));
+        return -4;
+    }
+    return launch_accept(P, p_seq, p_pos, Q, q_seq, q_pos, d, n_seq, k, V, temp, seed, seq_id, pos0, n_acc, next,
+                         workspace, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// round-loop kernels
+// ---------------------------------------------------------------------------
+struct SpecDev {
+    int S, k, cap, max_new, max_ctx;
+    int *c;          // [S][cap] committed tokens (prompt + generated)
+    int *L;          // [S]
+    int *gen;        // [S]
+    int *done;       // [S]
+    int *seq_id;     // [S]
+    int *slot;       // [S] = 0..S-1
+    int *out;        // [S][max_new]
+    int *tok0, *pos0, *lrow0;   // draft step 0: [2S], [S], [S]
+    int *dpos;       // [k][S] positions of draft step i rows (i>=1) / sampling positions
+    int *dtok;       // [k][S] sampled draft tokens
+    int *vtok, *vpos, *vrows;   // verify: [S(k+1)], [S], [S(k+1)]
+    int *dseq;       // [S][k] draft tokens seq-major
+    int *apos;       // [S] = L (position of d_1)
+    int *n_acc, *next;
+    long long *ctr;  // [3] drafted, accepted, emitted
+    int *n_done;     // [1]
+};
+
+__global__ void k_round_prep(SpecDev D) {
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= D.S) return;
+    const int L = D.L[s];
+    const int *c = D.c + (size_t)s * D.cap;
+    if (L >= 2) {
+        D.tok0[2 * s] = c[L - 2];
+        D.tok0[2 * s + 1] = c[L - 1];
+        D.pos0[s] = L - 2;
+        D.lrow0[s] = 2 * s + 1;
+    } else {
+        D.tok0[2 * s] = c[0];
+        D.tok0[2 * s + 1] = c[0];
+        D.pos0[s] = 0;
+        D.lrow0[s] = 2 * s;
+    }
+    for (int i = 0; i < D.k; i++) D.dpos[i * D.S + s] = L + i;   // sampling position of d_{i+1}
+    D.vpos[s] = L - 1;
+    D.apos[s] = L;
+    D.vtok[s * (D.k + 1)] = c[L - 1];
+    for (int j = 0; j <= D.k; j++) D.vrows[s * (D.k + 1) + j] = s * (D.k + 1) + j;
+}
+
+// draft step i >= 1 processes d_i at position L+i-1 = dpos[(i-1)][s]
+__global__ void k_gather_verify(SpecDev D) {
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= D.S) return;
+    for (int i = 0; i < D.k; i++) {
+        int t = D.dtok[i * D.S + s];
+        D.vtok[s * (D.k + 1) + 1 + i] = t;
+        D.dseq[s * D.k + i] = t;
+    }
+}
+
+__global__ void k_commit(SpecDev D) {
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= D.S) return;
+    if (D.done[s]) return;
+    const int a = D.n_acc[s], nx = D.next[s];
+    const int L = D.L[s];
+    int *c = D.c + (size_t)s * D.cap;
+    int g = D.gen[s];
+    int emitted = 0;
+    for (int i = 0; i <= a; i++) {
+        int t = i < a ? D.dseq[s * D.k + i] : nx;
+        c[L + i] = t;
+        if (g < D.max_new) {
+            D.out[(size_t)s * D.max_new + g] = t;
+            g++;
+            emitted++;
+        }
+    }
+    D.L[s] = L + a + 1;
+    D.gen[s] = g;
+    atomicAdd((unsigned long long *)&D.ctr[0], (unsigned long long)D.k);
+    atomicAdd((unsigned long long *)&D.ctr[1], (unsigned long long)a);
+    atomicAdd((unsigned long long *)&D.ctr[2], (unsigned long long)emitted);
+    if (g >= D.max_new || L + a + 1 + D.k + 1 > D.max_ctx) {
+        D.done[s] = 1;
+        atomicAdd(D.n_done, 1);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// engine
+// ---------------------------------------------------------------------------
+struct vxc_spec {
+    const vxc_net *tnet, *dnet;
+    vxc_seqs *ts, *ds;
+    int S, k, max_ctx, V, cap_alloc;
+    SpecDev D;
+    float *dlog;       // [k][S][V]
+    float *vlog;       // [S][k+1][V]
+    void *acc_ws;
+    int *prefill_buf;  // staging for prefill tokens/meta
+    int prefill_rows;
+    cudaStream_t st;
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    int *h_ndone;      // pinned
+};
+
+extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int n_seq, int k, int max_ctx,
+                               vxc_spec **out) {
+    int rc = vxc_require_device();
+    if (rc) return rc;
+    vxc_net_config tc, dc;
+    if (!target || !draft || !out || n_seq <= 0 || k <= 0 || max_ctx <= 2 || vxc_net_config_get(target, &tc) ||
+        vxc_net_config_get(draft, &dc)) {
+        vxc_set_error("vxc_spec_create: bad arguments");
+        return -4;
+    }
+    if (tc.n_vocab != dc.n_vocab) {
+        vxc_set_error("vxc_spec_create: draft vocab %d != target vocab %d", dc.n_vocab, tc.n_vocab);
+        return -4;
+    }
+    vxc_spec *e = (vxc_spec *)calloc(1, sizeof(vxc_spec));
+    e->tnet = target;
+    e->dnet = draft;
+    e->S = n_seq;
+    e->k = k;
+    e->max_ctx = max_ctx;
+    e->V = tc.n_vocab;
+    int trows = n_seq * (k + 1) > 64 ? n_seq * (k + 1) : 64;
+    int drows = 2 * n_seq > 64 ? 2 * n_seq : 64;
+    e->prefill_rows = 64;
+    if ((rc = vxc_seqs_create(target, n_seq, max_ctx, trows, &e->ts)) ||
+        (rc = vxc_seqs_create(draft, n_seq, max_ctx, drows, &e->ds))) {
+        vxc_spec_destroy(e);
+        return rc;
+    }
+    const int S = n_seq;
+    SpecDev &D = e->D;
+    D.S = S;
+    D.k = k;
+    D.cap = max_ctx + k + 2;
+    D.max_ctx = max_ctx;
+    cudaError_t err = cudaSuccess;
+#define DALLOC(p, n) if (err == cudaSuccess) err = cudaMalloc((void **)&(p), (n))
+    DALLOC(D.c, (size_t)S * D.cap * sizeof(int));
+    DALLOC(D.L, S * sizeof(int));
+    DALLOC(D.gen, S * sizeof(int));
+    DALLOC(D.done, S * sizeof(int));
+    DALLOC(D.seq_id, S * sizeof(int));
+    DALLOC(D.slot, S * sizeof(int));
+    DALLOC(D.tok0, 2 * S * sizeof(int));
+    DALLOC(D.pos0, S * sizeof(int));
+    DALLOC(D.lrow0, S * sizeof(int));
+    DALLOC(D.dpos, (size_t)k * S * sizeof(int));
+    DALLOC(D.dtok, (size_t)k * S * sizeof(int));
+    DALLOC(D.vtok, (size_t)S * (k + 1) * sizeof(int));
+    DALLOC(D.vpos, S * sizeof(int));
+    DALLOC(D.vrows, (size_t)S * (k + 1) * sizeof(int));
+    DALLOC(D.dseq, (size_t)S * k * sizeof(int));
+    DALLOC(D.apos, S * sizeof(int));
+    DALLOC(D.n_acc, S * sizeof(int));
+    DALLOC(D.next, S * sizeof(int));
+    DALLOC(D.ctr, 3 * sizeof(long long));
+    DALLOC(D.n_done, sizeof(int));
+    DALLOC(e->dlog, (size_t)k * S * e->V * sizeof(float));
+    DALLOC(e->vlog, (size_t)S * (k + 1) * e->V * sizeof(float));
+    DALLOC(e->acc_ws, accept_ws(S, k));
+    DALLOC(e->prefill_buf, (size_t)(64 + 3 * S + 8) * sizeof(int));
+#undef DALLOC
+    if (err == cudaSuccess) err = cudaMemset(e->acc_ws, 0, accept_ws(S, k));
+    if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaMallocHost((void **)&e->h_ndone, 4 * sizeof(int));
+    if (err == cudaSuccess) {
+        std::vector<int> sl(S);
+        for (int i = 0; i < S; i++) sl[i] = i;
+        err = cudaMemcpy(D.slot, sl.data(), S * sizeof(int), cudaMemcpyHostToDevice);
+    }
+    if (err != cudaSuccess) {
+        vxc_set_error("vxc_spec_create: %s", cudaGetErrorString(err));
+        vxc_spec_destroy(e);
+        return -3;
+    }
+    *out = e;
+    return 0;
+}
+
+extern "C" void vxc_spec_destroy(vxc_spec *e) {
+    if (!e) return;
+    if (e->exec) cudaGraphExecDestroy(e->exec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    vxc_seqs_destroy(e->ts);
+    vxc_seqs_destroy(e->ds);
+    SpecDev &D = e->D;
+    void *ptrs[] = {D.c, D.L, D.gen, D.done, D.seq_id, D.slot, D.out, D.tok0, D.pos0, D.lrow0, D.dpos, D.dtok,
+                    D.vtok, D.vpos, D.vrows, D.dseq, D.apos, D.n_acc, D.next, D.ctr, D.n_done, e->dlog, e->vlog,
+                    e->acc_ws, e->prefill_buf};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    if (e->h_ndone) cudaFreeHost(e->h_ndone);
+    if (e->st) cudaStreamDestroy(e->st);
+    free(e);
+}
+
+// Enqueue one round on e->st (capturable).
+static int enqueue_round(vxc_spec *e, float temp, uint64_t seed) {
+    SpecDev &D = e->D;
+    const int S = D.S, k = D.k, V = e->V;
+    cudaStream_t st = e->st;
+    const int tb = 128, gb = (S + tb - 1) / tb;
+    int rc;
+    k_round_prep<<<gb, tb, 0, st>>>(D);
+    // draft step 0: 2 rows per sequence
+    if ((rc = vxc_forward(e->ds, D.tok0, D.slot, D.pos0, S, 2, D.lrow0, S, e->dlog, st))) return rc;
+    k_sample_rows<<<S, SMP_THREADS, 0, st>>>(e->dlog, V, temp, seed, D.dpos, D.seq_id, VXC_PURPOSE_DRAFT, D.dtok);
+    for (int i = 1; i < k; i++) {
+        float *q = e->dlog + (size_t)i * S * V;
+        // rows: d_i at position L+i-1 == dpos[i-1]; logits of all S rows
+        if ((rc = vxc_forward(e->ds, D.dtok + (size_t)(i - 1) * S, D.slot, D.dpos + (size_t)(i - 1) * S, S, 1,
+                              D.slot, S, q, st)))
+            return rc;
+        k_sample_rows<<<S, SMP_THREADS, 0, st>>>(q, V, temp, seed, D.dpos + (size_t)i * S, D.seq_id,
+                                                 VXC_PURPOSE_DRAFT, D.dtok + (size_t)i * S);
+    }
+    k_gather_verify<<<gb, tb, 0, st>>>(D);
+    if ((rc = vxc_forward(e->ts, D.vtok, D.slot, D.vpos, S, k + 1, D.vrows, S * (k + 1), e->vlog, st))) return rc;
+    if ((rc = launch_accept(e->vlog, (long long)(k + 1) * V, V, e->dlog, V, (long long)S * V, D.dseq, S, k, V, temp,
+                            seed, D.seq_id, D.apos, D.n_acc, D.next, e->acc_ws, st)))
+        return rc;
+    k_commit<<<gb, tb, 0, st>>>(D);
+    cudaError_t er = cudaGetLastError();
+    if (er != cudaSuccess) { vxc_set_error("round: %s", cudaGetErrorString(er)); return -3; }
+    return 0;
+}
+
+extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *prompt_len, const int *seq_id,
+                                 int n_seq, int max_new, float temp, uint64_t seed, int *out, int *counts,
+                                 vxc_spec_stats *stats) {
+    if (!e || !prompts || !prompt_len || n_seq != e->S || max_new <= 0 || !out) {
+        vxc_set_error("vxc_spec_generate: bad arguments (engine holds %d sequences)", e ? e->S : 0);
+        return -4;
+    }
+    SpecDev &D = e->D;
+    const int S = e->S, k = e->k;
+    int maxp = 0;
+    for (int s = 0; s < S; s++) {
+        if (prompt_len[s] < 1) { vxc_set_error("vxc_spec_generate: empty prompt"); return -4; }
+        if (prompt_len[s] > maxp) maxp = prompt_len[s];
+    }
+    if (maxp + k + 2 > e->max_ctx) { vxc_set_error("vxc_spec_generate: prompt longer than the context"); return -4; }
+    cudaStream_t st = e->st;
+    cudaError_t err = cudaSuccess;
+    // output buffer sized for this call
+    if (D.out == NULL || D.max_new < max_new) {
+        if (D.out) cudaFree(D.out);
+        D.out = NULL;
+        err = cudaMalloc((void **)&D.out, (size_t)S * max_new * sizeof(int));
+        if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: %s", cudaGetErrorString(err)); return -3; }
+        if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = NULL; }
+        if (e->graph) { cudaGraphDestroy(e->graph); e->graph = NULL; }
+    }
+    D.max_new = max_new;
+    // committed tokens, lengths, ids
+    {
+        std::vector<int> c((size_t)S * D.cap, 0), L(S), ids(S);
+        size_t off = 0;
+        for (int s = 0; s < S; s++) {
+            memcpy(&c[(size_t)s * D.cap], prompts + off, (size_t)prompt_len[s] * sizeof(int));
+            off += prompt_len[s];
+            L[s] = prompt_len[s];
+            ids[s] = seq_id ? seq_id[s] : s;
+        }
+        err = cudaMemcpyAsync(D.c, c.data(), c.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (err == cudaSuccess) err = cudaMemcpyAsync(D.L, L.data(), S * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (err == cudaSuccess) err = cudaMemcpyAsync(D.seq_id, ids.data(), S * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (err == cudaSuccess) err = cudaMemsetAsync(D.gen, 0, S * sizeof(int), st);
+        if (err == cudaSuccess) err = cudaMemsetAsync(D.done, 0, S * sizeof(int), st);
+        if (err == cudaSuccess) err = cudaMemsetAsync(D.ctr, 0, 3 * sizeof(long long), st);
+        if (err == cudaSuccess) err = cudaMemsetAsync(D.n_done, 0, sizeof(int), st);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+        if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: %s", cudaGetErrorString(err)); return -3; }
+    }
+    cudaEvent_t ev[4];
+    for (int i = 0; i < 4; i++) cudaEventCreate(&ev[i]);
+    // ---- prefill: target 0..L-2, draft 0..L-3 (one sequence at a time) ----
+    cudaEventRecord(ev[0], st);
+    {
+        size_t off = 0;
+        int *buf = e->prefill_buf;
+        for (int s = 0; s < S; s++) {
+            const int *p = prompts + off;
+            off += prompt_len[s];
+            for (int which = 0; which < 2; which++) {
+                int n = prompt_len[s] - (which == 0 ? 1 : 2);
+                vxc_seqs *q = which == 0 ? e->ts : e->ds;
+                for (int done = 0; done < n;) {
+                    int ch = n - done < 64 ? n - done : 64;
+                    int meta[2] = {s, done};
+                    cudaMemcpyAsync(buf, p + done, ch * sizeof(int), cudaMemcpyHostToDevice, st);
+                    cudaMemcpyAsync(buf + 64, meta, sizeof meta, cudaMemcpyHostToDevice, st);
+                    int rc = vxc_forward(q, buf, buf + 64, buf + 65, 1, ch, NULL, 0, NULL, st);
+                    if (rc) return rc;
+                    // staging buffer is reused: finish before the next chunk overwrites it
+                    cudaStreamSynchronize(st);
+                    done += ch;
+                }
+            }
+        }
+    }
+    cudaEventRecord(ev[1], st);
+    // ---- round loop: first round eager, then a captured graph ----
+    int rc = enqueue_round(e, temp, seed);
+    if (rc) return rc;
+    if (!e->exec || e->D.max_new != max_new) {
+        if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = NULL; }
+        if (e->graph) { cudaGraphDestroy(e->graph); e->graph = NULL; }
+    }
+    // temp/seed are baked into the graph: rebuild it each call
+    if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = NULL; }
+    if (e->graph) { cudaGraphDestroy(e->graph); e->graph = NULL; }
+    err = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
+    if (err == cudaSuccess) {
+        rc = enqueue_round(e, temp, seed);
+        if (rc == 0) err = cudaMemcpyAsync(e->h_ndone, D.n_done, sizeof(int), cudaMemcpyDeviceToHost, st);
+        cudaError_t e2 = cudaStreamEndCapture(st, &e->graph);
+        if (err == cudaSuccess) err = e2;
+        if (rc) return rc;
+    }
+    if (err == cudaSuccess) err = cudaGraphInstantiate(&e->exec, e->graph, 0);
+    if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: graph: %s", cudaGetErrorString(err)); return -3; }
+    // each round emits >= 1 token per active sequence: max_new rounds suffice
+    int launched = 1, checked = 0;
+    cudaEvent_t rev[2];
+    cudaEventCreateWithFlags(&rev[0], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&rev[1], cudaEventDisableTiming);
+    int pending = 0;
+    while (launched < max_new + 1) {
+        err = cudaGraphLaunch(e->exec, st);
+        if (err != cudaSuccess) break;
+        cudaEventRecord(rev[launched & 1], st);
+        launched++;
+        pending++;
+        if (pending == 2) {
+            // wait for the older of the two rounds in flight and read its count
+            cudaEventSynchronize(rev[launched & 1]);
+            pending = 1;
+            checked++;
+            if (*(volatile int *)e->h_ndone >= S) break;
+        }
+    }
+    cudaEventRecord(ev[2], st);
+    err = cudaStreamSynchronize(st);
+    cudaEventDestroy(rev[0]);
+    cudaEventDestroy(rev[1]);
+    if (err == cudaSuccess) {
+        std::vector<int> gen(S);
+        err = cudaMemcpy(out, D.out, (size_t)S * max_new * sizeof(int), cudaMemcpyDeviceToHost);
+        if (err == cudaSuccess) err = cudaMemcpy(gen.data(), D.gen, S * sizeof(int), cudaMemcpyDeviceToHost);
+        if (err == cudaSuccess && counts) memcpy(counts, gen.data(), S * sizeof(int));
+        if (err == cudaSuccess && stats) {
+            long long ctr[3];
+            cudaMemcpy(ctr, D.ctr, sizeof ctr, cudaMemcpyDeviceToHost);
+            float a = 0, b = 0;
+            cudaEventElapsedTime(&a, ev[0], ev[1]);
+            cudaEventElapsedTime(&b, ev[1], ev[2]);
+            stats->rounds = launched;
+            stats->drafted = ctr[0];
+            stats->accepted = ctr[1];
+            stats->emitted = ctr[2];
+            stats->prefill_ms = a;
+            stats->decode_ms = b;
+        }
+    }
+    for (int i = 0; i < 4; i++) cudaEventDestroy(ev[i]);
+    (void)checked;
+    if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: %s", cudaGetErrorString(err)); return -3; }
+    return vxc_check_device_error(NULL);
+}

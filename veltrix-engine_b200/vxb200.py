@@ -48,6 +48,26 @@ PROTOTYPES = {
     "vx_set_n_threads": (None, [ctypes.c_int]),
     "vx_set_forward_timing_enabled": (None, [ctypes.c_int]),
     "vx_print_forward_timing": (None, []),
+    "vxc_sample_rows": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_uint64, _vp, _vp,
+                                        ctypes.c_uint, _vp, _vp]),
+    "vxc_accept_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    "vxc_accept": (ctypes.c_int, [_vp, ctypes.c_longlong, ctypes.c_longlong, _vp, ctypes.c_longlong,
+                                  ctypes.c_longlong, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                  ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "vxc_spec_create": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
+    "vxc_spec_destroy": (None, [_vp]),
+    "vxc_spec_generate": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                         ctypes.c_uint64, _vp, _vp, _vp]),
+    # speculative.h
+    "vx_speculative_create": (_vp, [_vp, _vp, ctypes.c_int]),
+    "vx_speculative_destroy": (None, [_vp]),
+    "vx_speculative_set_temp": (None, [_vp, ctypes.c_float, ctypes.c_float]),
+    "vx_speculative_generate": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, ctypes.c_int]),
+    "vx_speculative_generate_stream": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int]),
+    "vx_speculative_set_seed": (None, [_vp, ctypes.c_uint64]),
+    "vx_speculative_set_seq_id_base": (None, [_vp, ctypes.c_int]),
+    "vx_speculative_generate_batch": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp]),
+    "vx_speculative_get_stats": (ctypes.c_int, [_vp, _vp]),
     # veltrix_synth.h
     "vx_synth_write_gguf": (ctypes.c_int, [ctypes.c_char_p, _vp, ctypes.c_uint64]),
 }
@@ -80,6 +100,57 @@ class ModelHead(ctypes.Structure):
 def write_synth(path, n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab, wtype, seed, rope_theta=10000.0):
     c = SynthConfig(n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab, rope_theta, wtype)
     check(lib().vx_synth_write_gguf(path.encode(), ctypes.byref(c), seed), "vx_synth_write_gguf")
+
+
+class SpecStats(ctypes.Structure):
+    _fields_ = [("rounds", ctypes.c_longlong), ("drafted", ctypes.c_longlong), ("accepted", ctypes.c_longlong),
+                ("emitted", ctypes.c_longlong), ("prefill_ms", ctypes.c_double), ("decode_ms", ctypes.c_double)]
+
+
+class Speculative:
+    """vx_speculative_state (include/speculative.h) over two Model handles."""
+
+    def __init__(self, draft, target, k, temp=0.0, top_p=1.0, seed=1, seq_id_base=0):
+        self.h = lib().vx_speculative_create(draft.h, target.h, k)
+        if not self.h:
+            raise VxError("vx_speculative_create failed")
+        lib().vx_speculative_set_temp(self.h, temp, top_p)
+        lib().vx_speculative_set_seed(self.h, seed)
+        lib().vx_speculative_set_seq_id_base(self.h, seq_id_base)
+
+    def generate(self, prompt, max_tokens):
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max_tokens, np.int32)
+        n = lib().vx_speculative_generate(self.h, p.ctypes.data, p.size, out.ctypes.data, max_tokens)
+        return out[:n]
+
+    def generate_batch(self, prompts, max_tokens):
+        import numpy as np
+        ps = [np.ascontiguousarray(p, dtype=np.int32) for p in prompts]
+        outs = [np.zeros(max_tokens, np.int32) for _ in ps]
+        pa = (_vp * len(ps))(*[p.ctypes.data for p in ps])
+        oa = (_vp * len(ps))(*[o.ctypes.data for o in outs])
+        lens = np.array([p.size for p in ps], np.int32)
+        cnt = np.zeros(len(ps), np.int32)
+        lib().vx_speculative_generate_batch(self.h, pa, lens.ctypes.data, len(ps), oa, max_tokens, cnt.ctypes.data)
+        return [o[:c] for o, c in zip(outs, cnt)]
+
+    def stats(self):
+        s = SpecStats()
+        check(lib().vx_speculative_get_stats(self.h, ctypes.byref(s)), "vx_speculative_get_stats")
+        return s
+
+    def close(self):
+        if self.h:
+            lib().vx_speculative_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Model:
