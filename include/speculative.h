@@ -61,6 +61,11 @@ typedef struct {
 
 int vx_speculative_get_stats(const vx_speculative_state *state, vx_speculative_stats *out);
 
+/* Device time of one piece of the last generate call's final round, averaged
+ * over `reps` re-runs: which = 0 target verify forward, 1 draft step, 2 fused
+ * acceptance (vxc_spec_probe).  Returns VX_OK or a vx_error code. */
+int vx_speculative_probe(vx_speculative_state *state, int which, int reps, double *ms, double *kv_bytes);
+
 #ifdef __cplusplus
 }
 #endif

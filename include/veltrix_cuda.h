@@ -36,6 +36,11 @@ const char *vxc_error_string(void);
  * trapping (timeouts, out-of-range token ids).  Synchronises the device. */
 int vxc_check_device_error(unsigned int *code_out);
 
+/* Number of kernels this library has launched in this process (measurement
+ * aid, no reference counterpart); a CUDA-graph replay counts the kernels it
+ * holds. */
+long long vxc_launch_count(void);
+
 /* ---- quantised weight matrices ------------------------------------------ */
 
 typedef struct vxc_qmat vxc_qmat;
@@ -187,6 +192,14 @@ void vxc_spec_destroy(vxc_spec *e);
  * commit) runs on the device as one CUDA graph per round. */
 int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *prompt_len, const int *seq_id, int n_seq,
                       int max_new, float temp, uint64_t seed, int *out, int *counts, vxc_spec_stats *stats);
+
+/* Measurement hook (no reference counterpart): after a generate call, re-run
+ * one piece of the last round `reps` times and return its average device
+ * time in *ms: which = 0 the (k+1)-row target verify forward, 1 one draft
+ * step, 2 the fused acceptance kernel.  *kv_bytes (may be NULL) receives the
+ * K/V cache bytes one such forward reads and writes.  The committed tokens
+ * are not changed. */
+int vxc_spec_probe(vxc_spec *e, int which, int reps, double *ms, double *kv_bytes);
 
 #ifdef __cplusplus
 }

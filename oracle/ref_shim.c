@@ -7,8 +7,8 @@
  *    land here.  The reference calls it in place for attn_o
  *    (src/model.c:543-544: y == x), a data race under OpenMP; this shim
  *    hands the kernel a private copy of x, i.e. the out-of-place GEMV.
- * 2. Accessors for struct vx_model fields, so Python tests need no struct
- *    layout of their own.
+ * The struct vx_model accessors live in ref_access.c, which both reference
+ * builds link.
  */
 #include <stdlib.h>
 #include <string.h>
@@ -27,12 +27,4 @@ void vx_gemv_f32(float *restrict y, const float *restrict A, const float *restri
         return;
     }
     vxref_gemv_f32_impl(y, A, x, rows, cols);
-}
-
-int vxref_cache_len(const vx_model *m) { return m->cache_len; }
-void vxref_set_cache_len(vx_model *m, int len) { m->cache_len = len; }
-void vxref_config(const vx_model *m, int *out) {
-    out[0] = m->config.n_layers; out[1] = m->config.n_heads; out[2] = m->config.n_kv_heads;
-    out[3] = m->config.n_embd; out[4] = m->config.n_head_dim; out[5] = m->config.n_ff;
-    out[6] = m->config.n_vocab; out[7] = m->config.n_ctx;
 }

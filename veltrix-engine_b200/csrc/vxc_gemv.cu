@@ -88,8 +88,8 @@ extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int 
         long long total = (long long)rows * w->nblk;
         int th = 256;
         unsigned gb = (unsigned)((total + th - 1) / th);
-        if (type == 2) k_repack_q4_0<<<gb, th>>>(staging, w->qs, w->sc, rows, w->nblk);
-        else k_repack_q8_0<<<gb, th>>>(staging, w->qs, w->sc, rows, w->nblk);
+        if (type == 2) (k_repack_q4_0<<<gb, th>>>(staging, w->qs, w->sc, rows, w->nblk), vxc_count_launches(1));
+        else (k_repack_q8_0<<<gb, th>>>(staging, w->qs, w->sc, rows, w->nblk), vxc_count_launches(1));
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -204,7 +204,7 @@ __global__ void k_splitk_reduce(const float *__restrict__ ws, int ks, int MR, fl
 
 int vxc_launch_splitk_reduce(const float *ws, int ks, int M, int R, float *y, cudaStream_t st) {
     int MR = M * R;
-    k_splitk_reduce<<<(MR + 255) / 256, 256, 0, st>>>(ws, ks, MR, y);
+    (k_splitk_reduce<<<(MR + 255) / 256, 256, 0, st>>>(ws, ks, MR, y), vxc_count_launches(1));
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -239,9 +239,9 @@ extern "C" int vxc_qgemv_simt(const vxc_qmat *w, const float *x, int M, float *y
     size_t smem = (size_t)SIMT_MC * bps * 32 * sizeof(float);
     float *dst = ks > 1 ? (float *)workspace : y;
     if (w->type == 2)
-        k_qgemv_simt<2><<<grid, 128, smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, bps);
+        (k_qgemv_simt<2><<<grid, 128, smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, bps), vxc_count_launches(1));
     else
-        k_qgemv_simt<8><<<grid, 128, smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, bps);
+        (k_qgemv_simt<8><<<grid, 128, smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, bps), vxc_count_launches(1));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { vxc_set_error("vxc_qgemv_simt: %s", cudaGetErrorString(e)); return -3; }
     if (ks > 1) return vxc_launch_splitk_reduce(dst, ks, M, w->rows, y, st);

@@ -480,8 +480,8 @@ static cudaError_t launch_tc(const vxc_qmat *w, const float *x, int M, float *ds
         attr_set = true;
     }
     dim3 grid(w->ntile, p.ks);
-    k_qgemv_tc<QT, NT><<<grid, 192, p.smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, p.nbs,
-                                                   vxc_device_error_ptr());
+    (k_qgemv_tc<QT, NT><<<grid, 192, p.smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, p.nbs,
+                                                   vxc_device_error_ptr()), vxc_count_launches(1));
     return cudaGetLastError();
 }
 

@@ -12,3 +12,5 @@ int vxc_require_device(void);
 unsigned int *vxc_device_error_ptr(void);
 int vxc_launch_splitk_reduce(const float *ws, int ks, int M, int R, float *y, cudaStream_t st);
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
+// Library-wide count of kernel launches (a CUDA-graph replay adds its kernels).
+void vxc_count_launches(long long n);

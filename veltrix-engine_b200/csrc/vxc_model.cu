@@ -142,8 +142,8 @@ __global__ void k_rope_kv(float *__restrict__ qkv, int T, const int *__restrict_
     }
     const int np = hd / 2;
     const float2 *cs = rope + (size_t)pos * np;
-    float *kdst = kc + ((size_t)slot * max_ctx + pos) * kvd;
-    float *vdst = vc + ((size_t)slot * max_ctx + pos) * kvd;
+    // head-major cache: [slot][kv head][pos][hd]
+    auto cache_row = [&](float *c, int kh) { return c + (((size_t)slot * KH + kh) * max_ctx + pos) * hd; };
     for (int i = threadIdx.x; i < (H + KH) * np; i += blockDim.x) {
         int head = i / np, p = i % np;
         float2 c = cs[p];
@@ -156,139 +156,206 @@ __global__ void k_rope_kv(float *__restrict__ qkv, int T, const int *__restrict_
             v[0] = r0;
             v[1] = r1;
         } else {
-            int off = (head - H) * hd + 2 * p;
-            kdst[off] = r0;
-            kdst[off + 1] = r1;
+            float *kdst = cache_row(kc, head - H) + 2 * p;
+            kdst[0] = r0;
+            kdst[1] = r1;
         }
     }
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) vdst[i] = row[E + kvd + i];
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) cache_row(vc, i / hd)[i % hd] = row[E + kvd + i];
 }
 
-// Decode/verify attention, split over the context.  CTA = (group g, kv head,
-// query chunk) x split.  Queries are the rows of group g times the q heads of
-// the kv head (GQA mapping kv_h = h*KH/H, src/model.c:303).  Each CTA writes
-// per query: running max m, sum l of exp(s - m), and o = sum exp(s - m) v.
-__global__ void __launch_bounds__(128) k_attn_partial(const float *__restrict__ qkv, int T,
-                                                      const int *__restrict__ d_slot,
-                                                      const int *__restrict__ d_pos, int H, int KH, int hd,
-                                                      const float *__restrict__ kc, const float *__restrict__ vc,
-                                                      int max_ctx, int SL, int nqc, float *__restrict__ part) {
-    extern __shared__ float sm[];
-    const int G = H / KH;
-    const int nq = T * G;
+// Decode/verify attention, split over the context (flash-decoding style).
+// CTA = (group g, kv head, chunk of <= ATTN_QC queries) x one split of SL
+// positions.  The queries are the rows of group g times the q heads that
+// share the kv head (GQA mapping kv_h = h*KH/H, src/model.c:303), so each K/V
+// byte of the split is read from HBM once for all of them.
+//
+// The cache is head-major ([slot][kv head][pos][hd]), so the split's K (and
+// V) rows are one contiguous span.  Tiles of ATTN_T positions stream through
+// an ATTN_NS-stage cp.async ring: the K tiles, then the V tiles of the split.
+// In shared memory the 16-byte chunk c of tile row p sits at c ^ (p & 7), so
+// both access patterns are free of bank conflicts:
+//   scores  lane = position, loop over chunks (q chunk is a broadcast),
+//   P.V     lane = chunk of the output row, loop over positions.
+// Per query the CTA writes its split's record [m, l, -, -, o[hd]] (16-byte
+// aligned): max m, sum l of exp(s - m) and o = sum exp(s - m) v;
+// k_attn_combine merges the splits.
+#define ATTN_NS 4
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qkv, int T, const int *__restrict__ d_slot,
+                                                    const int *__restrict__ d_pos, int H, int KH,
+                                                    const float *__restrict__ kc, const float *__restrict__ vc,
+                                                    int n_slots, int max_ctx, int SL, int nqc,
+                                                    float *__restrict__ part) {
+    constexpr int NC = HD / 4;                  // float4 chunks per row
+    constexpr int QPW = 32 / NC;                // query slots per warp in P.V
+    constexpr int QT1 = ATTN_QC / 4;            // queries per thread in the score pass
+    constexpr int QT3 = (ATTN_QC + 4 * QPW - 1) / (4 * QPW);   // ... in the P.V pass
+    static_assert(HD % 32 == 0 && HD <= 128, "head dim");
+    extern __shared__ __align__(16) float sm[];
+    float4 *ring = reinterpret_cast<float4 *>(sm);                 // [NS][T][NC]
+    float4 *qs = ring + ATTN_NS * ATTN_T * NC;                      // [QC][NC]
+    float *sc = reinterpret_cast<float *>(qs + ATTN_QC * NC);       // [QC][SL+1]
+    __shared__ float qmax[ATTN_QC], qsum[ATTN_QC];
+    const int G = H / KH, nq = T * G;
     const int bx = blockIdx.x;
     const int qc = bx % nqc;
     const int kvh = (bx / nqc) % KH;
     const int g = bx / (nqc * KH);
-    const int split = blockIdx.y;
-    const int nsplit = gridDim.y;
+    const int split = blockIdx.y, nsplit = gridDim.y;
     const int q0 = qc * ATTN_QC;
     const int nql = min(ATTN_QC, nq - q0);
-    const int E = H * hd, kvd = KH * hd;
+    const int E = H * HD, kvd = KH * HD;
     const int slot = d_slot[g];
     const int base = d_pos[g];
     const int p0 = split * SL;
-    const int pend = min(p0 + SL, base + T);        // exclusive, causal bound of the group
-    const int tid = threadIdx.x;
-    const int hdp = hd + 1;
-    float *qs = sm;                                 // [QC][hd]
-    float *ks = qs + ATTN_QC * hd;                  // [T][hd+1]
-    float *sc = ks + ATTN_T * hdp;                  // [QC][SL]
-    const float scale = 1.0f / sqrtf((float)hd);
-    // part layout: [g][kvh][q][split][hd + 2]
+    // exclusive end: causal bound of the group, clamped to the cache (k_rope_kv
+    // flags positions outside it; a bad slot reads nothing)
+    const int pend = (slot < 0 || slot >= n_slots || base < 0) ? 0 : min(min(p0 + SL, base + T), max_ctx);
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    const int SLP = SL + 1;
     auto part_ptr = [&](int q) {
-        return part + ((((size_t)g * KH + kvh) * (size_t)nq + q) * nsplit + split) * (hd + 2);
+        return part + ((((size_t)g * KH + kvh) * (size_t)nq + q) * nsplit + split) * (HD + 4);
     };
     if (nql <= 0) return;
     if (p0 >= pend) {
-        for (int i = tid; i < nql; i += blockDim.x) {
-            float *pp = part_ptr(q0 + i);
+        if (tid < nql) {
+            float *pp = part_ptr(q0 + tid);
             pp[0] = -INFINITY;
             pp[1] = 0.0f;
         }
         return;
     }
     const int npos = pend - p0;
-    for (int i = tid; i < nql * hd; i += blockDim.x) {
-        int ql = i / hd, d = i % hd;
-        int q = q0 + ql;
-        int t = q / G, j = q % G;
-        int h = kvh * G + j;
-        qs[ql * hd + d] = qkv[(size_t)(g * T + t) * (E + 2 * kvd) + (size_t)h * hd + d];
-    }
-    const float *kbase = kc + (size_t)slot * max_ctx * kvd + (size_t)kvh * hd;
-    const float *vbase = vc + (size_t)slot * max_ctx * kvd + (size_t)kvh * hd;
-    // scores
-    for (int t0 = 0; t0 < npos; t0 += ATTN_T) {
-        const int nt = min(ATTN_T, npos - t0);
-        __syncthreads();
-        for (int i = tid; i < nt * hd; i += blockDim.x) {
-            int r = i / hd, d = i % hd;
-            ks[r * hdp + d] = kbase[(size_t)(p0 + t0 + r) * kvd + d];
-        }
-        __syncthreads();
-        for (int i = tid; i < nql * ATTN_T; i += blockDim.x) {
-            int ql = i / ATTN_T, r = i % ATTN_T;
-            if (r >= nt) continue;
-            int t = (q0 + ql) / G;
-            int pos = p0 + t0 + r;
-            float s = -INFINITY;
-            if (pos <= base + t) {
-                const float *qv = qs + ql * hd, *kv = ks + r * hdp;
-                float a = 0.0f;
-                for (int d = 0; d < hd; d++) a = fmaf(qv[d], kv[d], a);
-                s = a * scale;
+    const int ntile = (npos + ATTN_T - 1) / ATTN_T;
+    const size_t head_off = ((size_t)slot * KH + kvh) * (size_t)max_ctx * HD;
+    const float4 *ksrc = reinterpret_cast<const float4 *>(kc + head_off + (size_t)p0 * HD);
+    const float4 *vsrc = reinterpret_cast<const float4 *>(vc + head_off + (size_t)p0 * HD);
+    // tile i < ntile: K tile i; i >= ntile: V tile i - ntile
+    auto issue = [&](int i) {
+        if (i < 2 * ntile) {
+            const int t = i < ntile ? i : i - ntile;
+            const float4 *src = (i < ntile ? ksrc : vsrc) + (size_t)t * ATTN_T * NC;
+            const int rows = min(ATTN_T, npos - t * ATTN_T);
+            float4 *dst = ring + (i % ATTN_NS) * ATTN_T * NC;
+            for (int e = tid; e < rows * NC; e += 128) {
+                const int p = e / NC, c = e % NC;
+                cp_async16(dst + p * NC + (c ^ (p & 7)), src + e);
             }
-            sc[ql * SL + t0 + r] = s;
         }
+        cp_async_commit();
+    };
+    for (int i = 0; i < ATTN_NS - 1; i++) issue(i);
+    // queries of this CTA (post-RoPE rows of qkv)
+    for (int e = tid; e < nql * NC; e += 128) {
+        const int ql = e / NC, c = e % NC;
+        const int q = q0 + ql, t = q / G, h = kvh * G + q % G;
+        qs[ql * NC + c] = reinterpret_cast<const float4 *>(qkv + (size_t)(g * T + t) * (E + 2 * kvd) + (size_t)h * HD)[c];
     }
-    __syncthreads();
-    // per-query max and exp-sum over this split (one warp per query)
-    const int w = tid >> 5, l = tid & 31;
-    __shared__ float qmax[ATTN_QC], qsum[ATTN_QC];
-    for (int ql = w; ql < nql; ql += 4) {
-        float mx = -INFINITY;
-        for (int i = l; i < npos; i += 32) mx = fmaxf(mx, sc[ql * SL + i]);
-        mx = warp_max(mx);
-        float su = 0.0f;
-        for (int i = l; i < npos; i += 32) {
-            float s = sc[ql * SL + i];
-            float e = (s == -INFINITY) ? 0.0f : expf(s - mx);
-            sc[ql * SL + i] = e;
-            su += e;
-        }
-        su = warp_sum(su);
-        if (l == 0) { qmax[ql] = mx; qsum[ql] = su; }
-    }
-    // o = sum e * v
-    float acc[ATTN_QC];
+    const float scale = 1.0f / sqrtf((float)HD);
+    float4 acc[QT3];
 #pragma unroll
-    for (int i = 0; i < ATTN_QC; i++) acc[i] = 0.0f;
-    for (int t0 = 0; t0 < npos; t0 += ATTN_T) {
-        const int nt = min(ATTN_T, npos - t0);
+    for (int j = 0; j < QT3; j++) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int qslot = lane / NC, cc = lane % NC;
+    for (int i = 0; i < 2 * ntile; i++) {
+        issue(i + ATTN_NS - 1);
+        cp_async_wait<ATTN_NS - 1>();
         __syncthreads();
-        for (int i = tid; i < nt * hd; i += blockDim.x) {
-            int r = i / hd, d = i % hd;
-            ks[r * hdp + d] = vbase[(size_t)(p0 + t0 + r) * kvd + d];
+        if (i == ntile) {
+            // softmax pieces of the split: one warp per query
+            for (int ql = w; ql < nql; ql += 4) {
+                float *row = sc + ql * SLP;
+                float mx = -INFINITY;
+                for (int p = lane; p < npos; p += 32) mx = fmaxf(mx, row[p]);
+                mx = warp_max(mx);
+                float su = 0.0f;
+                for (int p = lane; p < npos; p += 32) {
+                    const float s = row[p];
+                    const float e = (s == -INFINITY) ? 0.0f : expf(s - mx);
+                    row[p] = e;
+                    su += e;
+                }
+                su = warp_sum(su);
+                if (lane == 0) { qmax[ql] = mx; qsum[ql] = su; }
+            }
+            __syncthreads();
         }
-        __syncthreads();
-        for (int d = tid; d < hd; d += blockDim.x) {
-            // hd <= 128 = blockDim.x: one pass
+        const float4 *tile = ring + (i % ATTN_NS) * ATTN_T * NC;
+        if (i < ntile) {
+            // scores: lane = position p of the tile
+            const int t0 = i * ATTN_T, p = lane;
+            const int pos = p0 + t0 + p;
+            float a[QT1];
 #pragma unroll
-            for (int ql = 0; ql < ATTN_QC; ql++) {
-                if (ql < nql) {
-                    float a = acc[ql];
-                    for (int r = 0; r < nt; r++) a = fmaf(sc[ql * SL + t0 + r], ks[r * hdp + d], a);
-                    acc[ql] = a;
+            for (int j = 0; j < QT1; j++) a[j] = 0.0f;
+            if (t0 + p < npos) {
+                const float4 *krow = tile + p * NC;
+#pragma unroll 4
+                for (int c = 0; c < NC; c++) {
+                    const float4 kv = krow[c ^ (p & 7)];
+#pragma unroll
+                    for (int j = 0; j < QT1; j++) {
+                        const int ql = w + 4 * j;
+                        if (ql < nql) {
+                            const float4 qv = qs[ql * NC + c];
+                            float s = a[j];
+                            s = fmaf(qv.x, kv.x, s);
+                            s = fmaf(qv.y, kv.y, s);
+                            s = fmaf(qv.z, kv.z, s);
+                            s = fmaf(qv.w, kv.w, s);
+                            a[j] = s;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < QT1; j++) {
+                    const int ql = w + 4 * j;
+                    if (ql < nql) {
+                        const int tq = (q0 + ql) / G;
+                        sc[ql * SLP + t0 + p] = (pos <= base + tq) ? a[j] * scale : -INFINITY;
+                    }
+                }
+            }
+        } else if (qslot < QPW) {
+            // P.V: lane = (query slot, output chunk cc)
+            const int t0 = (i - ntile) * ATTN_T;
+            const int nt = min(ATTN_T, npos - t0);
+            for (int p = 0; p < nt; p++) {
+                const float4 vv = tile[p * NC + (cc ^ (p & 7))];
+#pragma unroll
+                for (int j = 0; j < QT3; j++) {
+                    const int ql = (w * QPW + qslot) + j * 4 * QPW;
+                    if (ql < nql) {
+                        const float e = sc[ql * SLP + t0 + p];
+                        acc[j].x = fmaf(e, vv.x, acc[j].x);
+                        acc[j].y = fmaf(e, vv.y, acc[j].y);
+                        acc[j].z = fmaf(e, vv.z, acc[j].z);
+                        acc[j].w = fmaf(e, vv.w, acc[j].w);
+                    }
                 }
             }
         }
+        __syncthreads();
     }
-    __syncthreads();
-    for (int d = tid; d < hd; d += blockDim.x) {
+    cp_async_wait<0>();
+    if (qslot < QPW) {
 #pragma unroll
-        for (int ql = 0; ql < ATTN_QC; ql++)
-            if (ql < nql) part_ptr(q0 + ql)[2 + d] = acc[ql];
+        for (int j = 0; j < QT3; j++) {
+            const int ql = (w * QPW + qslot) + j * 4 * QPW;
+            if (ql < nql) reinterpret_cast<float4 *>(part_ptr(q0 + ql) + 4)[cc] = acc[j];
+        }
     }
     if (tid < nql) {
         float *pp = part_ptr(q0 + tid);
@@ -305,13 +372,13 @@ __global__ void k_attn_combine(const float *__restrict__ part, int T, int H, int
     const int q = idx % nq;
     const int kvh = (idx / nq) % KH;
     const int g = idx / (nq * KH);
-    const float *pp = part + (size_t)idx * nsplit * (hd + 2);
+    const float *pp = part + (size_t)idx * nsplit * (hd + 4);
     float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, pp[(size_t)s * (hd + 2)]);
+    for (int s = 0; s < nsplit; s++) M = fmaxf(M, pp[(size_t)s * (hd + 4)]);
     float Ls = 0.0f;
     for (int s = 0; s < nsplit; s++) {
-        float ms = pp[(size_t)s * (hd + 2)];
-        if (ms != -INFINITY) Ls += expf(ms - M) * pp[(size_t)s * (hd + 2) + 1];
+        float ms = pp[(size_t)s * (hd + 4)];
+        if (ms != -INFINITY) Ls += expf(ms - M) * pp[(size_t)s * (hd + 4) + 1];
     }
     const float inv = 1.0f / (Ls + 1e-10f);
     const int t = q / G, h = kvh * G + q % G;
@@ -319,8 +386,8 @@ __global__ void k_attn_combine(const float *__restrict__ part, int T, int H, int
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float o = 0.0f;
         for (int s = 0; s < nsplit; s++) {
-            float ms = pp[(size_t)s * (hd + 2)];
-            if (ms != -INFINITY) o += expf(ms - M) * pp[(size_t)s * (hd + 2) + 2 + d];
+            float ms = pp[(size_t)s * (hd + 4)];
+            if (ms != -INFINITY) o += expf(ms - M) * pp[(size_t)s * (hd + 4) + 4 + d];
         }
         dst[d] = o * inv;
     }
@@ -401,7 +468,7 @@ extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *
     int rc = vxc_require_device();
     if (rc) return rc;
     if (!cfg || !tok_embd || !tok_embd->data || !layers || !out || cfg->n_layers <= 0 || cfg->n_heads <= 0 ||
-        cfg->n_kv_heads <= 0 || cfg->n_heads % cfg->n_kv_heads || cfg->n_head_dim % 2 || cfg->n_head_dim > 128 ||
+        cfg->n_kv_heads <= 0 || cfg->n_heads % cfg->n_kv_heads || cfg->n_head_dim % 32 || cfg->n_head_dim > 128 ||
         cfg->n_embd != cfg->n_heads * cfg->n_head_dim || cfg->n_embd % 32 || cfg->n_ff % 32) {
         vxc_set_error("vxc_net_create: unsupported configuration");
         return -4;
@@ -502,7 +569,20 @@ extern "C" size_t vxc_net_weight_bytes(const vxc_net *n) { return n ? n->weight_
 // host: sequences + forward
 // ---------------------------------------------------------------------------
 static size_t attn_smem(int hd, int SL) {
-    return ((size_t)ATTN_QC * hd + (size_t)ATTN_T * (hd + 1) + (size_t)ATTN_QC * SL) * sizeof(float);
+    return ((size_t)ATTN_NS * ATTN_T * hd + (size_t)ATTN_QC * hd + (size_t)ATTN_QC * (SL + 1)) * sizeof(float);
+}
+
+typedef void (*attn_kernel_t)(const float *, int, const int *, const int *, int, int, const float *, const float *,
+                              int, int, int, int, float *);
+
+static attn_kernel_t attn_kernel(int hd) {
+    switch (hd) {
+        case 32: return k_attn_split<32>;
+        case 64: return k_attn_split<64>;
+        case 96: return k_attn_split<96>;
+        case 128: return k_attn_split<128>;
+        default: return NULL;
+    }
 }
 
 extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int max_rows, vxc_seqs **out) {
@@ -518,13 +598,13 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     s->max_rows = max_rows;
     const int E = c.n_embd, kvd = c.n_kv_heads * c.n_head_dim, F = c.n_ff, hd = c.n_head_dim;
     size_t kvn = (size_t)c.n_layers * n_slots * max_ctx * kvd;
-    // attention split length: at most 16 splits, tiles of 32 positions
+    // attention split length: at most 16 splits of >= 64 positions (whole tiles)
     int SL = (max_ctx + 15) / 16;
     SL = ((SL + ATTN_T - 1) / ATTN_T) * ATTN_T;
-    if (SL < 256) SL = 256;
+    if (SL < 64) SL = 64;
     s->attn_sl = SL;
     s->attn_splits = (max_ctx + SL - 1) / SL;
-    size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 2);
+    size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 4);
     size_t ws = 0;
     for (int l = 0; l < c.n_layers; l++) {
         const vxc_layer_dev *d = &net->layers[l];
@@ -559,8 +639,18 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
 #undef ALLOC
     if (e == cudaSuccess) e = cudaMemset(s->k, 0, kvn * 4);
     if (e == cudaSuccess) e = cudaMemset(s->v, 0, kvn * 4);
-    if (e == cudaSuccess && attn_smem(hd, SL) > 48 * 1024)
-        e = cudaFuncSetAttribute(k_attn_partial, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(hd, SL));
+    if (e == cudaSuccess && !attn_kernel(hd)) {
+        vxc_set_error("vxc_seqs_create: head dim %d not supported (32, 64, 96 or 128)", hd);
+        vxc_seqs_destroy(s);
+        return -7;
+    }
+    if (e == cudaSuccess && attn_smem(hd, SL) > 227 * 1024) {
+        vxc_set_error("vxc_seqs_create: context %d too long for the attention split", max_ctx);
+        vxc_seqs_destroy(s);
+        return -4;
+    }
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_kernel(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(hd, SL));
     if (e != cudaSuccess) {
         vxc_set_error("vxc_seqs_create: %s", cudaGetErrorString(e));
         vxc_seqs_destroy(s);
@@ -600,35 +690,36 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     cudaStream_t st = (cudaStream_t)stream;
     unsigned int *err = vxc_device_error_ptr();
     int rc;
-    k_embed<<<M, 256, 0, st>>>(n->embd, n->embd_type, n->embd_row_bytes, n->embd_rows, E, d_tokens, s->x, err);
+    (k_embed<<<M, 256, 0, st>>>(n->embd, n->embd_type, n->embd_row_bytes, n->embd_rows, E, d_tokens, s->x, err), vxc_count_launches(1));
     const int G = H / KH, nq = T * G, nqc = (nq + ATTN_QC - 1) / ATTN_QC;
     const size_t asm_bytes = attn_smem(hd, s->attn_sl);
     for (int l = 0; l < c.n_layers; l++) {
         const vxc_layer_dev *d = &n->layers[l];
         float *kc = s->k + (size_t)l * s->n_slots * s->max_ctx * kvd;
         float *vc = s->v + (size_t)l * s->n_slots * s->max_ctx * kvd;
-        k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->attn_norm, E, NULL, s->h);
+        (k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->attn_norm, E, NULL, s->h), vxc_count_launches(1));
         if ((rc = vxc_qgemv(d->wqkv, s->h, M, s->qkv, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        k_rope_kv<<<M, 128, 0, st>>>(s->qkv, T, d_slot, d_pos, n->rope, c.max_pos, H, KH, hd, kc, vc, s->n_slots,
-                                     s->max_ctx, err);
-        k_attn_partial<<<dim3(n_groups * KH * nqc, s->attn_splits), 128, asm_bytes, st>>>(
-            s->qkv, T, d_slot, d_pos, H, KH, hd, kc, vc, s->max_ctx, s->attn_sl, nqc, s->attn_part);
-        k_attn_combine<<<n_groups * KH * nq, 128, 0, st>>>(s->attn_part, T, H, KH, hd, s->attn_splits, s->att);
+        (k_rope_kv<<<M, 128, 0, st>>>(s->qkv, T, d_slot, d_pos, n->rope, c.max_pos, H, KH, hd, kc, vc, s->n_slots,
+                                     s->max_ctx, err), vxc_count_launches(1));
+        (attn_kernel(hd)<<<dim3(n_groups * KH * nqc, s->attn_splits), 128, asm_bytes, st>>>(
+            s->qkv, T, d_slot, d_pos, H, KH, kc, vc, s->n_slots, s->max_ctx, s->attn_sl, nqc, s->attn_part),
+         vxc_count_launches(1));
+        (k_attn_combine<<<n_groups * KH * nq, 128, 0, st>>>(s->attn_part, T, H, KH, hd, s->attn_splits, s->att), vxc_count_launches(1));
         if ((rc = vxc_qgemv(d->wo, s->att, M, s->o, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E);
-        k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->ffn_norm, E, NULL, s->h);
+        (k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E), vxc_count_launches(1));
+        (k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->ffn_norm, E, NULL, s->h), vxc_count_launches(1));
         if ((rc = vxc_qgemv(d->wgu, s->h, M, s->gu, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        k_swiglu<<<nblk((size_t)M * F, 256), 256, 0, st>>>(s->gu, M, F, s->hf);
+        (k_swiglu<<<nblk((size_t)M * F, 256), 256, 0, st>>>(s->gu, M, F, s->hf), vxc_count_launches(1));
         if ((rc = vxc_qgemv(d->wd, s->hf, M, s->o, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E);
+        (k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E), vxc_count_launches(1));
     }
     if (n_logit_rows > 0) {
         const int V = c.n_vocab, R = n->out->rows;
         if (n->out_norm)
-            k_rmsnorm<<<n_logit_rows, 256, 0, st>>>(s->x, n->out_norm, E, d_logit_rows, s->h);
+            (k_rmsnorm<<<n_logit_rows, 256, 0, st>>>(s->x, n->out_norm, E, d_logit_rows, s->h), vxc_count_launches(1));
         else
             return vxc_set_error("vxc_forward: models without output_norm are not supported"), -7;
-        if (R < V) k_fill<<<nblk((size_t)n_logit_rows * V, 256), 256, 0, st>>>(d_logits, (size_t)n_logit_rows * V, -1e30f);
+        if (R < V) (k_fill<<<nblk((size_t)n_logit_rows * V, 256), 256, 0, st>>>(d_logits, (size_t)n_logit_rows * V, -1e30f), vxc_count_launches(1));
         if (R == V) {
             if ((rc = vxc_qgemv(n->out, s->h, n_logit_rows, d_logits, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
         } else {

@@ -5,8 +5,16 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
+
 static thread_local char t_err[512] = "";
 static unsigned int *g_err_ptr[64];   // per device
+
+static std::atomic<long long> g_launches{0};
+
+void vxc_count_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+extern "C" long long vxc_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 void vxc_set_error(const char *fmt, ...) {
     va_list ap;

@@ -155,8 +155,8 @@ extern "C" int vxc_sample_rows(const float *logits, int n_rows, int V, float tem
         vxc_set_error("vxc_sample_rows: bad arguments");
         return -4;
     }
-    k_sample_rows<<<n_rows, SMP_THREADS, 0, (cudaStream_t)stream>>>(logits, V, temp, seed, d_pos, d_seq, purpose,
-                                                                    d_tokens);
+    (k_sample_rows<<<n_rows, SMP_THREADS, 0, (cudaStream_t)stream>>>(logits, V, temp, seed, d_pos, d_seq, purpose,
+                                                                    d_tokens), vxc_count_launches(1));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { vxc_set_error("vxc_sample_rows: %s", cudaGetErrorString(e)); return -3; }
     return 0;
@@ -287,9 +287,9 @@ static int launch_accept(const float *P, long long p_seq, long long p_pos, const
                          long long q_pos, const int *d, int n_seq, int k, int V, float temp, uint64_t seed,
                          const int *seq_id, const int *pos0, int *n_acc, int *next, void *ws, cudaStream_t st) {
     size_t a = ((size_t)n_seq * (k + 1) * sizeof(AccStat) + 255) & ~(size_t)255;
-    k_accept<<<dim3(n_seq, k + 1), SMP_THREADS, 0, st>>>(P, p_seq, p_pos, Q, q_seq, q_pos, d, k, V, temp, seed,
+    (k_accept<<<dim3(n_seq, k + 1), SMP_THREADS, 0, st>>>(P, p_seq, p_pos, Q, q_seq, q_pos, d, k, V, temp, seed,
                                                          seq_id, pos0, n_acc, next, (AccStat *)ws,
-                                                         (unsigned int *)((char *)ws + a));
+                                                         (unsigned int *)((char *)ws + a)), vxc_count_launches(1));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { vxc_set_error("vxc_accept: %s", cudaGetErrorString(e)); return -3; }
     return 0;
@@ -519,25 +519,25 @@ static int enqueue_round(vxc_spec *e, float temp, uint64_t seed) {
     cudaStream_t st = e->st;
     const int tb = 128, gb = (S + tb - 1) / tb;
     int rc;
-    k_round_prep<<<gb, tb, 0, st>>>(D);
+    (k_round_prep<<<gb, tb, 0, st>>>(D), vxc_count_launches(1));
     // draft step 0: 2 rows per sequence
     if ((rc = vxc_forward(e->ds, D.tok0, D.slot, D.pos0, S, 2, D.lrow0, S, e->dlog, st))) return rc;
-    k_sample_rows<<<S, SMP_THREADS, 0, st>>>(e->dlog, V, temp, seed, D.dpos, D.seq_id, VXC_PURPOSE_DRAFT, D.dtok);
+    (k_sample_rows<<<S, SMP_THREADS, 0, st>>>(e->dlog, V, temp, seed, D.dpos, D.seq_id, VXC_PURPOSE_DRAFT, D.dtok), vxc_count_launches(1));
     for (int i = 1; i < k; i++) {
         float *q = e->dlog + (size_t)i * S * V;
         // rows: d_i at position L+i-1 == dpos[i-1]; logits of all S rows
         if ((rc = vxc_forward(e->ds, D.dtok + (size_t)(i - 1) * S, D.slot, D.dpos + (size_t)(i - 1) * S, S, 1,
                               D.slot, S, q, st)))
             return rc;
-        k_sample_rows<<<S, SMP_THREADS, 0, st>>>(q, V, temp, seed, D.dpos + (size_t)i * S, D.seq_id,
-                                                 VXC_PURPOSE_DRAFT, D.dtok + (size_t)i * S);
+        (k_sample_rows<<<S, SMP_THREADS, 0, st>>>(q, V, temp, seed, D.dpos + (size_t)i * S, D.seq_id,
+                                                 VXC_PURPOSE_DRAFT, D.dtok + (size_t)i * S), vxc_count_launches(1));
     }
-    k_gather_verify<<<gb, tb, 0, st>>>(D);
+    (k_gather_verify<<<gb, tb, 0, st>>>(D), vxc_count_launches(1));
     if ((rc = vxc_forward(e->ts, D.vtok, D.slot, D.vpos, S, k + 1, D.vrows, S * (k + 1), e->vlog, st))) return rc;
     if ((rc = launch_accept(e->vlog, (long long)(k + 1) * V, V, e->dlog, V, (long long)S * V, D.dseq, S, k, V, temp,
                             seed, D.seq_id, D.apos, D.n_acc, D.next, e->acc_ws, st)))
         return rc;
-    k_commit<<<gb, tb, 0, st>>>(D);
+    (k_commit<<<gb, tb, 0, st>>>(D), vxc_count_launches(1));
     cudaError_t er = cudaGetLastError();
     if (er != cudaSuccess) { vxc_set_error("round: %s", cudaGetErrorString(er)); return -3; }
     return 0;
@@ -628,6 +628,7 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     // temp/seed are baked into the graph: rebuild it each call
     if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = NULL; }
     if (e->graph) { cudaGraphDestroy(e->graph); e->graph = NULL; }
+    const long long n_before = vxc_launch_count();
     err = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
     if (err == cudaSuccess) {
         rc = enqueue_round(e, temp, seed);
@@ -636,6 +637,9 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
         if (err == cudaSuccess) err = e2;
         if (rc) return rc;
     }
+    // captured launches are not executed; each replay below counts them
+    const long long per_round = vxc_launch_count() - n_before;
+    vxc_count_launches(-per_round);
     if (err == cudaSuccess) err = cudaGraphInstantiate(&e->exec, e->graph, 0);
     if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: graph: %s", cudaGetErrorString(err)); return -3; }
     // each round emits >= 1 token per active sequence: max_new rounds suffice
@@ -647,6 +651,7 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     while (launched < max_new + 1) {
         err = cudaGraphLaunch(e->exec, st);
         if (err != cudaSuccess) break;
+        vxc_count_launches(per_round);
         cudaEventRecord(rev[launched & 1], st);
         launched++;
         pending++;
@@ -684,5 +689,59 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     for (int i = 0; i < 4; i++) cudaEventDestroy(ev[i]);
     (void)checked;
     if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: %s", cudaGetErrorString(err)); return -3; }
+    return vxc_check_device_error(NULL);
+}
+
+// Re-runs one piece of the last round `reps` times on the engine's stream and
+// reports its average device time: which = 0 the (k+1)-row target verify
+// forward, 1 one draft step (one row per sequence), 2 the fused acceptance.
+// Positions and tokens are those of the last round, so the KV rows written
+// lie past every committed position and the committed state is unchanged.
+// *kv_bytes receives the K/V bytes that one such forward reads and writes.
+extern "C" int vxc_spec_probe(vxc_spec *e, int which, int reps, double *ms, double *kv_bytes) {
+    if (!e || reps < 1 || which < 0 || which > 2 || !ms) {
+        vxc_set_error("vxc_spec_probe: bad arguments");
+        return -4;
+    }
+    SpecDev &D = e->D;
+    const int S = D.S, k = D.k, V = e->V;
+    cudaStream_t st = e->st;
+    std::vector<int> vpos(S);
+    cudaError_t err = cudaMemcpy(vpos.data(), D.vpos, S * sizeof(int), cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) { vxc_set_error("vxc_spec_probe: %s", cudaGetErrorString(err)); return -3; }
+    vxc_net_config c;
+    vxc_net_config_get(which == 1 ? e->dnet : e->tnet, &c);
+    const double kvd = (double)c.n_kv_heads * c.n_head_dim;
+    double kvb = 0.0;
+    for (int s = 0; s < S; s++) {
+        // verify: reads positions 0..vpos+k, writes k+1; draft step: reads 0..vpos+1, writes 1
+        double rd = which == 0 ? vpos[s] + k + 1 : which == 1 ? vpos[s] + 2 : 0;
+        double wr = which == 0 ? k + 1 : which == 1 ? 1 : 0;
+        kvb += (rd + wr) * kvd * 2.0 * 4.0 * c.n_layers;
+    }
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    int rc = 0;
+    for (int it = -1; it < reps && rc == 0; it++) {   // it == -1: untimed warm-up
+        if (it == 0) cudaEventRecord(a, st);
+        if (which == 0)
+            rc = vxc_forward(e->ts, D.vtok, D.slot, D.vpos, S, k + 1, D.vrows, S * (k + 1), e->vlog, st);
+        else if (which == 1)
+            rc = vxc_forward(e->ds, D.dtok, D.slot, D.dpos, S, 1, D.slot, S, e->dlog, st);
+        else
+            rc = launch_accept(e->vlog, (long long)(k + 1) * V, V, e->dlog, V, (long long)S * V, D.dseq, S, k, V,
+                               0.8f, 1, D.seq_id, D.apos, D.n_acc, D.next, e->acc_ws, st);
+    }
+    cudaEventRecord(b, st);
+    err = cudaStreamSynchronize(st);
+    float t = 0.0f;
+    if (rc == 0 && err == cudaSuccess) cudaEventElapsedTime(&t, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    if (rc) return rc;
+    if (err != cudaSuccess) { vxc_set_error("vxc_spec_probe: %s", cudaGetErrorString(err)); return -3; }
+    *ms = t / reps;
+    if (kv_bytes) *kv_bytes = kvb;
     return vxc_check_device_error(NULL);
 }

@@ -64,6 +64,13 @@ int vx_speculative_get_stats(const vx_speculative_state *s, vx_speculative_stats
     return VX_OK;
 }
 
+int vx_speculative_probe(vx_speculative_state *s, int which, int reps, double *ms, double *kv_bytes) {
+    if (!s || !s->eng || !ms) return VX_ERR_PARAM;
+    int rc = vxc_spec_probe(s->eng, which, reps, ms, kv_bytes);
+    if (rc) fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+    return rc ? VX_ERR_PARAM : VX_OK;
+}
+
 static int ensure_engine(vx_speculative_state *s, int n_seq, int ctx) {
     ctx = (ctx + 255) & ~255;
     if (s->eng && s->eng_seqs == n_seq && s->eng_ctx >= ctx) return 0;

@@ -30,6 +30,7 @@ PROTOTYPES = {
     "vxc_qgemv": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]),
     "vxc_qgemv_simt": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]),
     "vxc_device_current": (ctypes.c_int, []),
+    "vxc_launch_count": (ctypes.c_longlong, []),
     "vxc_net_create": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_vp)]),
     "vxc_net_destroy": (None, [_vp]),
     "vxc_net_config_get": (ctypes.c_int, [_vp, _vp]),
@@ -56,6 +57,7 @@ PROTOTYPES = {
                                   ctypes.c_uint64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "vxc_spec_create": (ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
     "vxc_spec_destroy": (None, [_vp]),
+    "vxc_spec_probe": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
     "vxc_spec_generate": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                          ctypes.c_uint64, _vp, _vp, _vp]),
     # speculative.h
@@ -68,6 +70,7 @@ PROTOTYPES = {
     "vx_speculative_set_seq_id_base": (None, [_vp, ctypes.c_int]),
     "vx_speculative_generate_batch": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp]),
     "vx_speculative_get_stats": (ctypes.c_int, [_vp, _vp]),
+    "vx_speculative_probe": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, _vp]),
     # veltrix_synth.h
     "vx_synth_write_gguf": (ctypes.c_int, [ctypes.c_char_p, _vp, ctypes.c_uint64]),
 }
@@ -140,6 +143,13 @@ class Speculative:
         s = SpecStats()
         check(lib().vx_speculative_get_stats(self.h, ctypes.byref(s)), "vx_speculative_get_stats")
         return s
+
+    def probe(self, which, reps=5):
+        """(ms, kv_bytes) of one piece of the last round: 0 verify, 1 draft step, 2 acceptance."""
+        ms, kvb = ctypes.c_double(0), ctypes.c_double(0)
+        check(lib().vx_speculative_probe(self.h, which, reps, ctypes.byref(ms), ctypes.byref(kvb)),
+              "vx_speculative_probe")
+        return ms.value, kvb.value
 
     def close(self):
         if self.h:
