@@ -8,25 +8,33 @@
 // 32-term sums are exact-integer weights times fp32 activations, accumulated
 // in fp32; only the summation order differs from the reference.
 #include "vxc_common.cuh"
+#include "vxc_image.cuh"
 #include "vxc_qmat.cuh"
 #include "vxc_internal.h"
 
+#include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 
 // ---------------------------------------------------------------------------
-// Repack: GGUF blocks (row-major, one row = nblk blocks) -> tiled planes.
+// Repack: GGUF blocks (row-major, one row = nblk blocks) -> tile records
+// (layout in vxc_qmat.cuh), scales multiplied by 2^wshift.
 // ---------------------------------------------------------------------------
-__global__ void k_repack_q4_0(const uint8_t *__restrict__ src, uint8_t *__restrict__ qs,
-                              uint16_t *__restrict__ sc, int R, int nblk) {
+__device__ __forceinline__ uint16_t scaled_scale(const uint8_t *blk, float mul) {
+    const float d = vxc_h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+    return __half_as_ushort(__float2half_rn(d * mul));   // exact: mul is a power of two
+}
+
+__global__ void k_repack_q4_0(const uint8_t *__restrict__ src, uint8_t *__restrict__ qs, int R, int nblk,
+                              float mul) {
     long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     long long total = (long long)R * nblk;
     if (id >= total) return;
     int r = (int)(id / nblk), b = (int)(id % nblk);
     const uint8_t *blk = src + (size_t)id * 18;
     int tile = r / VXC_TILE_ROWS, tr = r % VXC_TILE_ROWS;
-    size_t slot = ((size_t)tile * nblk + b) * VXC_TILE_ROWS + tr;
-    sc[slot] = (uint16_t)(blk[0] | (blk[1] << 8));
+    uint8_t *rec = qs + ((size_t)tile * nblk + b) * (VXC_TILE_ROWS * 16 + 256);
+    reinterpret_cast<uint16_t *>(rec + VXC_TILE_ROWS * 16)[tr] = scaled_scale(blk, mul);
     uint32_t w[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -41,22 +49,38 @@ __global__ void k_repack_q4_0(const uint8_t *__restrict__ src, uint8_t *__restri
         }
         w[j] = v;
     }
-    *reinterpret_cast<uint4 *>(qs + slot * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4 *>(rec + tr * 16) = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__global__ void k_repack_q8_0(const uint8_t *__restrict__ src, uint8_t *__restrict__ qs,
-                              uint16_t *__restrict__ sc, int R, int nblk) {
+__global__ void k_repack_q8_0(const uint8_t *__restrict__ src, uint8_t *__restrict__ qs, int R, int nblk,
+                              float mul) {
     long long id = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     long long total = (long long)R * nblk;
     if (id >= total) return;
     int r = (int)(id / nblk), b = (int)(id % nblk);
     const uint8_t *blk = src + (size_t)id * 34;
     int tile = r / VXC_TILE_ROWS, tr = r % VXC_TILE_ROWS;
-    size_t slot = ((size_t)tile * nblk + b) * VXC_TILE_ROWS + tr;
-    sc[slot] = (uint16_t)(blk[0] | (blk[1] << 8));
-    uint8_t *dst = qs + slot * 32;
+    uint8_t *rec = qs + ((size_t)tile * nblk + b) * (VXC_TILE_ROWS * 32 + 256);
+    reinterpret_cast<uint16_t *>(rec + VXC_TILE_ROWS * 32)[tr] = scaled_scale(blk, mul);
+    uint8_t *dst = rec + tr * 32;
 #pragma unroll
     for (int j = 0; j < 32; j++) dst[j] = blk[2 + j];
+}
+
+// wshift such that max|d| * qmax * 2^wshift <= 2^14 over the whole matrix.
+static int choose_wshift(int type, const uint8_t *blocks, size_t nblocks) {
+    const size_t bs = type == 2 ? 18 : 34;
+    uint16_t mx = 0;
+    for (size_t i = 0; i < nblocks; i++) {
+        uint16_t h = (uint16_t)((blocks[i * bs] | (blocks[i * bs + 1] << 8)) & 0x7FFF);
+        if (h < 0x7C00 && h > mx) mx = h;   // finite magnitudes order like their bits
+    }
+    if (mx == 0) return 0;
+    const float maxd = __half2float(__ushort_as_half(mx));
+    int e;
+    frexpf(maxd * (type == 2 ? 8.0f : 128.0f), &e);
+    int S = 14 - e;
+    return S < -60 ? -60 : S > 60 ? 60 : S;
 }
 
 extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out) {
@@ -73,23 +97,23 @@ extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int 
     w->nblk = cols / 32;
     w->ntile = (rows + VXC_TILE_ROWS - 1) / VXC_TILE_ROWS;
     w->qb = type == 2 ? 16 : 32;
-    size_t nslot = (size_t)w->ntile * w->nblk * VXC_TILE_ROWS;
-    w->qs_bytes = nslot * w->qb;
-    w->sc_bytes = nslot * 2;
+    w->rec = VXC_TILE_ROWS * w->qb + 256;
+    w->wshift = choose_wshift(type, (const uint8_t *)host_blocks, (size_t)rows * w->nblk);
+    w->wscale = ldexpf(1.0f, -w->wshift);
+    w->qs_bytes = (size_t)w->ntile * w->nblk * w->rec;
     size_t src_bytes = (size_t)rows * w->nblk * (type == 2 ? 18 : 34);
     uint8_t *staging = NULL;
     cudaError_t e = cudaMalloc((void **)&w->qs, w->qs_bytes);
-    if (e == cudaSuccess) e = cudaMalloc((void **)&w->sc, w->sc_bytes);
     if (e == cudaSuccess) e = cudaMalloc((void **)&staging, src_bytes);
     if (e == cudaSuccess) e = cudaMemset(w->qs, 0, w->qs_bytes);
-    if (e == cudaSuccess) e = cudaMemset(w->sc, 0, w->sc_bytes);
     if (e == cudaSuccess) e = cudaMemcpy(staging, host_blocks, src_bytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) {
         long long total = (long long)rows * w->nblk;
         int th = 256;
         unsigned gb = (unsigned)((total + th - 1) / th);
-        if (type == 2) (k_repack_q4_0<<<gb, th>>>(staging, w->qs, w->sc, rows, w->nblk), vxc_count_launches(1));
-        else (k_repack_q8_0<<<gb, th>>>(staging, w->qs, w->sc, rows, w->nblk), vxc_count_launches(1));
+        const float mul = ldexpf(1.0f, w->wshift);
+        if (type == 2) (k_repack_q4_0<<<gb, th>>>(staging, w->qs, rows, w->nblk, mul), vxc_count_launches(1));
+        else (k_repack_q8_0<<<gb, th>>>(staging, w->qs, rows, w->nblk, mul), vxc_count_launches(1));
         e = cudaGetLastError();
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -106,7 +130,6 @@ extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int 
 extern "C" void vxc_qmat_destroy(vxc_qmat *w) {
     if (!w) return;
     if (w->qs) cudaFree(w->qs);
-    if (w->sc) cudaFree(w->sc);
     free(w);
 }
 
@@ -122,13 +145,17 @@ extern "C" int vxc_qmat_shape(const vxc_qmat *w, int *type, int *rows, int *cols
 // Exact CUDA-core kernel: one thread per weight row of a 128-row tile, one
 // CTA per (tile, K-slice).  The CTA stages x[m][slice] in shared memory in
 // chunks of 8 rows; each block's 32 weights are dequantised once per chunk.
+// A second implementation of the same product, kept as a cross-check of the
+// tensor-core path.
 // ---------------------------------------------------------------------------
 #define SIMT_MC 8
 
 template <int QT>
-__global__ void __launch_bounds__(128) k_qgemv_simt(const uint8_t *__restrict__ qs, const uint16_t *__restrict__ sc,
-                                                    int R, int nblk, const float *__restrict__ x, int M,
-                                                    float *__restrict__ out, int bps) {
+__global__ void __launch_bounds__(128) k_qgemv_simt(const uint8_t *__restrict__ qs, int R, int nblk, float wscale,
+                                                    const float *__restrict__ x, int M, float *__restrict__ out,
+                                                    int bps) {
+    constexpr int QB = QT == 2 ? 16 : 32;
+    constexpr int REC = VXC_TILE_ROWS * QB + 256;
     extern __shared__ float xs[];   // [SIMT_MC][bps*32]
     const int tile = blockIdx.x, s = blockIdx.y;
     const int b0 = s * bps;
@@ -151,11 +178,11 @@ __global__ void __launch_bounds__(128) k_qgemv_simt(const uint8_t *__restrict__ 
 #pragma unroll
         for (int m = 0; m < SIMT_MC; m++) acc[m] = 0.0f;
         for (int b = b0; b < b1; b++) {
-            size_t slot = ((size_t)tile * nblk + b) * VXC_TILE_ROWS + t;
-            float d = vxc_h2f(sc[slot]);
+            const uint8_t *rec = qs + ((size_t)tile * nblk + b) * REC;
+            float d = vxc_h2f(reinterpret_cast<const uint16_t *>(rec + VXC_TILE_ROWS * QB)[t]);
             float wv[32];
             if (QT == 2) {
-                uint4 q = *reinterpret_cast<const uint4 *>(qs + slot * 16);
+                uint4 q = *reinterpret_cast<const uint4 *>(rec + t * 16);
                 uint32_t wd[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
                 for (int j = 0; j < 4; j++)
@@ -165,7 +192,7 @@ __global__ void __launch_bounds__(128) k_qgemv_simt(const uint8_t *__restrict__ 
                         wv[8 * j + 2 * i + 1] = (float)((int)((wd[j] >> (16 + 4 * i)) & 0xF) - 8);
                     }
             } else {
-                const int4 *p = reinterpret_cast<const int4 *>(qs + slot * 32);
+                const int4 *p = reinterpret_cast<const int4 *>(rec + t * 32);
                 int4 q0 = p[0], q1 = p[1];
                 int wd[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
@@ -188,9 +215,32 @@ __global__ void __launch_bounds__(128) k_qgemv_simt(const uint8_t *__restrict__ 
         if (row < R) {
 #pragma unroll
             for (int m = 0; m < SIMT_MC; m++)
-                if (m < mc) dst[(size_t)(m0 + m) * R + row] = acc[m];
+                if (m < mc) dst[(size_t)(m0 + m) * R + row] = acc[m] * wscale;
         }
     }
+}
+
+// Activation image of x[M][K] (one CTA per row): xs[m] and the hi/lo chunks.
+__global__ void k_act_image(const float *__restrict__ x, int K, int N, uint8_t *__restrict__ img,
+                            float *__restrict__ xs) {
+    __shared__ float red[32];
+    const int m = blockIdx.x;
+    const float *xr = x + (size_t)m * K;
+    float mx = 0.0f;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xr[k]));
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) mx = fmaxf(mx, red[i]);
+    const float s = vxc_prescale(mx);
+    if (threadIdx.x == 0) xs[m] = s;
+    vxc_image_row(img, N, m, K, s, [&](int k) { return xr[k]; });
+}
+
+int vxc_launch_act_image(const float *x, int M, int K, uint8_t *img, float *xs, cudaStream_t st) {
+    (k_act_image<<<M, 256, 0, st>>>(x, K, vxc_img_rows(M), img, xs), vxc_count_launches(1));
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 // Deterministic split-K reduction: y[m][r] = sum_{s<ks} ws[s][m][r] in order.
@@ -239,9 +289,11 @@ extern "C" int vxc_qgemv_simt(const vxc_qmat *w, const float *x, int M, float *y
     size_t smem = (size_t)SIMT_MC * bps * 32 * sizeof(float);
     float *dst = ks > 1 ? (float *)workspace : y;
     if (w->type == 2)
-        (k_qgemv_simt<2><<<grid, 128, smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, bps), vxc_count_launches(1));
+        (k_qgemv_simt<2><<<grid, 128, smem, st>>>(w->qs, w->rows, w->nblk, w->wscale, x, M, dst, bps),
+         vxc_count_launches(1));
     else
-        (k_qgemv_simt<8><<<grid, 128, smem, st>>>(w->qs, w->sc, w->rows, w->nblk, x, M, dst, bps), vxc_count_launches(1));
+        (k_qgemv_simt<8><<<grid, 128, smem, st>>>(w->qs, w->rows, w->nblk, w->wscale, x, M, dst, bps),
+         vxc_count_launches(1));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) { vxc_set_error("vxc_qgemv_simt: %s", cudaGetErrorString(e)); return -3; }
     if (ks > 1) return vxc_launch_splitk_reduce(dst, ks, M, w->rows, y, st);

@@ -11,6 +11,22 @@ int vxc_require_device(void);
 // Per-device error word (device memory), valid after vxc_require_device().
 unsigned int *vxc_device_error_ptr(void);
 int vxc_launch_splitk_reduce(const float *ws, int ks, int M, int R, float *y, cudaStream_t st);
+// Activation image of x[M][K] (layout in vxc_qmat.cuh) and its prescales xs[M].
+int vxc_launch_act_image(const float *x, int M, int K, uint8_t *img, float *xs, cudaStream_t st);
+
+// Tensor-core GEMV plan for M <= 64 activation rows (vxc_gemv_tc.cu).
+struct VxcGemvPlan {
+    int nt;       // N / 16 (N = padded rows of the image)
+    int ks;       // K-slices; the output is ks partial sums [ks][M][R]
+    int nbs;      // 32-column blocks per slice
+    int grid;     // CTAs
+    size_t smem;  // dynamic shared memory per CTA
+};
+bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p);
+// Launches the GEMV (programmatic dependent launch) reading an activation
+// image + prescales, writing part[ks][M][R] (ks == 1: the output itself).
+int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, float *part,
+                 const VxcGemvPlan &p, cudaStream_t st);
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
 // Library-wide count of kernel launches (a CUDA-graph replay adds its kernels).
 void vxc_count_launches(long long n);

@@ -17,6 +17,8 @@
 // rotation is written with explicitly rounded ops, so it matches the
 // reference bit-for-bit.  The KV cache is fp32 ([layer][slot][pos][kv_dim]).
 #include "vxc_common.cuh"
+#include "vxc_image.cuh"
+#include "vxc_ptx.cuh"
 #include "vxc_qmat.cuh"
 #include "vxc_internal.h"
 
@@ -44,13 +46,19 @@ struct vxc_net {
     size_t weight_bytes;
 };
 
+#define VXC_MAX_CHUNKS 16   // row chunks of 64 per forward (max_rows <= 1024)
+
 struct vxc_seqs {
     const vxc_net *net;
     int n_slots, max_ctx, max_rows;
-    float *k, *v;            // [L][slots][ctx][kvd]
-    float *x, *h, *qkv, *att, *gu, *hf, *o;
-    void *gemv_ws;
-    size_t gemv_ws_bytes;
+    float *k, *v;            // [L][slot][kv head][pos][hd]
+    float *x;                // [max_rows][E] residual stream
+    float *qbuf;             // [max_rows][E] rotated queries
+    uint8_t *img;            // activation images, one 64-row chunk per img_chunk bytes
+    size_t img_chunk;
+    float *xs;               // [chunks * 64] image prescales
+    float *part;             // GEMV partial sums, one slot per chunk
+    size_t part_slot;        // floats per chunk slot
     float *attn_part;
     int attn_sl, attn_splits;
 };
@@ -63,6 +71,8 @@ struct vxc_seqs {
 // ---------------------------------------------------------------------------
 __global__ void k_embed(const uint8_t *__restrict__ embd, int type, size_t row_bytes, int vocab, int E,
                         const int *__restrict__ tokens, float *__restrict__ x, unsigned int *err) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const int tok = tokens[m];
     float *xr = x + (size_t)m * E;
@@ -105,37 +115,94 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return t;
 }
 
-// out[m] = w * (x[src] * (1/sqrt(sum(x^2)/E + 1e-5)))  (src/tensor.c:132-140)
-__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, int E,
-                          const int *__restrict__ rows, float *__restrict__ out) {
-    __shared__ float red[32];
-    const int m = blockIdx.x;
-    const int src = rows ? rows[m] : m;
-    const float *xr = x + (size_t)src * E;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < E; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
-    ss = block_sum(ss, red);
-    float rms = sqrtf(ss / (float)E + 1e-5f);
-    float *o = out + (size_t)m * E;
-    if (rms < 1e-10f) {
-        for (int i = threadIdx.x; i < E; i += blockDim.x) o[i] = 0.0f;
-        return;
+// Split-K partial sums of a GEMV output, read by its consumer.  Rows are in
+// chunks of 64 (one GEMV launch each); chunk c holds ks slices of [Mc][R] at
+// base + c * slot.  Slices are added in order, so results are deterministic.
+struct Part {
+    const float *base;
+    size_t slot;
+    int R, M, ks_full, ks_last;
+    __device__ __forceinline__ float get(int m, int r) const {
+        const int c = m >> 6, ml = m & 63;
+        const int Mc = min(64, M - (c << 6));
+        const int ks = (c == ((M - 1) >> 6)) ? ks_last : ks_full;
+        const float *p = base + c * slot + (size_t)ml * R + r;
+        float acc = p[0];
+        for (int s = 1; s < ks; s++) acc += p[(size_t)s * Mc * R];
+        return acc;
     }
-    float inv = 1.0f / rms;
-    for (int i = threadIdx.x; i < E; i += blockDim.x) o[i] = __fmul_rn(w[i], __fmul_rn(xr[i], inv));
+};
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+    v = warp_max(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = red[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) t = fmaxf(t, red[i]);
+    return t;
 }
 
-// RoPE on q (in place) and k, then k, v -> cache at the row's position.
-__global__ void k_rope_kv(float *__restrict__ qkv, int T, const int *__restrict__ d_slot,
-                          const int *__restrict__ d_pos, const float2 *__restrict__ rope, int max_pos, int H,
-                          int KH, int hd, float *__restrict__ kc, float *__restrict__ vc, int n_slots,
+// Image row m of an M-row activation (chunks of 64 rows, vxc_qmat.cuh) from
+// the K values in shared memory v[]; xs[m] = the row's prescale.
+__device__ __forceinline__ void image_from_smem(const float *v, int K, int m, int M, uint8_t *img, size_t chunk_bytes,
+                                                float *xs, float *red) {
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(v[i]));
+    mx = block_max(mx, red);
+    const float s = vxc_prescale(mx);
+    if (threadIdx.x == 0) xs[m] = s;
+    const int c = m >> 6;
+    const int N = vxc_img_rows(min(64, M - (c << 6)));
+    vxc_image_row(img + c * chunk_bytes, N, m & 63, K, s, [&](int k) { return v[k]; });
+}
+
+// Residual update and RMSNorm into the next GEMV's image:
+//   x[src] += sum of the previous GEMV's partials (when add.base != NULL)
+//   h = w * (x[src] * (1/sqrt(sum(x^2)/E + 1e-5)))        (src/tensor.c:132-140)
+// Output row m reads source row rows[m] (all rows when rows == NULL); x is
+// written back only when write_x (every row is then its own source).
+__global__ void k_norm_image(float *__restrict__ x, Part add, const float *__restrict__ w, int E,
+                             const int *__restrict__ rows, int write_x, int M_out, uint8_t *__restrict__ img,
+                             size_t chunk_bytes, float *__restrict__ xs) {
+    extern __shared__ float v[];   // [E]
+    __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.x;
+    const int src = rows ? rows[m] : m;
+    float *xr = x + (size_t)src * E;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < E; i += blockDim.x) {
+        float val = xr[i];
+        if (add.base) val = __fadd_rn(val, add.get(src, i));
+        if (write_x) xr[i] = val;
+        v[i] = val;
+        ss = fmaf(val, val, ss);
+    }
+    ss = block_sum(ss, red);
+    const float rms = sqrtf(ss / (float)E + 1e-5f);
+    const float inv = 1.0f / rms;
+    __syncthreads();
+    for (int i = threadIdx.x; i < E; i += blockDim.x) v[i] = rms < 1e-10f ? 0.0f : __fmul_rn(w[i], __fmul_rn(v[i], inv));
+    __syncthreads();
+    image_from_smem(v, E, m, M_out, img, chunk_bytes, xs, red);
+}
+
+// RoPE on q and k of row m (qkv = sum of the fused QKV GEMV's partials), q ->
+// qbuf, k, v -> the head-major cache at the row's position.
+__global__ void k_rope_kv(Part qkv, int T, const int *__restrict__ d_slot, const int *__restrict__ d_pos,
+                          const float2 *__restrict__ rope, int max_pos, int H, int KH, int hd,
+                          float *__restrict__ qbuf, float *__restrict__ kc, float *__restrict__ vc, int n_slots,
                           int max_ctx, unsigned int *err) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const int g = m / T, t = m % T;
     const int slot = d_slot[g];
     const int pos = d_pos[g] + t;
     const int E = H * hd, kvd = KH * hd;
-    float *row = qkv + (size_t)m * (E + 2 * kvd);
     if (pos < 0 || pos >= max_ctx || pos >= max_pos || slot < 0 || slot >= n_slots) {
         if (threadIdx.x == 0) vxc_flag_error(err, VXC_DERR_CTX_FULL);
         return;
@@ -145,23 +212,18 @@ __global__ void k_rope_kv(float *__restrict__ qkv, int T, const int *__restrict_
     // head-major cache: [slot][kv head][pos][hd]
     auto cache_row = [&](float *c, int kh) { return c + (((size_t)slot * KH + kh) * max_ctx + pos) * hd; };
     for (int i = threadIdx.x; i < (H + KH) * np; i += blockDim.x) {
-        int head = i / np, p = i % np;
-        float2 c = cs[p];
-        float *v = head < H ? row + (size_t)head * hd + 2 * p : row + E + (size_t)(head - H) * hd + 2 * p;
-        float a = v[0], b = v[1];
-        // a*cr - b*ci ; a*ci + b*cr with the reference's separate roundings
-        float r0 = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
-        float r1 = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
-        if (head < H) {
-            v[0] = r0;
-            v[1] = r1;
-        } else {
-            float *kdst = cache_row(kc, head - H) + 2 * p;
-            kdst[0] = r0;
-            kdst[1] = r1;
-        }
+        const int head = i / np, p = i % np;
+        const float2 c = cs[p];
+        const int col = head < H ? head * hd + 2 * p : E + (head - H) * hd + 2 * p;
+        const float a = qkv.get(m, col), b = qkv.get(m, col + 1);
+        // a*cr - b*ci ; a*ci + b*cr with the reference's separate roundings (src/tensor.c:262-266)
+        const float r0 = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+        const float r1 = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+        float *dst = head < H ? qbuf + (size_t)m * E + col : cache_row(kc, head - H) + 2 * p;
+        dst[0] = r0;
+        dst[1] = r1;
     }
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) cache_row(vc, i / hd)[i % hd] = row[E + kvd + i];
+    for (int i = threadIdx.x; i < kvd; i += blockDim.x) cache_row(vc, i / hd)[i % hd] = qkv.get(m, E + kvd + i);
 }
 
 // Decode/verify attention, split over the context (flash-decoding style).
@@ -194,7 +256,7 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qkv, int T, const int *__restrict__ d_slot,
+__global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qbuf, int T, const int *__restrict__ d_slot,
                                                     const int *__restrict__ d_pos, int H, int KH,
                                                     const float *__restrict__ kc, const float *__restrict__ vc,
                                                     int n_slots, int max_ctx, int SL, int nqc,
@@ -217,7 +279,9 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qk
     const int split = blockIdx.y, nsplit = gridDim.y;
     const int q0 = qc * ATTN_QC;
     const int nql = min(ATTN_QC, nq - q0);
-    const int E = H * HD, kvd = KH * HD;
+    const int E = H * HD;
+    pdl_trigger();
+    pdl_wait();
     const int slot = d_slot[g];
     const int base = d_pos[g];
     const int p0 = split * SL;
@@ -262,7 +326,7 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qk
     for (int e = tid; e < nql * NC; e += 128) {
         const int ql = e / NC, c = e % NC;
         const int q = q0 + ql, t = q / G, h = kvh * G + q % G;
-        qs[ql * NC + c] = reinterpret_cast<const float4 *>(qkv + (size_t)(g * T + t) * (E + 2 * kvd) + (size_t)h * HD)[c];
+        qs[ql * NC + c] = reinterpret_cast<const float4 *>(qbuf + (size_t)(g * T + t) * E + (size_t)h * HD)[c];
     }
     const float scale = 1.0f / sqrtf((float)HD);
     float4 acc[QT3];
@@ -364,49 +428,67 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qk
     }
 }
 
-// out = (sum_i e^{m_i-M} o_i) / (sum_i e^{m_i-M} l_i + 1e-10)  (vx_softmax's +1e-10, src/tensor.c:168)
-__global__ void k_attn_combine(const float *__restrict__ part, int T, int H, int KH, int hd, int nsplit,
-                               float *__restrict__ att) {
+// Merge of the attention splits for every head of row m, then the image of
+// the row for the attention-output GEMV:
+//   out = (sum_s e^{m_s-M} o_s) / (sum_s e^{m_s-M} l_s + 1e-10)   (vx_softmax's +1e-10, src/tensor.c:168)
+// One warp per head; lane s holds split s's weight e^{m_s-M}.
+__global__ void k_combine_image(const float *__restrict__ part, int T, int H, int KH, int hd, int nsplit, int M,
+                                uint8_t *__restrict__ img, size_t chunk_bytes, float *__restrict__ xs) {
+    extern __shared__ float v[];   // [H*hd]
+    __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.x;
+    const int g = m / T, t = m % T;
     const int G = H / KH, nq = T * G;
-    const int idx = blockIdx.x;             // (g, kvh, q)
-    const int q = idx % nq;
-    const int kvh = (idx / nq) % KH;
-    const int g = idx / (nq * KH);
-    const float *pp = part + (size_t)idx * nsplit * (hd + 4);
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, pp[(size_t)s * (hd + 4)]);
-    float Ls = 0.0f;
-    for (int s = 0; s < nsplit; s++) {
-        float ms = pp[(size_t)s * (hd + 4)];
-        if (ms != -INFINITY) Ls += expf(ms - M) * pp[(size_t)s * (hd + 4) + 1];
-    }
-    const float inv = 1.0f / (Ls + 1e-10f);
-    const int t = q / G, h = kvh * G + q % G;
-    float *dst = att + (size_t)(g * T + t) * (H * hd) + (size_t)h * hd;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float o = 0.0f;
-        for (int s = 0; s < nsplit; s++) {
-            float ms = pp[(size_t)s * (hd + 4)];
-            if (ms != -INFINITY) o += expf(ms - M) * pp[(size_t)s * (hd + 4) + 4 + d];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int rec = hd + 4;
+    for (int h = w; h < H; h += nw) {
+        const int kvh = h / G, q = t * G + (h % G);
+        const float *pp = part + (((size_t)g * KH + kvh) * nq + q) * nsplit * rec;
+        const float ms = lane < nsplit ? pp[(size_t)lane * rec] : -INFINITY;
+        const float Mx = warp_max(ms);
+        const float e = (ms == -INFINITY) ? 0.0f : expf(ms - Mx);
+        const float Ls = warp_sum(lane < nsplit ? e * pp[(size_t)lane * rec + 1] : 0.0f);
+        const float inv = 1.0f / (Ls + 1e-10f);
+        for (int d = lane; d < hd; d += 32) {
+            float o = 0.0f;
+            for (int s = 0; s < nsplit; s++) {
+                const float es = __shfl_sync(0xffffffffu, e, s);
+                if (es != 0.0f) o += es * pp[(size_t)s * rec + 4 + d];
+            }
+            v[h * hd + d] = o * inv;
         }
-        dst[d] = o * inv;
     }
+    __syncthreads();
+    image_from_smem(v, H * hd, m, M, img, chunk_bytes, xs, red);
 }
 
-// f = |silu(g)| < 0.01 ? 0 : silu(g) * u   (src/model.c:580-585, src/tensor.c:71-88, :277)
-__global__ void k_swiglu(const float *__restrict__ gu, int M, int F, float *__restrict__ hf) {
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (size_t)M * F) return;
-    size_t m = i / F, j = i % F;
-    float g = gu[m * 2 * F + j];
-    float u = gu[m * 2 * F + F + j];
-    float s = g / (1.0f + expf(-g));
-    hf[i] = (fabsf(s) < 0.01f) ? __fmul_rn(s, 0.0f) : __fmul_rn(s, u);
+// f = |silu(g)| < 0.01 ? 0 : silu(g) * u  (src/model.c:580-585, src/tensor.c:71-88, :277)
+// from the fused gate/up GEMV's partials, then the image for the down GEMV.
+__global__ void k_swiglu_image(Part gu, int F, int M, uint8_t *__restrict__ img, size_t chunk_bytes,
+                               float *__restrict__ xs) {
+    extern __shared__ float v[];   // [F]
+    __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.x;
+    for (int j = threadIdx.x; j < F; j += blockDim.x) {
+        const float g = gu.get(m, j), u = gu.get(m, F + j);
+        const float s = g / (1.0f + expf(-g));
+        v[j] = (fabsf(s) < 0.01f) ? __fmul_rn(s, 0.0f) : __fmul_rn(s, u);
+    }
+    __syncthreads();
+    image_from_smem(v, F, m, M, img, chunk_bytes, xs, red);
 }
 
-__global__ void k_add(float *__restrict__ x, const float *__restrict__ o, size_t n) {
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) x[i] = __fadd_rn(x[i], o[i]);
+// logits[m][r] = sum of the LM head's partials
+__global__ void k_part_out(Part p, int n_rows, float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t n = (size_t)n_rows * p.R;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = p.get((int)(i / p.R), (int)(i % p.R));
 }
 
 __global__ void k_fill(float *__restrict__ p, size_t n, float v) {
@@ -460,7 +542,7 @@ static int upload_fused(const vxc_tensor_view *const *parts, int n, vxc_qmat **o
     return vxc_qmat_create(type, src, rows, cols, out);
 }
 
-static size_t qmat_bytes(const vxc_qmat *w) { return w ? w->qs_bytes + w->sc_bytes : 0; }
+static size_t qmat_bytes(const vxc_qmat *w) { return w ? w->qs_bytes : 0; }
 
 extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
                               const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
@@ -585,18 +667,63 @@ static attn_kernel_t attn_kernel(int hd) {
     }
 }
 
+// Kernel launch with programmatic dependent launch: the kernel may start while
+// its predecessor finishes; every kernel of the forward calls
+// griddepcontrol.wait before touching data.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, ((KArgs)args)...);
+    vxc_count_launches(1);
+    return e;
+}
+
+// Largest partial-sum slot (floats) any GEMV of the net needs for a chunk of <= 64 rows.
+static size_t part_slot_floats(const vxc_net *n) {
+    size_t best = 0;
+    auto consider = [&](const vxc_qmat *w) {
+        for (int m = 1; m <= 64; m++) {
+            VxcGemvPlan p;
+            if (vxc_gemv_plan(w, m, &p)) {
+                size_t f = (size_t)p.ks * m * w->rows;
+                if (f > best) best = f;
+            }
+        }
+    };
+    for (int l = 0; l < n->cfg.n_layers; l++) {
+        consider(n->layers[l].wqkv);
+        consider(n->layers[l].wo);
+        consider(n->layers[l].wgu);
+        consider(n->layers[l].wd);
+    }
+    consider(n->out);
+    return (best + 63) & ~(size_t)63;
+}
+
 extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int max_rows, vxc_seqs **out) {
     if (!net || !out || n_slots <= 0 || max_ctx <= 0 || max_rows <= 0) { vxc_set_error("vxc_seqs_create: bad args"); return -4; }
     int rc = vxc_require_device();
     if (rc) return rc;
     const vxc_net_config &c = net->cfg;
     if (max_ctx > c.max_pos) { vxc_set_error("vxc_seqs_create: max_ctx %d > rope table %d", max_ctx, c.max_pos); return -4; }
+    if (max_rows > 64 * VXC_MAX_CHUNKS) { vxc_set_error("vxc_seqs_create: max_rows %d > %d", max_rows, 64 * VXC_MAX_CHUNKS); return -4; }
     vxc_seqs *s = (vxc_seqs *)calloc(1, sizeof(vxc_seqs));
     s->net = net;
     s->n_slots = n_slots;
     s->max_ctx = max_ctx;
     s->max_rows = max_rows;
     const int E = c.n_embd, kvd = c.n_kv_heads * c.n_head_dim, F = c.n_ff, hd = c.n_head_dim;
+    const int nch = (max_rows + 63) / 64;
     size_t kvn = (size_t)c.n_layers * n_slots * max_ctx * kvd;
     // attention split length: at most 16 splits of >= 64 positions (whole tiles)
     int SL = (max_ctx + 15) / 16;
@@ -605,40 +732,22 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     s->attn_sl = SL;
     s->attn_splits = (max_ctx + SL - 1) / SL;
     size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 4);
-    size_t ws = 0;
-    for (int l = 0; l < c.n_layers; l++) {
-        const vxc_layer_dev *d = &net->layers[l];
-        const vxc_qmat *mats[4] = {d->wqkv, d->wo, d->wgu, d->wd};
-        for (int i = 0; i < 4; i++) {
-            size_t b = vxc_qgemv_workspace_bytes(mats[i], max_rows < 64 ? max_rows : 64);
-            for (int m = 1; m <= (max_rows < 64 ? max_rows : 64); m++) {
-                size_t bm = vxc_qgemv_workspace_bytes(mats[i], m);
-                if (bm > b) b = bm;
-            }
-            if (b > ws) ws = b;
-        }
-    }
-    for (int m = 1; m <= (max_rows < 64 ? max_rows : 64); m++) {
-        size_t bm = vxc_qgemv_workspace_bytes(net->out, m);
-        if (bm > ws) ws = bm;
-    }
-    s->gemv_ws_bytes = ws;
+    s->img_chunk = (size_t)(E > F ? E : F) / 32 * vxc_img_block_bytes(64);
+    s->part_slot = part_slot_floats(net);
     cudaError_t e = cudaSuccess;
 #define ALLOC(p, n) if (e == cudaSuccess) e = cudaMalloc((void **)&(p), (n))
     ALLOC(s->k, kvn * 4);
     ALLOC(s->v, kvn * 4);
     ALLOC(s->x, (size_t)max_rows * E * 4);
-    ALLOC(s->h, (size_t)max_rows * E * 4);
-    ALLOC(s->qkv, (size_t)max_rows * (E + 2 * kvd) * 4);
-    ALLOC(s->att, (size_t)max_rows * E * 4);
-    ALLOC(s->gu, (size_t)max_rows * 2 * F * 4);
-    ALLOC(s->hf, (size_t)max_rows * F * 4);
-    ALLOC(s->o, (size_t)max_rows * E * 4);
+    ALLOC(s->qbuf, (size_t)max_rows * E * 4);
+    ALLOC(s->img, (size_t)nch * s->img_chunk);
+    ALLOC(s->xs, (size_t)nch * 64 * 4);
+    ALLOC(s->part, (size_t)nch * s->part_slot * 4);
     ALLOC(s->attn_part, part * 4);
-    if (ws) ALLOC(s->gemv_ws, ws);
 #undef ALLOC
     if (e == cudaSuccess) e = cudaMemset(s->k, 0, kvn * 4);
     if (e == cudaSuccess) e = cudaMemset(s->v, 0, kvn * 4);
+    if (e == cudaSuccess) e = cudaMemset(s->img, 0, (size_t)nch * s->img_chunk);
     if (e == cudaSuccess && !attn_kernel(hd)) {
         vxc_set_error("vxc_seqs_create: head dim %d not supported (32, 64, 96 or 128)", hd);
         vxc_seqs_destroy(s);
@@ -649,8 +758,16 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
         vxc_seqs_destroy(s);
         return -4;
     }
+    const size_t row_smem = (size_t)(E > F ? E : F) * 4;
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(attn_kernel(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(hd, SL));
+    if (e == cudaSuccess && row_smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(k_norm_image, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_combine_image, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(k_swiglu_image, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_smem);
+    }
     if (e != cudaSuccess) {
         vxc_set_error("vxc_seqs_create: %s", cudaGetErrorString(e));
         vxc_seqs_destroy(s);
@@ -662,14 +779,42 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
 
 extern "C" void vxc_seqs_destroy(vxc_seqs *s) {
     if (!s) return;
-    float *ptrs[] = {s->k, s->v, s->x, s->h, s->qkv, s->att, s->gu, s->hf, s->o, s->attn_part};
-    for (float *p : ptrs)
+    void *ptrs[] = {s->k, s->v, s->x, s->qbuf, s->img, s->xs, s->part, s->attn_part};
+    for (void *p : ptrs)
         if (p) cudaFree(p);
-    if (s->gemv_ws) cudaFree(s->gemv_ws);
     free(s);
 }
 
 static inline unsigned nblk(size_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+// GEMV over M rows in chunks of 64 (image chunks -> partial slots); returns
+// the Part view of its output.
+static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStream_t st) {
+    Part p;
+    p.base = s->part;
+    p.slot = s->part_slot;
+    p.R = w->rows;
+    p.M = M;
+    p.ks_full = p.ks_last = 1;
+    for (int c = 0; c * 64 < M; c++) {
+        const int Mc = M - c * 64 < 64 ? M - c * 64 : 64;
+        VxcGemvPlan pl;
+        if (!vxc_gemv_plan(w, Mc, &pl)) {
+            vxc_set_error("vxc_forward: no GEMV plan for %d x %d", w->rows, w->cols);
+            return -7;
+        }
+        if ((size_t)pl.ks * Mc * w->rows > s->part_slot) {
+            vxc_set_error("vxc_forward: partial slot too small");
+            return -4;
+        }
+        int rc = vxc_gemv_run(w, s->img + c * s->img_chunk, s->xs + c * 64, Mc, s->part + c * s->part_slot, pl, st);
+        if (rc) return rc;
+        if (Mc == 64) p.ks_full = pl.ks;
+        p.ks_last = pl.ks;
+    }
+    *out = p;
+    return 0;
+}
 
 extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
                            int rows_per_group, const int *d_logit_rows, int n_logit_rows, float *d_logits,
@@ -687,47 +832,67 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     const vxc_net_config &c = n->cfg;
     const int E = c.n_embd, H = c.n_heads, KH = c.n_kv_heads, hd = c.n_head_dim, F = c.n_ff;
     const int kvd = KH * hd;
+    if (n_logit_rows > 0 && !n->out_norm) {
+        vxc_set_error("vxc_forward: models without output_norm are not supported");
+        return -7;
+    }
+    if (n_logit_rows > 0 && n->out->rows != c.n_vocab) {
+        vxc_set_error("vxc_forward: LM head rows %d != vocab %d not supported", n->out->rows, c.n_vocab);
+        return -7;
+    }
     cudaStream_t st = (cudaStream_t)stream;
     unsigned int *err = vxc_device_error_ptr();
     int rc;
-    (k_embed<<<M, 256, 0, st>>>(n->embd, n->embd_type, n->embd_row_bytes, n->embd_rows, E, d_tokens, s->x, err), vxc_count_launches(1));
+    cudaError_t e = launch_pdl(k_embed, dim3(M), dim3(256), 0, st, n->embd, n->embd_type, n->embd_row_bytes,
+                               n->embd_rows, E, d_tokens, s->x, err);
     const int G = H / KH, nq = T * G, nqc = (nq + ATTN_QC - 1) / ATTN_QC;
     const size_t asm_bytes = attn_smem(hd, s->attn_sl);
-    for (int l = 0; l < c.n_layers; l++) {
+    Part prev;
+    prev.base = NULL;
+    prev.slot = 0;
+    prev.R = prev.M = prev.ks_full = prev.ks_last = 0;
+    Part pp;
+    for (int l = 0; l < c.n_layers && e == cudaSuccess; l++) {
         const vxc_layer_dev *d = &n->layers[l];
         float *kc = s->k + (size_t)l * s->n_slots * s->max_ctx * kvd;
         float *vc = s->v + (size_t)l * s->n_slots * s->max_ctx * kvd;
-        (k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->attn_norm, E, NULL, s->h), vxc_count_launches(1));
-        if ((rc = vxc_qgemv(d->wqkv, s->h, M, s->qkv, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        (k_rope_kv<<<M, 128, 0, st>>>(s->qkv, T, d_slot, d_pos, n->rope, c.max_pos, H, KH, hd, kc, vc, s->n_slots,
-                                     s->max_ctx, err), vxc_count_launches(1));
-        (attn_kernel(hd)<<<dim3(n_groups * KH * nqc, s->attn_splits), 128, asm_bytes, st>>>(
-            s->qkv, T, d_slot, d_pos, H, KH, kc, vc, s->n_slots, s->max_ctx, s->attn_sl, nqc, s->attn_part),
-         vxc_count_launches(1));
-        (k_attn_combine<<<n_groups * KH * nq, 128, 0, st>>>(s->attn_part, T, H, KH, hd, s->attn_splits, s->att), vxc_count_launches(1));
-        if ((rc = vxc_qgemv(d->wo, s->att, M, s->o, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        (k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E), vxc_count_launches(1));
-        (k_rmsnorm<<<M, 256, 0, st>>>(s->x, d->ffn_norm, E, NULL, s->h), vxc_count_launches(1));
-        if ((rc = vxc_qgemv(d->wgu, s->h, M, s->gu, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        (k_swiglu<<<nblk((size_t)M * F, 256), 256, 0, st>>>(s->gu, M, F, s->hf), vxc_count_launches(1));
-        if ((rc = vxc_qgemv(d->wd, s->hf, M, s->o, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        (k_add<<<nblk((size_t)M * E, 256), 256, 0, st>>>(s->x, s->o, (size_t)M * E), vxc_count_launches(1));
+        e = launch_pdl(k_norm_image, dim3(M), dim3(256), (size_t)E * 4, st, s->x, prev, d->attn_norm, E,
+                       (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+        if (e != cudaSuccess) break;
+        if ((rc = gemv_rows(s, d->wqkv, M, &pp, st))) return rc;
+        e = launch_pdl(k_rope_kv, dim3(M), dim3(128), 0, st, pp, T, d_slot, d_pos, (const float2 *)n->rope,
+                       c.max_pos, H, KH, hd, s->qbuf, kc, vc, s->n_slots, s->max_ctx, err);
+        if (e != cudaSuccess) break;
+        e = launch_pdl(attn_kernel(hd), dim3(n_groups * KH * nqc, s->attn_splits), dim3(128), asm_bytes, st,
+                       (const float *)s->qbuf, T, d_slot, d_pos, H, KH, (const float *)kc, (const float *)vc,
+                       s->n_slots, s->max_ctx, s->attn_sl, nqc, s->attn_part);
+        if (e != cudaSuccess) break;
+        e = launch_pdl(k_combine_image, dim3(M), dim3(512), (size_t)E * 4, st, (const float *)s->attn_part, T, H, KH,
+                       hd, s->attn_splits, M, s->img, s->img_chunk, s->xs);
+        if (e != cudaSuccess) break;
+        if ((rc = gemv_rows(s, d->wo, M, &pp, st))) return rc;
+        e = launch_pdl(k_norm_image, dim3(M), dim3(256), (size_t)E * 4, st, s->x, pp, d->ffn_norm, E,
+                       (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+        if (e != cudaSuccess) break;
+        if ((rc = gemv_rows(s, d->wgu, M, &pp, st))) return rc;
+        e = launch_pdl(k_swiglu_image, dim3(M), dim3(512), (size_t)F * 4, st, pp, F, M, s->img, s->img_chunk,
+                       s->xs);
+        if (e != cudaSuccess) break;
+        if ((rc = gemv_rows(s, d->wd, M, &prev, st))) return rc;
     }
-    if (n_logit_rows > 0) {
-        const int V = c.n_vocab, R = n->out->rows;
-        if (n->out_norm)
-            (k_rmsnorm<<<n_logit_rows, 256, 0, st>>>(s->x, n->out_norm, E, d_logit_rows, s->h), vxc_count_launches(1));
-        else
-            return vxc_set_error("vxc_forward: models without output_norm are not supported"), -7;
-        if (R < V) (k_fill<<<nblk((size_t)n_logit_rows * V, 256), 256, 0, st>>>(d_logits, (size_t)n_logit_rows * V, -1e30f), vxc_count_launches(1));
-        if (R == V) {
-            if ((rc = vxc_qgemv(n->out, s->h, n_logit_rows, d_logits, s->gemv_ws, s->gemv_ws_bytes, st))) return rc;
-        } else {
-            vxc_set_error("vxc_forward: LM head rows %d != vocab %d not supported", R, V);
-            return -7;
+    if (e == cudaSuccess && n_logit_rows > 0) {
+        const int V = c.n_vocab;
+        // last residual update fused with the final norm, for the requested rows only
+        e = launch_pdl(k_norm_image, dim3(n_logit_rows), dim3(256), (size_t)E * 4, st, s->x, prev, n->out_norm, E,
+                       d_logit_rows, 0, n_logit_rows, s->img, s->img_chunk, s->xs);
+        if (e == cudaSuccess) {
+            if ((rc = gemv_rows(s, n->out, n_logit_rows, &pp, st))) return rc;
+            const size_t tot = (size_t)n_logit_rows * V;
+            e = launch_pdl(k_part_out, dim3(nblk(tot, 256) < 1184 ? nblk(tot, 256) : 1184), dim3(256), 0, st, pp,
+                           n_logit_rows, d_logits);
         }
     }
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { vxc_set_error("vxc_forward: %s", cudaGetErrorString(e)); return -3; }
     return 0;
 }
