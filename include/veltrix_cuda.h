@@ -54,8 +54,8 @@ int vxc_qmat_create(int type, const void *host_blocks, int rows, int cols, vxc_q
 void vxc_qmat_destroy(vxc_qmat *w);
 int vxc_qmat_shape(const vxc_qmat *w, int *type, int *rows, int *cols);
 
-/* Bytes of scratch vxc_qgemv needs for M activation rows (0 when the chosen
- * split needs none). */
+/* Bytes of scratch vxc_qgemv (and vxc_qgemv_simt) needs for M activation
+ * rows: the activation image, its prescales and the split-K partial sums. */
 size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M);
 
 /* y[m][r] = sum_k W[r][k] * x[m][k] for m < M (fp32 in, fp32 out, device

@@ -455,7 +455,9 @@ extern "C" size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M) {
         size_t t = chunk_ws_bytes(w, M % 64);
         if (t > b) b = t;
     }
-    return b;
+    // the same scratch also serves vxc_qgemv_simt
+    const size_t simt = vxc_qgemv_simt_ws(w, M);
+    return b > simt ? b : simt;
 }
 
 extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, void *workspace,
