@@ -18,21 +18,30 @@
 // Work split.  Items are (128-row tile, K-slice of nbs blocks).  CTA c owns
 // slice c % ks and the tiles c / ks, c / ks + cps, ...  (cps = CTAs per
 // slice), so its slice of the activation image is fetched once (one bulk
-// copy per block) and stays in shared memory for all its tiles.  Each item
-// writes fp32 partial sums part[slice][m][row]; the consumer of the GEMV
-// output adds the ks slices in slice order (deterministic).
+// copy per block, one barrier per stage) and stays in shared memory for all
+// its tiles.  Each item writes fp32 partial sums part[slice][m][row]; the
+// consumer of the GEMV output adds the ks slices in slice order.
+//
+// MMA shape.  A tcgen05.mma of N <= 64 costs ~50 cycles of its issuing
+// thread whatever N is, so one issuer cannot keep up with HBM at these
+// sizes; several threads issuing into separate accumulators can.  The image
+// stacks [x_hi; x_lo] as 2N rows of B, so per K step two MMAs (A = w_hi, then
+// A = w_lo) give all four hi/lo products in one 2N-column accumulator; the
+// epilogue adds column m and N + m.
 //
 // Warp roles (448 threads, one CTA per SM):
-//   warp 0      producer: cp.async.bulk of GM_KB weight records per stage into
-//               a ring of RS stages (weights first: they do not depend on the
+//   warp 0      producer: cp.async.bulk of KB weight records per stage into a
+//               ring of RS stages (weights first: they do not depend on the
 //               preceding kernel), then the image slice after griddepcontrol.wait
-//   warp 1      TMEM owner; lane 0 issues the MMAs and tcgen05.commit
+//   warp 1      TMEM owner
 //   warps 2-9   two converter groups (even / odd stages): thread = weight row;
 //               raw quants -> w_hi, w_lo fp16 -> tcgen05.st into the group's
 //               TMEM A buffer (A operand read from TMEM by the MMA)
-//   warps 10-13 epilogue: tcgen05.ld of the accumulator, scale, store partials
-// TMEM: A buffers 2 x GM_KB*32 columns, accumulators 2 x N columns
-// (double-buffered across items).  No TMA multicast anywhere.
+//   warps 10-13 lane 0 of the first NI: MMA issuers, issuer i taking blocks
+//               i, i+NI, ... of the slice into its own accumulator; then all
+//               four warps run the epilogue (tcgen05.ld, sum, scale, store)
+// TMEM: A buffers 2 x KB*32 columns, NI accumulators x 2N columns.  No TMA
+// multicast anywhere.
 //
 // Every mbarrier wait is bounded (VXC_WAIT_NS); on expiry the CTA records an
 // error code, all roles stop, in-flight copies and MMAs are drained (bounded)
@@ -44,19 +53,24 @@
 
 #include <stdio.h>
 
-#define GM_KB 4
 #define GM_THREADS 448
 #define GM_SMS 148
 #define GM_SMEM_DYN (220 * 1024)
 #define GM_TMEM_COLS 512u
-#define GM_ACOL (GM_KB * 32)
+#define GM_MAXG 48          // image barriers: stages of one K-slice
 
-template <int QT>
+// Per (quant type, N/16): blocks per stage KB, MMA issuers NI and ring depth
+// RS such that TMEM holds 2 A buffers (KB*32 columns each) plus NI
+// accumulators of 2N columns, and ~55-70 KB of weights are in flight.
+template <int QT, int NT>
 struct GmCfg {
     static constexpr int QB = QT == 2 ? 16 : 32;
     static constexpr int REC = 128 * QB + 256;
-    static constexpr int STAGE = GM_KB * REC;
-    static constexpr int RS = QT == 2 ? 6 : 4;
+    static constexpr int KB = NT >= 3 ? 2 : 4;
+    static constexpr int NI = NT == 4 ? 2 : 4;
+    static constexpr int STAGE = KB * REC;
+    static constexpr int RS = (QT == 2 ? 6 : 4) * (4 / KB);
+    static_assert(2 * KB * 32 + NI * 32 * NT <= 512, "TMEM budget");
 };
 
 struct GmArgs {
@@ -101,11 +115,11 @@ __device__ __forceinline__ void deq_q8_words(uint32_t w0, uint32_t w1, __half2 *
 // ---------------------------------------------------------------------------
 template <int QT, int NT>
 __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
-    using C = GmCfg<QT>;
-    constexpr int N = 16 * NT;
-    constexpr int RS = C::RS;
+    using C = GmCfg<QT, NT>;
+    constexpr int N = 16 * NT, NP = 2 * N;   // B = [x_hi; x_lo]: NP rows
+    constexpr int KB = C::KB, RS = C::RS, NI = C::NI, ACOL = KB * 32;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[2 * RS + 10];
+    __shared__ __align__(8) uint64_t bars[2 * RS + 6 + GM_MAXG];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_flag;
     __shared__ float xinv[N];
@@ -117,9 +131,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
     const int r0 = blockIdx.x / ks;
     const int b0 = slice * a.nbs;
     const int nb = min(a.nbs, a.nblk - b0);
-    const int nst = (nb + GM_KB - 1) / GM_KB;
-    const int nitems = r0 < a.ntile ? (a.ntile - 1 - r0) / cps + 1 : 0;
-    const int total = nb > 0 ? nitems * nst : 0;
+    const int nst = (nb + KB - 1) / KB;
+    const int nitems = (r0 < a.ntile && nb > 0) ? (a.ntile - 1 - r0) / cps + 1 : 0;
+    const int total = nitems * nst;
 
     uint8_t *Bs = smem;                                   // nbs blocks x 128*N bytes
     uint8_t *Raw = Bs + (size_t)a.nbs * 128 * N;          // RS stages
@@ -129,10 +143,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
     auto raw_empty = [&](int s) { return bar0 + 8u * (RS + s); };
     auto a_full = [&](int j) { return bar0 + 8u * (2 * RS + j); };
     auto a_empty = [&](int j) { return bar0 + 8u * (2 * RS + 2 + j); };
-    auto acc_full = [&](int j) { return bar0 + 8u * (2 * RS + 4 + j); };
-    auto acc_empty = [&](int j) { return bar0 + 8u * (2 * RS + 6 + j); };
-    const uint32_t b_full = bar0 + 8u * (2 * RS + 8);
-    const uint32_t fin_bar = bar0 + 8u * (2 * RS + 9);
+    const uint32_t acc_full = bar0 + 8u * (2 * RS + 4);
+    const uint32_t fin_bar = bar0 + 8u * (2 * RS + 5);
+    auto b_full = [&](int g) { return bar0 + 8u * (2 * RS + 6 + g); };
 
     if (tid == 0) {
         for (int s = 0; s < RS; s++) {
@@ -141,12 +154,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
         }
         for (int j = 0; j < 2; j++) {
             mbar_init(a_full(j), 128);
-            mbar_init(a_empty(j), 1);
-            mbar_init(acc_full(j), 1);
-            mbar_init(acc_empty(j), 128);
+            mbar_init(a_empty(j), NI);
         }
-        mbar_init(b_full, 1);
-        mbar_init(fin_bar, 1);
+        mbar_init(acc_full, NI);
+        mbar_init(fin_bar, NI);
+        for (int g = 0; g < GM_MAXG; g++) mbar_init(b_full(g), 1);
         abort_flag = 0;
         mbar_init_fence();
     }
@@ -169,8 +181,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
                     return false;
                 const int item = qq / nst, g = qq % nst;
                 const int tile = r0 + item * cps;
-                const int kbn = min(GM_KB, nb - g * GM_KB);
-                const uint8_t *src = a.qs + ((size_t)tile * a.nblk + b0 + g * GM_KB) * C::REC;
+                const int kbn = min(KB, nb - g * KB);
+                const uint8_t *src = a.qs + ((size_t)tile * a.nblk + b0 + g * KB) * C::REC;
                 mbar_expect_tx(raw_full(s), (uint32_t)(kbn * C::REC));
                 bulk_g2s(smem_u32(Raw + (size_t)s * C::STAGE), src, (uint32_t)(kbn * C::REC), raw_full(s));
                 return true;
@@ -179,9 +191,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
             for (; q < total && q < RS; q++) issue(q);
             pdl_wait();
             if (total > 0) {
-                mbar_expect_tx(b_full, (uint32_t)(nb * 128 * N));
-                for (int b = 0; b < nb; b++)
-                    bulk_g2s(smem_u32(Bs + (size_t)b * 128 * N), a.img + (size_t)(b0 + b) * 128 * N, 128 * N, b_full);
+                // the image slice, one barrier per stage so the first MMAs need not wait for all of it
+                for (int g = 0; g < nst; g++) {
+                    const int kbn = min(KB, nb - g * KB);
+                    mbar_expect_tx(b_full(g), (uint32_t)(kbn * 128 * N));
+                    for (int kb = 0; kb < kbn; kb++) {
+                        const int b = g * KB + kb;
+                        bulk_g2s(smem_u32(Bs + (size_t)b * 128 * N), a.img + (size_t)(b0 + b) * 128 * N, 128 * N,
+                                 b_full(g));
+                    }
+                }
             }
             for (; q < total; q++)
                 if (!issue(q)) break;
@@ -191,48 +210,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
                     const uint64_t t0 = vxc_globaltimer();
                     while (!mbar_try(raw_full(qq % RS), (qq / RS) & 1) && vxc_globaltimer() - t0 < 100000000ull) {}
                 }
-                const uint64_t t0 = vxc_globaltimer();
-                while (total > 0 && !mbar_try(b_full, 0) && vxc_globaltimer() - t0 < 100000000ull) {}
-            }
-        }
-    } else if (warp == 1) {
-        // ------------------------------ MMA issuer ----------------------------
-        if (lane == 0 && total > 0) {
-            const uint32_t idesc = (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-            const uint32_t bbase = smem_u32(Bs);
-            bool ok = mbar_wait(b_full, 0, abortp, err, VXC_DERR_TIMEOUT_TMA);
-            tc_fence_after();
-            for (int q = 0; q < total && ok; q++) {
-                const int item = q / nst, g = q % nst, j = q & 1, u = q >> 1, acc = item & 1;
-                if (g == 0 && item >= 2 &&
-                    !mbar_wait(acc_empty(acc), ((item - 2) >> 1) & 1, abortp, err, VXC_DERR_TIMEOUT_MMA))
-                    break;
-                if (!mbar_wait(a_full(j), u & 1, abortp, err, VXC_DERR_TIMEOUT_MMA)) break;
-                tc_fence_after();
-                const int kbn = min(GM_KB, nb - g * GM_KB);
-                const uint32_t dcol = tmem_base + 2 * GM_ACOL + acc * N;
-                for (int kb = 0; kb < kbn; kb++) {
-                    const int bl = g * GM_KB + kb;
-#pragma unroll
-                    for (int kk = 0; kk < 2; kk++) {
-                        const uint32_t ahi = tmem_base + j * GM_ACOL + kb * 32 + kk * 8;
-                        const uint32_t alo = ahi + 16;
-                        const uint64_t bhi = sdesc(bbase + (uint32_t)((bl * 8 + 2 * kk) * N * 16), N * 16, 128);
-                        const uint64_t blo = sdesc(bbase + (uint32_t)((bl * 8 + 4 + 2 * kk) * N * 16), N * 16, 128);
-                        mma_f16_ts(dcol, ahi, bhi, idesc, (g | kb | kk) != 0 ? 1u : 0u);
-                        mma_f16_ts(dcol, ahi, blo, idesc, 1u);
-                        mma_f16_ts(dcol, alo, bhi, idesc, 1u);
-                    }
+                for (int g = 0; total > 0 && g < nst; g++) {
+                    const uint64_t t0 = vxc_globaltimer();
+                    while (!mbar_try(b_full(g), 0) && vxc_globaltimer() - t0 < 100000000ull) {}
                 }
-                mma_commit(a_empty(j));
-                if (g == nst - 1) mma_commit(acc_full(acc));
             }
-            // nothing this thread issued may still run when TMEM is freed
-            mma_commit(fin_bar);
-            const uint64_t t0 = vxc_globaltimer();
-            while (!mbar_try(fin_bar, 0) && vxc_globaltimer() - t0 < 100000000ull) {}
         }
-    } else if (warp < 10) {
+    } else if (warp >= 2 && warp < 10) {
         // ------------------------------ converters ----------------------------
         const int group = (warp - 2) >> 2;
         const int quarter = warp & 3;
@@ -241,12 +225,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
         for (int q = group; q < total; q += 2) {
             const int s = q % RS, g = q % nst, u = q >> 1;
             if (!mbar_wait_warp(raw_full(s), (q / RS) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA)) break;
-            const int kbn = min(GM_KB, nb - g * GM_KB);
+            const int kbn = min(KB, nb - g * KB);
             const uint8_t *st = Raw + (size_t)s * C::STAGE;
-            uint32_t qw[GM_KB][C::QB / 4];
-            uint32_t dh[GM_KB];
+            uint32_t qw[KB][C::QB / 4];
+            uint32_t dh[KB];
 #pragma unroll
-            for (int kb = 0; kb < GM_KB; kb++) {
+            for (int kb = 0; kb < KB; kb++) {
                 if (kb < kbn) {
                     const uint8_t *rec = st + kb * C::REC;
                     const uint4 *qp = reinterpret_cast<const uint4 *>(rec + row * C::QB);
@@ -266,7 +250,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
             if (u >= 1 && !mbar_wait_warp(a_empty(group), (u - 1) & 1, abortp, err, VXC_DERR_TIMEOUT_MMA)) break;
             tc_fence_after();
 #pragma unroll
-            for (int kb = 0; kb < GM_KB; kb++) {
+            for (int kb = 0; kb < KB; kb++) {
                 if (kb < kbn) {
                     const __half2 d2 = u2h(dh[kb]);
                     uint32_t hi[16], lo[16];
@@ -282,7 +266,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
                             lo[4 * c + i] = h2u(__hfma2(qh[i], d2, __hneg2(h)));
                         }
                     }
-                    const uint32_t col = tlane + group * GM_ACOL + kb * 32;
+                    const uint32_t col = tlane + group * ACOL + kb * 32;
                     tmem_st16(col, hi);
                     tmem_st16(col + 16, lo);
                 }
@@ -291,8 +275,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
             tc_fence_before();
             mbar_arrive(a_full(group));
         }
-    } else {
-        // ------------------------------ epilogue ------------------------------
+    } else if (warp >= 10) {
+        // ---------------- MMA issuers (lane 0 of warps 10..10+NI-1) + epilogue ----------------
+        const int ii = warp - 10;                 // issuer index / lane quarter of the epilogue
         const int quarter = warp & 3;
         const int trow = quarter * 32 + lane;
         const uint32_t tlane = tmem_base + ((uint32_t)(quarter * 32) << 16);
@@ -300,24 +285,79 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
         pdl_wait();   // xs comes from the preceding kernel; part may still be read by it
         for (int m = tid - 320; m < N; m += 128) xinv[m] = m < M ? a.wscale / a.xs[m] : 0.0f;
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        for (int item = 0; item < nitems && total > 0; item++) {
-            const int acc = item & 1;
-            if (!mbar_wait_warp(acc_full(acc), (item >> 1) & 1, abortp, err, VXC_DERR_TIMEOUT_EPI)) break;
-            tc_fence_after();
-            uint32_t v[N];
+        const uint32_t idesc = (1u << 4) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+        const uint32_t bbase = smem_u32(Bs);
+        const uint32_t dcol = tmem_base + 2 * ACOL + ii * NP;
+        bool ok = true;
+        for (int item = 0; item < nitems && ok; item++) {
+            // ---- MMAs of this item: issuer ii takes the slice's blocks b with b % NI == ii
+            if (ii < NI && lane == 0) {
+                bool first = true;
+                for (int g = 0; g < nst && ok; g++) {
+                    const int q = item * nst + g, j = q & 1, u = q >> 1;
+                    ok = mbar_wait(a_full(j), u & 1, abortp, err, VXC_DERR_TIMEOUT_MMA);
+                    if (ok && item == 0) ok = mbar_wait(b_full(g), 0, abortp, err, VXC_DERR_TIMEOUT_TMA);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const int kbn = min(KB, nb - g * KB);
+                    for (int kb = 0; kb < kbn; kb++) {
+                        const int bl = g * KB + kb;
+                        if (bl % NI != ii) continue;
 #pragma unroll
-            for (int nt = 0; nt < NT; nt++) tmem_ld16(tlane + 2 * GM_ACOL + acc * N + nt * 16, &v[nt * 16]);
-            tmem_wait_ld();
+                        for (int kk = 0; kk < 2; kk++) {
+                            const uint32_t ahi = tmem_base + j * ACOL + kb * 32 + kk * 8;
+                            const uint64_t bd = sdesc(bbase + (uint32_t)((bl * 4 + 2 * kk) * NP * 16), NP * 16, 128);
+                            mma_f16_ts(dcol, ahi, bd, idesc, first ? 0u : 1u);
+                            mma_f16_ts(dcol, ahi + 16, bd, idesc, 1u);
+                            first = false;
+                        }
+                    }
+                    mma_commit(a_empty(j));
+                }
+                if (ok) mma_commit(acc_full);
+            }
+            __syncwarp();
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            // ---- epilogue: y[m] = sum over issuers of (acc[m] + acc[N + m]) in fixed order
+            if (ok) ok = mbar_wait_warp(acc_full, item & 1, abortp, err, VXC_DERR_TIMEOUT_EPI);
+            // the four epilogue warps decide together, so the named barrier below is met by all or none
+            ok = bar_and(1, 128, ok);
+            if (!ok) break;
+            tc_fence_after();
+            float y[N];
+#pragma unroll
+            for (int m = 0; m < N; m++) y[m] = 0.0f;
+            const int nact = nb < NI ? nb : NI;   // issuer i owns blocks i, i+NI, ... of the slice
+#pragma unroll
+            for (int i = 0; i < NI; i++) {
+                if (i >= nact) break;
+#pragma unroll
+                for (int c = 0; c < NP / 16; c++) {
+                    uint32_t v[16];
+                    tmem_ld16(tlane + 2 * ACOL + i * NP + c * 16, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; e++) y[(c * 16 + e) % N] += __uint_as_float(v[e]);
+                }
+            }
             tc_fence_before();
-            mbar_arrive(acc_empty(acc));
+            // every epilogue warp has read the accumulators before the next item's MMAs overwrite them
+            asm volatile("bar.sync 1, 128;" ::: "memory");
             const int row = (r0 + item * cps) * 128 + trow;
             if (row < a.R) {
                 float *dst = a.part + (size_t)slice * M * a.R + row;
 #pragma unroll
                 for (int m = 0; m < N; m++)
-                    if (m < M) dst[(size_t)m * a.R] = __uint_as_float(v[m]) * xinv[m];
+                    if (m < M) dst[(size_t)m * a.R] = y[m] * xinv[m];
             }
         }
+        if (ii < NI && lane == 0) {
+            // nothing this thread issued may still run when TMEM is freed
+            mma_commit(fin_bar);
+            const uint64_t t0 = vxc_globaltimer();
+            while (!mbar_try(fin_bar, 0) && vxc_globaltimer() - t0 < 100000000ull) {}
+        }
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -328,18 +368,22 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static int gm_rs(int qt) { return qt == 2 ? GmCfg<2>::RS : GmCfg<8>::RS; }
-static int gm_stage(int qt) { return qt == 2 ? GmCfg<2>::STAGE : GmCfg<8>::STAGE; }
+static int gm_kb(int nt) { return nt >= 3 ? 2 : 4; }
+static int gm_stage(int qt, int nt) { return gm_kb(nt) * (128 * (qt == 2 ? 16 : 32) + 256); }
+static int gm_rs(int qt, int nt) { return (qt == 2 ? 6 : 4) * (4 / gm_kb(nt)); }
 
-static size_t gm_smem(int qt, int N, int nbs) { return (size_t)nbs * 128 * N + (size_t)gm_rs(qt) * gm_stage(qt); }
+static size_t gm_smem(int qt, int nt, int nbs) {
+    return (size_t)nbs * 128 * 16 * nt + (size_t)gm_rs(qt, nt) * gm_stage(qt, nt);
+}
 
 // Plan: pick the K-slice count minimising the busiest CTA's stages plus the
 // partial-sum traffic (served mostly from L2).
 bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p) {
     if (!w || M < 1 || M > 64) return false;
-    const int nt = (M + 15) / 16, N = 16 * nt;
-    const long avail = GM_SMEM_DYN - (long)gm_rs(w->type) * gm_stage(w->type);
-    const int nbs_max = (int)(avail / (128L * N));
+    const int nt = (M + 15) / 16, N = 16 * nt, KB = gm_kb(nt);
+    const long avail = GM_SMEM_DYN - (long)gm_rs(w->type, nt) * gm_stage(w->type, nt);
+    int nbs_max = (int)(avail / (128L * N));
+    if (nbs_max > GM_MAXG * KB) nbs_max = GM_MAXG * KB;
     if (nbs_max < 1) return false;
     double best = 1e30;
     int bks = 0, bnbs = 0, bcps = 0;
@@ -352,9 +396,9 @@ bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p) {
         if (cps > w->ntile) cps = w->ntile;
         if (cps < 1) continue;
         const int tpc = (w->ntile + cps - 1) / cps;
-        const int stages = (nbs + GM_KB - 1) / GM_KB;
-        const double part = ks > 1 ? 0.5 * ks * (double)M * w->rows * 8.0 / ((double)GM_SMS * gm_stage(w->type)) : 0.0;
-        const double cost = tpc * (stages + 0.5) + part;
+        const double blocks = (double)tpc * nbs;
+        const double part = ks > 1 ? 0.5 * ks * (double)M * w->rows * 8.0 / ((double)GM_SMS * (128 * 18)) : 0.0;
+        const double cost = blocks + tpc * 2.0 * KB + part;
         if (cost < best - 1e-9) {
             best = cost;
             bks = ks;
@@ -367,7 +411,7 @@ bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p) {
     p->ks = bks;
     p->nbs = bnbs;
     p->grid = bks * bcps;
-    p->smem = gm_smem(w->type, N, bnbs);
+    p->smem = gm_smem(w->type, nt, bnbs);
     return p->smem <= GM_SMEM_DYN;
 }
 

@@ -42,7 +42,8 @@ __device__ __forceinline__ void vxc_image_row(uint8_t *__restrict__ img, int N, 
         for (int i = 0; i < 8; i++) v[i] = val(8 * ch + i);
         uint4 hi, lo;
         vxc_hilo8(v, s, hi, lo);
-        *reinterpret_cast<uint4 *>(img + ((size_t)(b * 8 + c) * N + m) * 16) = hi;
-        *reinterpret_cast<uint4 *>(img + ((size_t)(b * 8 + 4 + c) * N + m) * 16) = lo;
+        uint8_t *chunk = img + (size_t)(b * 4 + c) * 2 * N * 16;
+        *reinterpret_cast<uint4 *>(chunk + (size_t)m * 16) = hi;
+        *reinterpret_cast<uint4 *>(chunk + (size_t)(N + m) * 16) = lo;
     }
 }

@@ -62,6 +62,21 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
     return __all_sync(0xffffffffu, ok) != 0;
 }
 
+// AND of `p` over the `count` threads that reach named barrier `id` (a
+// barrier like bar.sync, so every participant gets the same answer).
+__device__ __forceinline__ bool bar_and(int id, int count, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)(p ? 1 : 0)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 // ---- bulk copies (TMA, 1-D) --------------------------------------------------
 // Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {

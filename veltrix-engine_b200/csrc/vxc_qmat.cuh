@@ -27,10 +27,12 @@
 // activations): N rows (N = 16 * ceil(M / 16)), each row m prescaled by
 // xs[m] = 2^e (max|x[m]| * 2^e in [2^14, 2^15)) and split into fp16
 // hi = RN(x * xs) and lo = RN(x * xs - hi).  Per 32-column block b the image
-// holds 8 chunks of N x 16 bytes (chunks 0-3: hi elements 8c..8c+7, chunks
-// 4-7: lo), rows consecutive:  byte offset ((b * 8 + c) * N + m) * 16.  This
-// is the K-major, no-swizzle canonical layout of tcgen05 (8-row core
-// matrices, 16-byte rows), so a slice of blocks is one contiguous span.
+// holds 4 chunks c (elements 8c..8c+7) of 2N rows x 16 bytes: rows 0..N-1
+// the hi parts, rows N..2N-1 the lo parts:
+//   byte offset ((b * 4 + c) * 2N + n) * 16
+// This is the K-major, no-swizzle canonical layout of tcgen05 (8-row core
+// matrices, 16-byte rows) for a 2N-row B operand, so one MMA multiplies the
+// weights by both parts, and a slice of blocks is one contiguous span.
 #pragma once
 #include <stddef.h>
 #include <stdint.h>
