@@ -396,6 +396,17 @@ def run_spec7b_gpu(args, ws, rank, local):
     v_ms, v_kv = sp.probe(0, 10)
     d_ms, d_kv = sp.probe(1, 10)
     a_ms, _ = sp.probe(2, 10)
+    # stage breakdown of one verify / draft forward (events between kernels: slightly slower than v_ms)
+    stages = {}
+    names = ["embed", "attn_norm", "qkv_gemv", "rope_kv", "attention", "attn_merge", "o_gemv", "ffn_norm",
+             "gate_up_gemv", "swiglu", "down_gemv", "lm_head"]
+    for which, key in ((0, "verify"), (1, "draft_step")):
+        vxb200.lib().vxc_profile_enable(1)
+        sp.probe(which, 5)
+        buf = (ctypes.c_double * 12)()
+        vxb200.lib().vxc_profile_read(buf, 12)
+        vxb200.lib().vxc_profile_enable(0)
+        stages[key] = {nm: round(buf[i] / 6, 4) for i, nm in enumerate(names)}
     t = torch.tensor([dec_ms, pre_ms, wall_s, v_ms, d_ms, a_ms], device="cuda", dtype=torch.float64)
     n = torch.tensor([emitted, accepted, drafted, rounds, launches], device="cuda", dtype=torch.float64)
     if dist:
@@ -407,7 +418,7 @@ def run_spec7b_gpu(args, ws, rank, local):
     d2h = S * new * 4
     res = dict(emitted=emitted, accepted=accepted, drafted=drafted, rounds=rounds, dec_ms=dec_ms, pre_ms=pre_ms,
                wall_s=wall_s, v_ms=v_ms_max, v_kv=v_kv, d_ms=d_ms_max, d_kv=d_kv, a_ms=a_ms_max, clocks=clocks,
-               launches=launches, h2d=h2d, d2h=d2h, first=[int(x) for x in outs[0][:8]])
+               launches=launches, h2d=h2d, d2h=d2h, first=[int(x) for x in outs[0][:8]], stages=stages)
     sp.close()
     draft.close()
     target.close()
@@ -568,6 +579,7 @@ def main_spec7b(args, ws, rank, threads):
            "acceptance": {"rounds": r["rounds"], "drafted": r["drafted"], "accepted": r["accepted"],
                           "emitted": r["emitted"], "rate": round(r["accepted"] / max(1, r["drafted"]), 4)},
            "prefill_ms_per_step": round(r["pre_ms"] / args.steps, 2),
+           "stage_ms": r["stages"],
            "cpu_baseline": cpu,
            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": r["h2d"] * ws,
                    "d2h_bytes_per_step": r["d2h"] * ws,

@@ -41,6 +41,18 @@ int vxc_check_device_error(unsigned int *code_out);
  * holds. */
 long long vxc_launch_count(void);
 
+/* Per-stage device time of vxc_forward (measurement aid, no reference
+ * counterpart).  While enabled, every eager (not graph-captured) forward
+ * records CUDA events around its stages; vxc_profile_read synchronises,
+ * writes the summed milliseconds of stage i to ms[i] for i < n, clears the
+ * record and returns VXC_N_STAGES.  Stages: 0 embedding, 1 attention norm,
+ * 2 QKV GEMV, 3 RoPE + KV write, 4 attention, 5 attention merge, 6 output
+ * GEMV, 7 FFN norm, 8 gate/up GEMV, 9 SwiGLU, 10 down GEMV, 11 final norm +
+ * LM head. */
+#define VXC_N_STAGES 12
+void vxc_profile_enable(int on);
+int vxc_profile_read(double *ms, int n);
+
 /* ---- quantised weight matrices ------------------------------------------ */
 
 typedef struct vxc_qmat vxc_qmat;

@@ -787,6 +787,52 @@ extern "C" void vxc_seqs_destroy(vxc_seqs *s) {
 
 static inline unsigned nblk(size_t n, int t) { return (unsigned)((n + t - 1) / t); }
 
+// ---- optional per-stage device timing of vxc_forward (measurement aid) ----
+static bool g_prof = false;
+struct ProfEv {
+    int stage;
+    cudaEvent_t a, b;
+};
+static std::vector<ProfEv> g_prof_ev;
+
+// Start / end of one timed stage on `st` (no-ops unless enabled, and while
+// the stream is being captured into a graph).
+static cudaEvent_t prof_begin(cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (!g_prof || cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return NULL;
+    cudaEvent_t a = NULL;
+    if (cudaEventCreate(&a) != cudaSuccess) return NULL;
+    cudaEventRecord(a, st);
+    return a;
+}
+
+static void prof_end(int stage, cudaEvent_t a, cudaStream_t st) {
+    if (!a) return;
+    cudaEvent_t b;
+    if (cudaEventCreate(&b) != cudaSuccess) {
+        cudaEventDestroy(a);
+        return;
+    }
+    cudaEventRecord(b, st);
+    g_prof_ev.push_back({stage, a, b});
+}
+
+extern "C" void vxc_profile_enable(int on) { g_prof = on != 0; }
+
+extern "C" int vxc_profile_read(double *ms, int n) {
+    if (ms)
+        for (int i = 0; i < n; i++) ms[i] = 0.0;
+    for (const ProfEv &e : g_prof_ev) {
+        float t = 0.0f;
+        cudaEventSynchronize(e.b);
+        if (ms && e.stage < n && cudaEventElapsedTime(&t, e.a, e.b) == cudaSuccess) ms[e.stage] += t;
+        cudaEventDestroy(e.a);
+        cudaEventDestroy(e.b);
+    }
+    g_prof_ev.clear();
+    return VXC_N_STAGES;
+}
+
 // GEMV over M rows in chunks of 64 (image chunks -> partial slots); returns
 // the Part view of its output.
 static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStream_t st) {
@@ -843,8 +889,11 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     cudaStream_t st = (cudaStream_t)stream;
     unsigned int *err = vxc_device_error_ptr();
     int rc;
-    cudaError_t e = launch_pdl(k_embed, dim3(M), dim3(256), 0, st, n->embd, n->embd_type, n->embd_row_bytes,
+    cudaError_t e;
+    cudaEvent_t pe = prof_begin(st);
+    e = launch_pdl(k_embed, dim3(M), dim3(256), 0, st, n->embd, n->embd_type, n->embd_row_bytes,
                                n->embd_rows, E, d_tokens, s->x, err);
+    prof_end(0, pe, st);
     const int G = H / KH, nq = T * G, nqc = (nq + ATTN_QC - 1) / ATTN_QC;
     const size_t asm_bytes = attn_smem(hd, s->attn_sl);
     Part prev;
@@ -856,31 +905,52 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         const vxc_layer_dev *d = &n->layers[l];
         float *kc = s->k + (size_t)l * s->n_slots * s->max_ctx * kvd;
         float *vc = s->v + (size_t)l * s->n_slots * s->max_ctx * kvd;
+        pe = prof_begin(st);
         e = launch_pdl(k_norm_image, dim3(M), dim3(256), (size_t)E * 4, st, s->x, prev, d->attn_norm, E,
                        (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+        prof_end(1, pe, st);
         if (e != cudaSuccess) break;
+        pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wqkv, M, &pp, st))) return rc;
+        prof_end(2, pe, st);
+        pe = prof_begin(st);
         e = launch_pdl(k_rope_kv, dim3(M), dim3(128), 0, st, pp, T, d_slot, d_pos, (const float2 *)n->rope,
                        c.max_pos, H, KH, hd, s->qbuf, kc, vc, s->n_slots, s->max_ctx, err);
+        prof_end(3, pe, st);
         if (e != cudaSuccess) break;
+        pe = prof_begin(st);
         e = launch_pdl(attn_kernel(hd), dim3(n_groups * KH * nqc, s->attn_splits), dim3(128), asm_bytes, st,
                        (const float *)s->qbuf, T, d_slot, d_pos, H, KH, (const float *)kc, (const float *)vc,
                        s->n_slots, s->max_ctx, s->attn_sl, nqc, s->attn_part);
+        prof_end(4, pe, st);
         if (e != cudaSuccess) break;
+        pe = prof_begin(st);
         e = launch_pdl(k_combine_image, dim3(M), dim3(512), (size_t)E * 4, st, (const float *)s->attn_part, T, H, KH,
                        hd, s->attn_splits, M, s->img, s->img_chunk, s->xs);
+        prof_end(5, pe, st);
         if (e != cudaSuccess) break;
+        pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wo, M, &pp, st))) return rc;
+        prof_end(6, pe, st);
+        pe = prof_begin(st);
         e = launch_pdl(k_norm_image, dim3(M), dim3(256), (size_t)E * 4, st, s->x, pp, d->ffn_norm, E,
                        (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+        prof_end(7, pe, st);
         if (e != cudaSuccess) break;
+        pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wgu, M, &pp, st))) return rc;
+        prof_end(8, pe, st);
+        pe = prof_begin(st);
         e = launch_pdl(k_swiglu_image, dim3(M), dim3(512), (size_t)F * 4, st, pp, F, M, s->img, s->img_chunk,
                        s->xs);
+        prof_end(9, pe, st);
         if (e != cudaSuccess) break;
+        pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wd, M, &prev, st))) return rc;
+        prof_end(10, pe, st);
     }
     if (e == cudaSuccess && n_logit_rows > 0) {
+        pe = prof_begin(st);
         const int V = c.n_vocab;
         // last residual update fused with the final norm, for the requested rows only
         e = launch_pdl(k_norm_image, dim3(n_logit_rows), dim3(256), (size_t)E * 4, st, s->x, prev, n->out_norm, E,
@@ -891,6 +961,7 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
             e = launch_pdl(k_part_out, dim3(nblk(tot, 256) < 1184 ? nblk(tot, 256) : 1184), dim3(256), 0, st, pp,
                            n_logit_rows, d_logits);
         }
+        prof_end(11, pe, st);
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { vxc_set_error("vxc_forward: %s", cudaGetErrorString(e)); return -3; }

@@ -31,6 +31,8 @@ PROTOTYPES = {
     "vxc_qgemv_simt": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]),
     "vxc_device_current": (ctypes.c_int, []),
     "vxc_launch_count": (ctypes.c_longlong, []),
+    "vxc_profile_enable": (None, [ctypes.c_int]),
+    "vxc_profile_read": (ctypes.c_int, [_vp, ctypes.c_int]),
     "vxc_net_create": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_vp)]),
     "vxc_net_destroy": (None, [_vp]),
     "vxc_net_config_get": (ctypes.c_int, [_vp, _vp]),
