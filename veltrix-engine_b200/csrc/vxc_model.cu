@@ -22,6 +22,7 @@
 #include "vxc_qmat.cuh"
 #include "vxc_internal.h"
 
+#include <cooperative_groups.h>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -45,6 +46,8 @@ struct vxc_net {
     float2 *rope;            // [max_pos][hd/2]
     size_t weight_bytes;
 };
+
+namespace cg = cooperative_groups;
 
 #define VXC_MAX_CHUNKS 16   // row chunks of 64 per forward (max_rows <= 1024)
 
@@ -144,86 +147,42 @@ __device__ __forceinline__ float block_max(float v, float *red) {
     return t;
 }
 
-// Image row m of an M-row activation (chunks of 64 rows, vxc_qmat.cuh) from
-// the K values in shared memory v[]; xs[m] = the row's prescale.
-__device__ __forceinline__ void image_from_smem(const float *v, int K, int m, int M, uint8_t *img, size_t chunk_bytes,
-                                                float *xs, float *red) {
-    float mx = 0.0f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(v[i]));
-    mx = block_max(mx, red);
-    const float s = vxc_prescale(mx);
-    if (threadIdx.x == 0) xs[m] = s;
-    const int c = m >> 6;
-    const int N = vxc_img_rows(min(64, M - (c << 6)));
-    vxc_image_row(img + c * chunk_bytes, N, m & 63, K, s, [&](int k) { return v[k]; });
-}
-
-// Residual update and RMSNorm into the next GEMV's image:
-//   x[src] += sum of the previous GEMV's partials (when add.base != NULL)
-//   h = w * (x[src] * (1/sqrt(sum(x^2)/E + 1e-5)))        (src/tensor.c:132-140)
-// Output row m reads source row rows[m] (all rows when rows == NULL); x is
-// written back only when write_x (every row is then its own source).
-__global__ void k_norm_image(float *__restrict__ x, Part add, const float *__restrict__ w, int E,
-                             const int *__restrict__ rows, int write_x, int M_out, uint8_t *__restrict__ img,
-                             size_t chunk_bytes, float *__restrict__ xs) {
-    extern __shared__ float v[];   // [E]
-    __shared__ float red[32];
-    pdl_trigger();
-    pdl_wait();
-    const int m = blockIdx.x;
-    const int src = rows ? rows[m] : m;
-    float *xr = x + (size_t)src * E;
-    float ss = 0.0f;
-    for (int i = threadIdx.x; i < E; i += blockDim.x) {
-        float val = xr[i];
-        if (add.base) val = __fadd_rn(val, add.get(src, i));
-        if (write_x) xr[i] = val;
-        v[i] = val;
-        ss = fmaf(val, val, ss);
-    }
-    ss = block_sum(ss, red);
-    const float rms = sqrtf(ss / (float)E + 1e-5f);
-    const float inv = 1.0f / rms;
-    __syncthreads();
-    for (int i = threadIdx.x; i < E; i += blockDim.x) v[i] = rms < 1e-10f ? 0.0f : __fmul_rn(w[i], __fmul_rn(v[i], inv));
-    __syncthreads();
-    image_from_smem(v, E, m, M_out, img, chunk_bytes, xs, red);
-}
-
-// RoPE on q and k of row m (qkv = sum of the fused QKV GEMV's partials), q ->
-// qbuf, k, v -> the head-major cache at the row's position.
+// RoPE of one head of row m (qkv = sum of the fused QKV GEMV's partials):
+// blockIdx.x < H: q head -> qbuf; < H + KH: k head -> cache; else v head ->
+// cache (head-major [slot][kv head][pos][hd]).  Thread = one (even, odd) pair.
 __global__ void k_rope_kv(Part qkv, int T, const int *__restrict__ d_slot, const int *__restrict__ d_pos,
                           const float2 *__restrict__ rope, int max_pos, int H, int KH, int hd,
                           float *__restrict__ qbuf, float *__restrict__ kc, float *__restrict__ vc, int n_slots,
                           int max_ctx, unsigned int *err) {
     pdl_trigger();
     pdl_wait();
-    const int m = blockIdx.x;
+    const int head = blockIdx.x, m = blockIdx.y, p = threadIdx.x;
     const int g = m / T, t = m % T;
     const int slot = d_slot[g];
     const int pos = d_pos[g] + t;
     const int E = H * hd, kvd = KH * hd;
     if (pos < 0 || pos >= max_ctx || pos >= max_pos || slot < 0 || slot >= n_slots) {
-        if (threadIdx.x == 0) vxc_flag_error(err, VXC_DERR_CTX_FULL);
+        if (head == 0 && p == 0) vxc_flag_error(err, VXC_DERR_CTX_FULL);
         return;
     }
-    const int np = hd / 2;
-    const float2 *cs = rope + (size_t)pos * np;
-    // head-major cache: [slot][kv head][pos][hd]
+    if (2 * p >= hd) return;
     auto cache_row = [&](float *c, int kh) { return c + (((size_t)slot * KH + kh) * max_ctx + pos) * hd; };
-    for (int i = threadIdx.x; i < (H + KH) * np; i += blockDim.x) {
-        const int head = i / np, p = i % np;
-        const float2 c = cs[p];
-        const int col = head < H ? head * hd + 2 * p : E + (head - H) * hd + 2 * p;
-        const float a = qkv.get(m, col), b = qkv.get(m, col + 1);
-        // a*cr - b*ci ; a*ci + b*cr with the reference's separate roundings (src/tensor.c:262-266)
-        const float r0 = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
-        const float r1 = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
-        float *dst = head < H ? qbuf + (size_t)m * E + col : cache_row(kc, head - H) + 2 * p;
-        dst[0] = r0;
-        dst[1] = r1;
+    if (head >= H + KH) {
+        const int vh = head - H - KH;
+        float *dst = cache_row(vc, vh) + 2 * p;
+        dst[0] = qkv.get(m, E + kvd + vh * hd + 2 * p);
+        dst[1] = qkv.get(m, E + kvd + vh * hd + 2 * p + 1);
+        return;
     }
-    for (int i = threadIdx.x; i < kvd; i += blockDim.x) cache_row(vc, i / hd)[i % hd] = qkv.get(m, E + kvd + i);
+    const float2 c = rope[(size_t)pos * (hd / 2) + p];
+    const int col = head < H ? head * hd + 2 * p : E + (head - H) * hd + 2 * p;
+    const float a = qkv.get(m, col), b = qkv.get(m, col + 1);
+    // a*cr - b*ci ; a*ci + b*cr with the reference's separate roundings (src/tensor.c:262-266)
+    const float r0 = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
+    const float r1 = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+    float *dst = head < H ? qbuf + (size_t)m * E + col : cache_row(kc, head - H) + 2 * p;
+    dst[0] = r0;
+    dst[1] = r1;
 }
 
 // Decode/verify attention, split over the context (flash-decoding style).
@@ -428,22 +387,153 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
     }
 }
 
-// Merge of the attention splits for every head of row m, then the image of
-// the row for the attention-output GEMV:
-//   out = (sum_s e^{m_s-M} o_s) / (sum_s e^{m_s-M} l_s + 1e-10)   (vx_softmax's +1e-10, src/tensor.c:168)
-// One warp per head; lane s holds split s's weight e^{m_s-M}.
-__global__ void k_combine_image(const float *__restrict__ part, int T, int H, int KH, int hd, int nsplit, int M,
-                                uint8_t *__restrict__ img, size_t chunk_bytes, float *__restrict__ xs) {
-    extern __shared__ float v[];   // [H*hd]
-    __shared__ float red[32];
+// ---------------------------------------------------------------------------
+// Row kernels on thread-block clusters.  A row of M (40 at batch 8 x 5) is
+// far too little parallelism for one CTA per row, so each row is spread over
+// a cluster of ROW_CL CTAs, each owning a column range (multiple of 8); the
+// row-wide sum of squares and max|value| are combined through distributed
+// shared memory in fixed rank order (deterministic, identical in every CTA).
+// ---------------------------------------------------------------------------
+#define ROW_CL 8
+#define ROW_THREADS 256
+
+// Sum (op 0) or max (op 1) of one value per CTA over the cluster; `slot` is
+// this reduction's own shared word.  Ends with the values read, so the slot
+// may not be rewritten before a later cluster.sync().
+__device__ __forceinline__ float cluster_reduce(cg::cluster_group &cl, float v, float *slot, int op) {
+    if (threadIdx.x == 0) *slot = v;
+    cl.sync();
+    float t = op ? 0.0f : 0.0f;
+#pragma unroll
+    for (int r = 0; r < ROW_CL; r++) {
+        const float u = *cl.map_shared_rank(slot, r);
+        t = op ? fmaxf(t, u) : t + u;
+    }
+    return t;
+}
+
+__device__ __forceinline__ void col_range(int K, int align, int *k0, int *k1) {
+    const int c = blockIdx.x;
+    int cw = (K + ROW_CL - 1) / ROW_CL;
+    cw = (cw + align - 1) / align * align;
+    *k0 = min(K, c * cw);
+    *k1 = min(K, *k0 + cw);
+}
+
+// Image columns [k0, k1) of row m (chunks of 64 rows, vxc_qmat.cuh).
+template <class F>
+__device__ __forceinline__ void image_cols(uint8_t *img, size_t chunk_bytes, int m, int M, int k0, int k1, float s,
+                                           F val) {
+    const int c = m >> 6;
+    const int N = vxc_img_rows(min(64, M - (c << 6)));
+    uint8_t *base = img + c * chunk_bytes;
+    for (int ch = k0 / 8 + threadIdx.x; ch < k1 / 8; ch += blockDim.x) {
+        const int b = ch >> 2, cc = ch & 3;
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = val(8 * ch + i);
+        uint4 hi, lo;
+        vxc_hilo8(v, s, hi, lo);
+        uint8_t *chunk = base + (size_t)(b * 4 + cc) * 2 * N * 16;
+        *reinterpret_cast<uint4 *>(chunk + (size_t)(m & 63) * 16) = hi;
+        *reinterpret_cast<uint4 *>(chunk + (size_t)(N + (m & 63)) * 16) = lo;
+    }
+}
+
+// Residual update and RMSNorm into the next GEMV's image:
+//   x[src] += sum of the previous GEMV's partials (when add.base != NULL)
+//   h = w * (x[src] * (1/sqrt(sum(x^2)/E + 1e-5)))        (src/tensor.c:132-140)
+// Output row m (blockIdx.y) reads source row rows[m] (all rows when rows ==
+// NULL); x is written back only when write_x.
+__global__ void __launch_bounds__(ROW_THREADS) k_norm_image(float *__restrict__ x, Part add,
+                                                              const float *__restrict__ w, int E,
+                                                              const int *__restrict__ rows, int write_x, int M_out,
+                                                              uint8_t *__restrict__ img, size_t chunk_bytes,
+                                                              float *__restrict__ xs) {
+    extern __shared__ float v[];   // local columns
+    __shared__ float red[32], slots[2];
+    cg::cluster_group cl = cg::this_cluster();
     pdl_trigger();
     pdl_wait();
-    const int m = blockIdx.x;
+    const int m = blockIdx.y;
+    const int src = rows ? rows[m] : m;
+    int k0, k1;
+    col_range(E, 8, &k0, &k1);
+    float *xr = x + (size_t)src * E;
+    float ss = 0.0f;
+    for (int i = k0 + threadIdx.x; i < k1; i += blockDim.x) {
+        float val = xr[i];
+        if (add.base) val = __fadd_rn(val, add.get(src, i));
+        if (write_x) xr[i] = val;
+        v[i - k0] = val;
+        ss = fmaf(val, val, ss);
+    }
+    ss = cluster_reduce(cl, block_sum(ss, red), &slots[0], 0);
+    const float rms = sqrtf(ss / (float)E + 1e-5f);
+    const float inv = 1.0f / rms;
+    float mx = 0.0f;
+    for (int i = k0 + threadIdx.x; i < k1; i += blockDim.x) {
+        const float h = rms < 1e-10f ? 0.0f : __fmul_rn(w[i], __fmul_rn(v[i - k0], inv));
+        v[i - k0] = h;
+        mx = fmaxf(mx, fabsf(h));
+    }
+    mx = cluster_reduce(cl, block_max(mx, red), &slots[1], 1);
+    const float s = vxc_prescale(mx);
+    if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
+    __syncthreads();
+    image_cols(img, chunk_bytes, m, M_out, k0, k1, s, [&](int k) { return v[k - k0]; });
+    cl.sync();   // peers have read this CTA's slots
+}
+
+// f = |silu(g)| < 0.01 ? 0 : silu(g) * u  (src/model.c:580-585, src/tensor.c:71-88, :277)
+// from the fused gate/up GEMV's partials, then the image for the down GEMV.
+__global__ void __launch_bounds__(ROW_THREADS) k_swiglu_image(Part gu, int F, int M, uint8_t *__restrict__ img,
+                                                                size_t chunk_bytes, float *__restrict__ xs) {
+    extern __shared__ float v[];
+    __shared__ float red[32], slots[1];
+    cg::cluster_group cl = cg::this_cluster();
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.y;
+    int k0, k1;
+    col_range(F, 8, &k0, &k1);
+    float mx = 0.0f;
+    for (int j = k0 + threadIdx.x; j < k1; j += blockDim.x) {
+        const float g = gu.get(m, j), u = gu.get(m, F + j);
+        const float sl = g / (1.0f + expf(-g));
+        const float f = (fabsf(sl) < 0.01f) ? __fmul_rn(sl, 0.0f) : __fmul_rn(sl, u);
+        v[j - k0] = f;
+        mx = fmaxf(mx, fabsf(f));
+    }
+    mx = cluster_reduce(cl, block_max(mx, red), &slots[0], 1);
+    const float s = vxc_prescale(mx);
+    if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
+    __syncthreads();
+    image_cols(img, chunk_bytes, m, M, k0, k1, s, [&](int k) { return v[k - k0]; });
+    cl.sync();
+}
+
+// Merge of the attention splits for the heads of row m owned by this CTA,
+// then the image of the row for the attention-output GEMV:
+//   out = (sum_s e^{m_s-M} o_s) / (sum_s e^{m_s-M} l_s + 1e-10)   (vx_softmax's +1e-10, src/tensor.c:168)
+// One warp per head; lane s holds split s's weight e^{m_s-M}.
+__global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__restrict__ part, int T, int H, int KH,
+                                                                 int hd, int nsplit, int M, uint8_t *__restrict__ img,
+                                                                 size_t chunk_bytes, float *__restrict__ xs) {
+    extern __shared__ float v[];
+    __shared__ float red[32], slots[1];
+    cg::cluster_group cl = cg::this_cluster();
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.y;
     const int g = m / T, t = m % T;
     const int G = H / KH, nq = T * G;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int rec = hd + 4;
-    for (int h = w; h < H; h += nw) {
+    const int hpc = (H + ROW_CL - 1) / ROW_CL;
+    const int h0 = min(H, blockIdx.x * hpc), h1 = min(H, h0 + hpc);
+    float mx = 0.0f;
+    for (int h = h0 + w; h < h1; h += nw) {
         const int kvh = h / G, q = t * G + (h % G);
         const float *pp = part + (((size_t)g * KH + kvh) * nq + q) * nsplit * rec;
         const float ms = lane < nsplit ? pp[(size_t)lane * rec] : -INFINITY;
@@ -453,33 +543,21 @@ __global__ void k_combine_image(const float *__restrict__ part, int T, int H, in
         const float inv = 1.0f / (Ls + 1e-10f);
         for (int d = lane; d < hd; d += 32) {
             float o = 0.0f;
-            for (int s = 0; s < nsplit; s++) {
-                const float es = __shfl_sync(0xffffffffu, e, s);
-                if (es != 0.0f) o += es * pp[(size_t)s * rec + 4 + d];
+            for (int sp = 0; sp < nsplit; sp++) {
+                const float es = __shfl_sync(0xffffffffu, e, sp);
+                if (es != 0.0f) o += es * pp[(size_t)sp * rec + 4 + d];
             }
-            v[h * hd + d] = o * inv;
+            const float val = o * inv;
+            v[(h - h0) * hd + d] = val;
+            mx = fmaxf(mx, fabsf(val));
         }
     }
+    mx = cluster_reduce(cl, block_max(mx, red), &slots[0], 1);
+    const float s = vxc_prescale(mx);
+    if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
     __syncthreads();
-    image_from_smem(v, H * hd, m, M, img, chunk_bytes, xs, red);
-}
-
-// f = |silu(g)| < 0.01 ? 0 : silu(g) * u  (src/model.c:580-585, src/tensor.c:71-88, :277)
-// from the fused gate/up GEMV's partials, then the image for the down GEMV.
-__global__ void k_swiglu_image(Part gu, int F, int M, uint8_t *__restrict__ img, size_t chunk_bytes,
-                               float *__restrict__ xs) {
-    extern __shared__ float v[];   // [F]
-    __shared__ float red[32];
-    pdl_trigger();
-    pdl_wait();
-    const int m = blockIdx.x;
-    for (int j = threadIdx.x; j < F; j += blockDim.x) {
-        const float g = gu.get(m, j), u = gu.get(m, F + j);
-        const float s = g / (1.0f + expf(-g));
-        v[j] = (fabsf(s) < 0.01f) ? __fmul_rn(s, 0.0f) : __fmul_rn(s, u);
-    }
-    __syncthreads();
-    image_from_smem(v, F, m, M, img, chunk_bytes, xs, red);
+    image_cols(img, chunk_bytes, m, M, h0 * hd, h1 * hd, s, [&](int k) { return v[k - h0 * hd]; });
+    cl.sync();
 }
 
 // logits[m][r] = sum of the LM head's partials
@@ -688,6 +766,29 @@ static cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
     return e;
 }
 
+// Same with a cluster of `clx` CTAs along x (row kernels).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl_cluster(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                      int clx, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = clx;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, ((KArgs)args)...);
+    vxc_count_launches(1);
+    return e;
+}
+
 // Largest partial-sum slot (floats) any GEMV of the net needs for a chunk of <= 64 rows.
 static size_t part_slot_floats(const vxc_net *n) {
     size_t best = 0;
@@ -725,10 +826,10 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     const int E = c.n_embd, kvd = c.n_kv_heads * c.n_head_dim, F = c.n_ff, hd = c.n_head_dim;
     const int nch = (max_rows + 63) / 64;
     size_t kvn = (size_t)c.n_layers * n_slots * max_ctx * kvd;
-    // attention split length: at most 16 splits of >= 64 positions (whole tiles)
+    // attention split length: at most 16 splits of >= 128 positions (whole tiles)
     int SL = (max_ctx + 15) / 16;
     SL = ((SL + ATTN_T - 1) / ATTN_T) * ATTN_T;
-    if (SL < 64) SL = 64;
+    if (SL < 128) SL = 128;
     s->attn_sl = SL;
     s->attn_splits = (max_ctx + SL - 1) / SL;
     size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 4);
@@ -758,16 +859,8 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
         vxc_seqs_destroy(s);
         return -4;
     }
-    const size_t row_smem = (size_t)(E > F ? E : F) * 4;
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(attn_kernel(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(hd, SL));
-    if (e == cudaSuccess && row_smem > 48 * 1024) {
-        e = cudaFuncSetAttribute(k_norm_image, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_smem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_combine_image, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_smem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(k_swiglu_image, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)row_smem);
-    }
     if (e != cudaSuccess) {
         vxc_set_error("vxc_seqs_create: %s", cudaGetErrorString(e));
         vxc_seqs_destroy(s);
@@ -896,6 +989,12 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     prof_end(0, pe, st);
     const int G = H / KH, nq = T * G, nqc = (nq + ATTN_QC - 1) / ATTN_QC;
     const size_t asm_bytes = attn_smem(hd, s->attn_sl);
+    // local columns of a row kernel's CTA (norm: E / ROW_CL, SwiGLU: F / ROW_CL, merge: heads x hd)
+    auto cols8 = [](int K) { return ((K + ROW_CL - 1) / ROW_CL + 7) / 8 * 8; };
+    size_t row_smem = (size_t)cols8(E);
+    if ((size_t)cols8(F) > row_smem) row_smem = cols8(F);
+    if ((size_t)((H + ROW_CL - 1) / ROW_CL) * hd > row_smem) row_smem = (size_t)((H + ROW_CL - 1) / ROW_CL) * hd;
+    row_smem *= sizeof(float);
     Part prev;
     prev.base = NULL;
     prev.slot = 0;
@@ -906,15 +1005,15 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         float *kc = s->k + (size_t)l * s->n_slots * s->max_ctx * kvd;
         float *vc = s->v + (size_t)l * s->n_slots * s->max_ctx * kvd;
         pe = prof_begin(st);
-        e = launch_pdl(k_norm_image, dim3(M), dim3(256), (size_t)E * 4, st, s->x, prev, d->attn_norm, E,
-                       (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+        e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, prev,
+                               d->attn_norm, E, (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
         prof_end(1, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wqkv, M, &pp, st))) return rc;
         prof_end(2, pe, st);
         pe = prof_begin(st);
-        e = launch_pdl(k_rope_kv, dim3(M), dim3(128), 0, st, pp, T, d_slot, d_pos, (const float2 *)n->rope,
+        e = launch_pdl(k_rope_kv, dim3(H + 2 * KH, M), dim3(((hd / 2) + 31) / 32 * 32), 0, st, pp, T, d_slot, d_pos, (const float2 *)n->rope,
                        c.max_pos, H, KH, hd, s->qbuf, kc, vc, s->n_slots, s->max_ctx, err);
         prof_end(3, pe, st);
         if (e != cudaSuccess) break;
@@ -925,24 +1024,25 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         prof_end(4, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
-        e = launch_pdl(k_combine_image, dim3(M), dim3(512), (size_t)E * 4, st, (const float *)s->attn_part, T, H, KH,
-                       hd, s->attn_splits, M, s->img, s->img_chunk, s->xs);
+        e = launch_pdl_cluster(k_combine_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL,
+                               (const float *)s->attn_part, T, H, KH, hd, s->attn_splits, M, s->img, s->img_chunk,
+                               s->xs);
         prof_end(5, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wo, M, &pp, st))) return rc;
         prof_end(6, pe, st);
         pe = prof_begin(st);
-        e = launch_pdl(k_norm_image, dim3(M), dim3(256), (size_t)E * 4, st, s->x, pp, d->ffn_norm, E,
-                       (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+        e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, pp,
+                               d->ffn_norm, E, (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
         prof_end(7, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wgu, M, &pp, st))) return rc;
         prof_end(8, pe, st);
         pe = prof_begin(st);
-        e = launch_pdl(k_swiglu_image, dim3(M), dim3(512), (size_t)F * 4, st, pp, F, M, s->img, s->img_chunk,
-                       s->xs);
+        e = launch_pdl_cluster(k_swiglu_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, pp, F, M,
+                               s->img, s->img_chunk, s->xs);
         prof_end(9, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
@@ -953,8 +1053,9 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         pe = prof_begin(st);
         const int V = c.n_vocab;
         // last residual update fused with the final norm, for the requested rows only
-        e = launch_pdl(k_norm_image, dim3(n_logit_rows), dim3(256), (size_t)E * 4, st, s->x, prev, n->out_norm, E,
-                       d_logit_rows, 0, n_logit_rows, s->img, s->img_chunk, s->xs);
+        e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, n_logit_rows), dim3(ROW_THREADS), row_smem, st, ROW_CL,
+                               s->x, prev, n->out_norm, E, d_logit_rows, 0, n_logit_rows, s->img, s->img_chunk,
+                               s->xs);
         if (e == cudaSuccess) {
             if ((rc = gemv_rows(s, n->out, n_logit_rows, &pp, st))) return rc;
             const size_t tot = (size_t)n_logit_rows * V;
