@@ -543,6 +543,39 @@ static int enqueue_round(vxc_spec *e, float temp, uint64_t seed) {
     return 0;
 }
 
+// Tail of a generate call: wait for the rounds, copy the outputs and the
+// counters, fill *stats (events ev[0..2]: start, end of prompt pass, end).
+static int finish_generate(vxc_spec *e, int *out, int *counts, vxc_spec_stats *stats, cudaEvent_t *ev,
+                           int launched) {
+    SpecDev &D = e->D;
+    const int S = e->S, max_new = D.max_new;
+    cudaStream_t st = e->st;
+    cudaEventRecord(ev[2], st);
+    cudaError_t err = cudaStreamSynchronize(st);
+    if (err == cudaSuccess) {
+        std::vector<int> gen(S);
+        err = cudaMemcpy(out, D.out, (size_t)S * max_new * sizeof(int), cudaMemcpyDeviceToHost);
+        if (err == cudaSuccess) err = cudaMemcpy(gen.data(), D.gen, S * sizeof(int), cudaMemcpyDeviceToHost);
+        if (err == cudaSuccess && counts) memcpy(counts, gen.data(), S * sizeof(int));
+        if (err == cudaSuccess && stats) {
+            long long ctr[3];
+            cudaMemcpy(ctr, D.ctr, sizeof ctr, cudaMemcpyDeviceToHost);
+            float a = 0, b = 0;
+            cudaEventElapsedTime(&a, ev[0], ev[1]);
+            cudaEventElapsedTime(&b, ev[1], ev[2]);
+            stats->rounds = launched;
+            stats->drafted = ctr[0];
+            stats->accepted = ctr[1];
+            stats->emitted = ctr[2];
+            stats->prefill_ms = a;
+            stats->decode_ms = b;
+        }
+    }
+    for (int i = 0; i < 4; i++) cudaEventDestroy(ev[i]);
+    if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: %s", cudaGetErrorString(err)); return -3; }
+    return vxc_check_device_error(NULL);
+}
+
 extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *prompt_len, const int *seq_id,
                                  int n_seq, int max_new, float temp, uint64_t seed, int *out, int *counts,
                                  vxc_spec_stats *stats) {
@@ -621,9 +654,20 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     // ---- round loop: first round eager, then a captured graph ----
     int rc = enqueue_round(e, temp, seed);
     if (rc) return rc;
-    if (!e->exec || e->D.max_new != max_new) {
-        if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = NULL; }
-        if (e->graph) { cudaGraphDestroy(e->graph); e->graph = NULL; }
+    int launched = 1;
+    // VX_SPEC_EAGER=1 runs every round as plain launches (for kernel profilers,
+    // which cannot attribute work inside graph replays); results are identical.
+    static const bool eager = getenv("VX_SPEC_EAGER") != NULL && getenv("VX_SPEC_EAGER")[0] == '1';
+    if (eager) {
+        while (launched < max_new + 1 && rc == 0) {
+            err = cudaMemcpyAsync(e->h_ndone, D.n_done, sizeof(int), cudaMemcpyDeviceToHost, st);
+            if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+            if (err != cudaSuccess || *(volatile int *)e->h_ndone >= S) break;
+            rc = enqueue_round(e, temp, seed);
+            launched++;
+        }
+        if (rc) return rc;
+        return finish_generate(e, out, counts, stats, ev, launched);
     }
     // temp/seed are baked into the graph: rebuild it each call
     if (e->exec) { cudaGraphExecDestroy(e->exec); e->exec = NULL; }
@@ -643,7 +687,7 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     if (err == cudaSuccess) err = cudaGraphInstantiate(&e->exec, e->graph, 0);
     if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: graph: %s", cudaGetErrorString(err)); return -3; }
     // each round emits >= 1 token per active sequence: max_new rounds suffice
-    int launched = 1, checked = 0;
+    int checked = 0;
     cudaEvent_t rev[2];
     cudaEventCreateWithFlags(&rev[0], cudaEventDisableTiming);
     cudaEventCreateWithFlags(&rev[1], cudaEventDisableTiming);
@@ -663,33 +707,11 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
             if (*(volatile int *)e->h_ndone >= S) break;
         }
     }
-    cudaEventRecord(ev[2], st);
-    err = cudaStreamSynchronize(st);
     cudaEventDestroy(rev[0]);
     cudaEventDestroy(rev[1]);
-    if (err == cudaSuccess) {
-        std::vector<int> gen(S);
-        err = cudaMemcpy(out, D.out, (size_t)S * max_new * sizeof(int), cudaMemcpyDeviceToHost);
-        if (err == cudaSuccess) err = cudaMemcpy(gen.data(), D.gen, S * sizeof(int), cudaMemcpyDeviceToHost);
-        if (err == cudaSuccess && counts) memcpy(counts, gen.data(), S * sizeof(int));
-        if (err == cudaSuccess && stats) {
-            long long ctr[3];
-            cudaMemcpy(ctr, D.ctr, sizeof ctr, cudaMemcpyDeviceToHost);
-            float a = 0, b = 0;
-            cudaEventElapsedTime(&a, ev[0], ev[1]);
-            cudaEventElapsedTime(&b, ev[1], ev[2]);
-            stats->rounds = launched;
-            stats->drafted = ctr[0];
-            stats->accepted = ctr[1];
-            stats->emitted = ctr[2];
-            stats->prefill_ms = a;
-            stats->decode_ms = b;
-        }
-    }
-    for (int i = 0; i < 4; i++) cudaEventDestroy(ev[i]);
     (void)checked;
     if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: %s", cudaGetErrorString(err)); return -3; }
-    return vxc_check_device_error(NULL);
+    return finish_generate(e, out, counts, stats, ev, launched);
 }
 
 // Re-runs one piece of the last round `reps` times on the engine's stream and
