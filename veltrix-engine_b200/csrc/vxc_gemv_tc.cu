@@ -59,18 +59,19 @@
 #define GM_TMEM_COLS 512u
 #define GM_MAXG 48          // image barriers: stages of one K-slice
 
-// Per (quant type, N/16): blocks per stage KB, MMA issuers NI and ring depth
-// RS such that TMEM holds 2 A buffers (KB*32 columns each) plus NI
-// accumulators of 2N columns, and ~55-70 KB of weights are in flight.
+// Per (quant type, N/16): blocks per stage KB, MMA issuers per converter
+// group IG and ring depth RS, such that TMEM holds the two groups' A buffers
+// (KB*32 columns each) plus 2*IG accumulators of 2N columns, and ~55-70 KB of
+// weights are in flight.
 template <int QT, int NT>
 struct GmCfg {
     static constexpr int QB = QT == 2 ? 16 : 32;
     static constexpr int REC = 128 * QB + 256;
     static constexpr int KB = NT >= 3 ? 2 : 4;
-    static constexpr int NI = NT == 4 ? 2 : 4;
+    static constexpr int IG = NT == 1 ? 4 : NT == 4 ? 1 : 2;
     static constexpr int STAGE = KB * REC;
     static constexpr int RS = (QT == 2 ? 6 : 4) * (4 / KB);
-    static_assert(2 * KB * 32 + NI * 32 * NT <= 512, "TMEM budget");
+    static_assert(2 * KB * 32 + 2 * IG * 32 * NT <= 512, "TMEM budget");
 };
 
 struct GmArgs {
@@ -117,7 +118,7 @@ template <int QT, int NT>
 __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
     using C = GmCfg<QT, NT>;
     constexpr int N = 16 * NT, NP = 2 * N;   // B = [x_hi; x_lo]: NP rows
-    constexpr int KB = C::KB, RS = C::RS, NI = C::NI, ACOL = KB * 32;
+    constexpr int KB = C::KB, RS = C::RS, IG = C::IG, ACOL = KB * 32, NACC = 2 * IG;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[2 * RS + 6 + GM_MAXG];
     __shared__ uint32_t tmem_slot;
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
     const int nst = (nb + KB - 1) / KB;
     const int nitems = (r0 < a.ntile && nb > 0) ? (a.ntile - 1 - r0) / cps + 1 : 0;
     const int total = nitems * nst;
+    const int ngroups = nst >= 2 ? 2 : 1;      // converter groups with stages in every item
 
     uint8_t *Bs = smem;                                   // nbs blocks x 128*N bytes
     uint8_t *Raw = Bs + (size_t)a.nbs * 128 * N;          // RS stages
@@ -141,10 +143,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
     const uint32_t bar0 = smem_u32(bars);
     auto raw_full = [&](int s) { return bar0 + 8u * s; };
     auto raw_empty = [&](int s) { return bar0 + 8u * (RS + s); };
-    auto a_full = [&](int j) { return bar0 + 8u * (2 * RS + j); };
-    auto a_empty = [&](int j) { return bar0 + 8u * (2 * RS + 2 + j); };
-    const uint32_t acc_full = bar0 + 8u * (2 * RS + 4);
-    const uint32_t fin_bar = bar0 + 8u * (2 * RS + 5);
+    auto a_empty = [&](int j) { return bar0 + 8u * (2 * RS + j); };
+    const uint32_t acc_full = bar0 + 8u * (2 * RS + 2);
+    const uint32_t acc_empty = bar0 + 8u * (2 * RS + 3);
+    const uint32_t fin_bar = bar0 + 8u * (2 * RS + 4);
     auto b_full = [&](int g) { return bar0 + 8u * (2 * RS + 6 + g); };
 
     if (tid == 0) {
@@ -152,12 +154,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
             mbar_init(raw_full(s), 1);
             mbar_init(raw_empty(s), 128);
         }
-        for (int j = 0; j < 2; j++) {
-            mbar_init(a_full(j), 128);
-            mbar_init(a_empty(j), NI);
-        }
-        mbar_init(acc_full, NI);
-        mbar_init(fin_bar, NI);
+        for (int j = 0; j < 2; j++) mbar_init(a_empty(j), IG);
+        mbar_init(acc_full, IG * ngroups);
+        mbar_init(acc_empty, 128);
+        mbar_init(fin_bar, NACC);
         for (int g = 0; g < GM_MAXG; g++) mbar_init(b_full(g), 1);
         abort_flag = 0;
         mbar_init_fence();
@@ -217,132 +217,150 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
             }
         }
     } else if (warp >= 2 && warp < 10) {
-        // ------------------------------ converters ----------------------------
+        // ----------------- converters + MMA issue (lane 0 of the first IG warps of a group) -----------------
         const int group = (warp - 2) >> 2;
+        const int kw = (warp - 2) & 3;            // warp within the group
         const int quarter = warp & 3;
         const int row = quarter * 32 + lane;
         const uint32_t tlane = tmem_base + ((uint32_t)(quarter * 32) << 16);
-        for (int q = group; q < total; q += 2) {
-            const int s = q % RS, g = q % nst, u = q >> 1;
-            if (!mbar_wait_warp(raw_full(s), (q / RS) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA)) break;
-            const int kbn = min(KB, nb - g * KB);
-            const uint8_t *st = Raw + (size_t)s * C::STAGE;
-            uint32_t qw[KB][C::QB / 4];
-            uint32_t dh[KB];
+        const bool issuer = kw < IG && lane == 0;
+        const uint32_t idesc = (1u << 4) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+        const uint32_t bbase = smem_u32(Bs);
+        const uint32_t dcol = tmem_base + 2 * ACOL + (group * IG + kw) * NP;
+        const int per_item = (nst - group + 1) / 2;   // this group's stages per item
+        bool ok = true;
+        for (int item = 0; item < nitems && ok; item++) {
+            for (int gl = group; gl < nst; gl += 2) {
+                const int q = item * nst + gl, s = q % RS;
+                const int u = item * per_item + (gl >> 1);   // use count of this group's A buffer
+                const int kbn = min(KB, nb - gl * KB);
+                bool w_ok = mbar_wait_warp(raw_full(s), (q / RS) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA);
+                uint32_t qw[KB][C::QB / 4];
+                uint32_t dh[KB];
+                if (w_ok) {
+                    const uint8_t *st = Raw + (size_t)s * C::STAGE;
 #pragma unroll
-            for (int kb = 0; kb < KB; kb++) {
-                if (kb < kbn) {
-                    const uint8_t *rec = st + kb * C::REC;
-                    const uint4 *qp = reinterpret_cast<const uint4 *>(rec + row * C::QB);
+                    for (int kb = 0; kb < KB; kb++) {
+                        if (kb < kbn) {
+                            const uint8_t *rec = st + kb * C::REC;
+                            const uint4 *qp = reinterpret_cast<const uint4 *>(rec + row * C::QB);
 #pragma unroll
-                    for (int v = 0; v < C::QB / 16; v++) {
-                        const uint4 w4 = qp[v];
-                        qw[kb][4 * v] = w4.x;
-                        qw[kb][4 * v + 1] = w4.y;
-                        qw[kb][4 * v + 2] = w4.z;
-                        qw[kb][4 * v + 3] = w4.w;
-                    }
-                    const uint32_t h = reinterpret_cast<const uint16_t *>(rec + 128 * C::QB)[row];
-                    dh[kb] = h | (h << 16);
-                }
-            }
-            mbar_arrive(raw_empty(s));
-            if (u >= 1 && !mbar_wait_warp(a_empty(group), (u - 1) & 1, abortp, err, VXC_DERR_TIMEOUT_MMA)) break;
-            tc_fence_after();
-#pragma unroll
-            for (int kb = 0; kb < KB; kb++) {
-                if (kb < kbn) {
-                    const __half2 d2 = u2h(dh[kb]);
-                    uint32_t hi[16], lo[16];
-#pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        __half2 qh[4];
-                        if (QT == 2) deq_q4_word(qw[kb][c], qh);
-                        else deq_q8_words(qw[kb][2 * c], qw[kb][2 * c + 1], qh);
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const __half2 h = __hmul2(qh[i], d2);
-                            hi[4 * c + i] = h2u(h);
-                            lo[4 * c + i] = h2u(__hfma2(qh[i], d2, __hneg2(h)));
+                            for (int v = 0; v < C::QB / 16; v++) {
+                                const uint4 w4 = qp[v];
+                                qw[kb][4 * v] = w4.x;
+                                qw[kb][4 * v + 1] = w4.y;
+                                qw[kb][4 * v + 2] = w4.z;
+                                qw[kb][4 * v + 3] = w4.w;
+                            }
+                            const uint32_t h = reinterpret_cast<const uint16_t *>(rec + 128 * C::QB)[row];
+                            dh[kb] = h | (h << 16);
                         }
                     }
-                    const uint32_t col = tlane + group * ACOL + kb * 32;
-                    tmem_st16(col, hi);
-                    tmem_st16(col + 16, lo);
+                    mbar_arrive(raw_empty(s));
                 }
+                // the MMAs of this group's previous stage have finished reading its A buffer
+                if (w_ok && u >= 1) w_ok = mbar_wait_warp(a_empty(group), (u - 1) & 1, abortp, err, VXC_DERR_TIMEOUT_MMA);
+                if (w_ok) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int kb = 0; kb < KB; kb++) {
+                        if (kb < kbn) {
+                            const __half2 d2 = u2h(dh[kb]);
+                            uint32_t hi[16], lo[16];
+#pragma unroll
+                            for (int c = 0; c < 4; c++) {
+                                __half2 qh[4];
+                                if (QT == 2) deq_q4_word(qw[kb][c], qh);
+                                else deq_q8_words(qw[kb][2 * c], qw[kb][2 * c + 1], qh);
+#pragma unroll
+                                for (int i = 0; i < 4; i++) {
+                                    const __half2 h = __hmul2(qh[i], d2);
+                                    hi[4 * c + i] = h2u(h);
+                                    lo[4 * c + i] = h2u(__hfma2(qh[i], d2, __hneg2(h)));
+                                }
+                            }
+                            const uint32_t col = tlane + group * ACOL + kb * 32;
+                            tmem_st16(col, hi);
+                            tmem_st16(col + 16, lo);
+                        }
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                }
+                // all four warps of the group have written their quarter of the A buffer (or
+                // all stop together: the decision is the same in every warp of the group)
+                ok = bar_and(2 + group, 128, w_ok && !*abortp);
+                if (!ok) break;
+                if (issuer) {
+                    tc_fence_after();
+                    bool iok = true;
+                    // the accumulators were zeroed by the epilogue of the previous item
+                    if (gl == group) iok = mbar_wait(acc_empty, item & 1, abortp, err, VXC_DERR_TIMEOUT_MMA);
+                    if (iok && item == 0) iok = mbar_wait(b_full(gl), 0, abortp, err, VXC_DERR_TIMEOUT_TMA);
+                    if (iok) {
+                        tc_fence_after();
+                        for (int kb = kw; kb < kbn; kb += IG) {
+                            const int bl = gl * KB + kb;
+#pragma unroll
+                            for (int kk = 0; kk < 2; kk++) {
+                                const uint32_t ahi = tmem_base + group * ACOL + kb * 32 + kk * 8;
+                                const uint64_t bd =
+                                    sdesc(bbase + (uint32_t)((bl * 4 + 2 * kk) * NP * 16), NP * 16, 128);
+                                mma_f16_ts(dcol, ahi, bd, idesc, 1u);
+                                mma_f16_ts(dcol, ahi + 16, bd, idesc, 1u);
+                            }
+                        }
+                    }
+                    mma_commit(a_empty(group));
+                    if (gl + 2 >= nst) mma_commit(acc_full);   // this group's last stage of the item
+                }
+                __syncwarp();
             }
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(a_full(group));
+        }
+        if (issuer) {
+            // nothing this thread issued may still run when TMEM is freed
+            mma_commit(fin_bar);
+            const uint64_t t0 = vxc_globaltimer();
+            while (!mbar_try(fin_bar, 0) && vxc_globaltimer() - t0 < 100000000ull) {}
         }
     } else if (warp >= 10) {
-        // ---------------- MMA issuers (lane 0 of warps 10..10+NI-1) + epilogue ----------------
-        const int ii = warp - 10;                 // issuer index / lane quarter of the epilogue
+        // ------------------------------ epilogue ------------------------------
         const int quarter = warp & 3;
         const int trow = quarter * 32 + lane;
         const uint32_t tlane = tmem_base + ((uint32_t)(quarter * 32) << 16);
         const int M = a.M;
+        uint32_t zero[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) zero[i] = 0u;
+        // zero the accumulators (the MMAs always accumulate), then hand them to the issuers
+#pragma unroll
+        for (int c = 0; c < NACC * NP / 16; c++) tmem_st16(tlane + 2 * ACOL + c * 16, zero);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(acc_empty);
         pdl_wait();   // xs comes from the preceding kernel; part may still be read by it
         for (int m = tid - 320; m < N; m += 128) xinv[m] = m < M ? a.wscale / a.xs[m] : 0.0f;
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        const uint32_t idesc = (1u << 4) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-        const uint32_t bbase = smem_u32(Bs);
-        const uint32_t dcol = tmem_base + 2 * ACOL + ii * NP;
-        bool ok = true;
-        for (int item = 0; item < nitems && ok; item++) {
-            // ---- MMAs of this item: issuer ii takes the slice's blocks b with b % NI == ii
-            if (ii < NI && lane == 0) {
-                bool first = true;
-                for (int g = 0; g < nst && ok; g++) {
-                    const int q = item * nst + g, j = q & 1, u = q >> 1;
-                    ok = mbar_wait(a_full(j), u & 1, abortp, err, VXC_DERR_TIMEOUT_MMA);
-                    if (ok && item == 0) ok = mbar_wait(b_full(g), 0, abortp, err, VXC_DERR_TIMEOUT_TMA);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const int kbn = min(KB, nb - g * KB);
-                    for (int kb = 0; kb < kbn; kb++) {
-                        const int bl = g * KB + kb;
-                        if (bl % NI != ii) continue;
-#pragma unroll
-                        for (int kk = 0; kk < 2; kk++) {
-                            const uint32_t ahi = tmem_base + j * ACOL + kb * 32 + kk * 8;
-                            const uint64_t bd = sdesc(bbase + (uint32_t)((bl * 4 + 2 * kk) * NP * 16), NP * 16, 128);
-                            mma_f16_ts(dcol, ahi, bd, idesc, first ? 0u : 1u);
-                            mma_f16_ts(dcol, ahi + 16, bd, idesc, 1u);
-                            first = false;
-                        }
-                    }
-                    mma_commit(a_empty(j));
-                }
-                if (ok) mma_commit(acc_full);
-            }
-            __syncwarp();
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            // ---- epilogue: y[m] = sum over issuers of (acc[m] + acc[N + m]) in fixed order
-            if (ok) ok = mbar_wait_warp(acc_full, item & 1, abortp, err, VXC_DERR_TIMEOUT_EPI);
-            // the four epilogue warps decide together, so the named barrier below is met by all or none
-            ok = bar_and(1, 128, ok);
+        for (int item = 0; item < nitems; item++) {
+            bool ok = mbar_wait_warp(acc_full, item & 1, abortp, err, VXC_DERR_TIMEOUT_EPI);
             if (!ok) break;
             tc_fence_after();
+            // y[m] = sum over accumulators of (acc[m] + acc[N + m]), fixed order
             float y[N];
 #pragma unroll
             for (int m = 0; m < N; m++) y[m] = 0.0f;
-            const int nact = nb < NI ? nb : NI;   // issuer i owns blocks i, i+NI, ... of the slice
 #pragma unroll
-            for (int i = 0; i < NI; i++) {
-                if (i >= nact) break;
+            for (int c = 0; c < NACC * NP / 16; c++) {
+                uint32_t v[16];
+                tmem_ld16(tlane + 2 * ACOL + c * 16, v);
+                tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < NP / 16; c++) {
-                    uint32_t v[16];
-                    tmem_ld16(tlane + 2 * ACOL + i * NP + c * 16, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 16; e++) y[(c * 16 + e) % N] += __uint_as_float(v[e]);
-                }
+                for (int e = 0; e < 16; e++) y[(c * 16 + e) % N] += __uint_as_float(v[e]);
+                tmem_st16(tlane + 2 * ACOL + c * 16, zero);
             }
+            tmem_wait_st();
             tc_fence_before();
-            // every epilogue warp has read the accumulators before the next item's MMAs overwrite them
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            mbar_arrive(acc_empty);
             const int row = (r0 + item * cps) * 128 + trow;
             if (row < a.R) {
                 float *dst = a.part + (size_t)slice * M * a.R + row;
@@ -351,13 +369,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
                     if (m < M) dst[(size_t)m * a.R] = y[m] * xinv[m];
             }
         }
-        if (ii < NI && lane == 0) {
-            // nothing this thread issued may still run when TMEM is freed
-            mma_commit(fin_bar);
-            const uint64_t t0 = vxc_globaltimer();
-            while (!mbar_try(fin_bar, 0) && vxc_globaltimer() - t0 < 100000000ull) {}
-        }
-        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
