@@ -11,7 +11,7 @@
  * (out-of-place attn_o GEMV, reference src/model.c:543-544), plus the
  * corrected speculative-sampling procedure ("O-spec") whose uniforms come
  * from Philox4x32-10.  Each function cites the reference lines it follows.
- * Parity pin: tests/test_oracle_vs_ref.py checks the forward restatement
+ * Parity pin: tests/test_oracle_pin.py checks the forward restatement
  * bit-for-bit against the reference sources compiled by oracle/Makefile.
  */
 #ifndef VXO_H
