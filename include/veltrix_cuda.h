@@ -85,6 +85,19 @@ int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, void *workspac
 int vxc_qgemv_simt(const vxc_qmat *w, const float *x, int M, float *y, void *workspace,
                    size_t workspace_bytes, void *stream);
 
+/* vxc_qgemv without a caller-provided workspace, for callers that cannot
+ * allocate device memory (a host application that owns the device memory
+ * budget and forbids libraries to call cudaMalloc, or latency-bound code that
+ * cannot afford cudaMalloc's device synchronisation).  No reference
+ * counterpart.  The scratch is a static device array of
+ * VXC_QGEMV_NOALLOC_BYTES (8 MiB) held by every GPU that loads the library;
+ * shapes whose vxc_qgemv_workspace_bytes exceeds it are rejected (-4, see
+ * vxc_error_string).  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  Calls share the array: calls that overlap on the GPU race. */
+#define VXC_QGEMV_NOALLOC_BYTES (8u << 20)
+int vxc_qgemv_noalloc(const vxc_qmat *w, const float *x, int M, float *y, void *stream);
+
 /* ---- device model ---------------------------------------------------------- */
 
 /* A host tensor in GGUF layout: type 0 = F32, 2 = Q4_0, 8 = Q8_0; `rows` x

@@ -4,6 +4,8 @@ import sys
 import pytest
 
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+# the package binding (veltrix-engine_b200/vxb200.py), for tests run on their own
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "veltrix-engine_b200"))
 
 
 def pytest_configure(config):

@@ -540,3 +540,50 @@ extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, voi
     }
     return 0;
 }
+
+// ---------------------------------------------------------------------------
+// vxc_qgemv_noalloc: vxc_qgemv for callers that cannot allocate device
+// memory — for instance a host application that owns the whole device
+// memory budget and forbids libraries to call cudaMalloc, or a latency-bound
+// caller that cannot afford cudaMalloc's implicit device synchronisation.
+// The scratch (activation image, prescales and split-K partial sums) lives in
+// one static device array of VXC_QGEMV_NOALLOC_BYTES, which every GPU that
+// loads this library holds until the process exits.  Nothing in it has to
+// start at zero: every byte a call reads was written earlier by the same
+// call.  All calls on a device share the array, so calls whose GPU work
+// overlaps (different streams without ordering between them) race on it.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_qgemv_scratch[VXC_QGEMV_NOALLOC_BYTES];
+
+static void *g_qgemv_scratch_ptr[64];   // device address of g_qgemv_scratch, per device
+
+extern "C" int vxc_qgemv_noalloc(const vxc_qmat *w, const float *x, int M, float *y, void *stream) {
+    if (!w || !x || !y || M <= 0) {
+        vxc_set_error("vxc_qgemv_noalloc: bad arguments");
+        return -4;
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        vxc_set_error("vxc_qgemv_noalloc: no current CUDA device");
+        return -7;
+    }
+    const size_t need = vxc_qgemv_workspace_bytes(w, M);
+    if (need > VXC_QGEMV_NOALLOC_BYTES) {
+        vxc_set_error("vxc_qgemv_noalloc: %d x %d with %d rows needs %zu bytes of scratch; the static limit is %zu",
+                      w->rows, w->cols, M, need, (size_t)VXC_QGEMV_NOALLOC_BYTES);
+        return -4;
+    }
+    if (!g_qgemv_scratch_ptr[dev]) {
+        // set-up, once per device, with that device current: the host-side
+        // name of the array is not a device address
+        void *p = NULL;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_qgemv_scratch);
+        if (e != cudaSuccess || !p) {
+            vxc_set_error("vxc_qgemv_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+            return -3;
+        }
+        g_qgemv_scratch_ptr[dev] = p;
+    }
+    return vxc_qgemv(w, x, M, y, g_qgemv_scratch_ptr[dev], VXC_QGEMV_NOALLOC_BYTES, stream);
+}
