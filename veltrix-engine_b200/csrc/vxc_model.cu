@@ -68,6 +68,9 @@ struct vxc_seqs {
 
 #define ATTN_QC 16      // queries per attention CTA
 #define ATTN_T 32       // key positions per smem tile
+#ifndef ATTN_SL_MIN
+#define ATTN_SL_MIN 64  // shortest context split
+#endif
 
 // ---------------------------------------------------------------------------
 // kernels
@@ -201,7 +204,9 @@ __global__ void k_rope_kv(Part qkv, int T, const int *__restrict__ d_slot, const
 // Per query the CTA writes its split's record [m, l, -, -, o[hd]] (16-byte
 // aligned): max m, sum l of exp(s - m) and o = sum exp(s - m) v;
 // k_attn_combine merges the splits.
-#define ATTN_NS 4
+#ifndef ATTN_NS
+#define ATTN_NS 2
+#endif
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
@@ -221,6 +226,9 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
                                                     int n_slots, int max_ctx, int SL, int nqc,
                                                     float *__restrict__ part) {
     constexpr int NC = HD / 4;                  // float4 chunks per row
+    constexpr int QPW = 32 / NC;                // query slots per warp in P.V
+    constexpr int QT1 = ATTN_QC / 4;            // queries per thread in the score pass
+    constexpr int QT3 = (ATTN_QC + 4 * QPW - 1) / (4 * QPW);   // ... in the P.V pass
     static_assert(HD % 32 == 0 && HD <= 128, "head dim");
     extern __shared__ __align__(16) float sm[];
     float4 *ring = reinterpret_cast<float4 *>(sm);                 // [NS][T][NC]
@@ -285,17 +293,10 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
         qs[ql * NC + c] = reinterpret_cast<const float4 *>(qbuf + (size_t)(g * T + t) * E + (size_t)h * HD)[c];
     }
     const float scale = 1.0f / sqrtf((float)HD);
-    // score pass: warp w takes positions 8w..8w+7 of each tile; lane = (position
-    // pl, dim quarter qd); quarter qd owns chunks qd, qd+4, ... and the four
-    // partial dots of a position meet by two shuffles.
-    const int pl = lane >> 2, qd = lane & 3;
-    // P.V pass: warp w takes the same positions; lane = (group gp, chunk cc) with
-    // LG = 32/NC groups splitting the warp's 8 positions.
-    constexpr int LG = (32 / NC) >= 1 ? (32 / NC) : 1;
-    const int cc = lane % NC, gp = lane / NC;
-    float2 acc[ATTN_QC][2];
+    float4 acc[QT3];
 #pragma unroll
-    for (int j = 0; j < ATTN_QC; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
+    for (int j = 0; j < QT3; j++) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int qslot = lane / NC, cc = lane % NC;
     for (int i = 0; i < 2 * ntile; i++) {
         issue(i + ATTN_NS - 1);
         cp_async_wait<ATTN_NS - 1>();
@@ -309,8 +310,8 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
                 mx = warp_max(mx);
                 float su = 0.0f;
                 for (int p = lane; p < npos; p += 32) {
-                    const float sv = row[p];
-                    const float e = (sv == -INFINITY) ? 0.0f : expf(sv - mx);
+                    const float s = row[p];
+                    const float e = (s == -INFINITY) ? 0.0f : expf(s - mx);
                     row[p] = e;
                     su += e;
                 }
@@ -321,54 +322,55 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
         }
         const float4 *tile = ring + (i % ATTN_NS) * ATTN_T * NC;
         if (i < ntile) {
-            const int t0 = i * ATTN_T, p = 8 * w + pl;
-            const bool valid = t0 + p < npos;
-            float2 a2[ATTN_QC];
+            // scores: lane = position p of the tile
+            const int t0 = i * ATTN_T, p = lane;
+            const int pos = p0 + t0 + p;
+            float a[QT1];
 #pragma unroll
-            for (int j = 0; j < ATTN_QC; j++) a2[j] = make_float2(0.f, 0.f);
-            if (valid) {
+            for (int j = 0; j < QT1; j++) a[j] = 0.0f;
+            if (t0 + p < npos) {
                 const float4 *krow = tile + p * NC;
-#pragma unroll
-                for (int jj = 0; jj < NC / 4; jj++) {
-                    const int c = 4 * jj + qd;
+#pragma unroll 4
+                for (int c = 0; c < NC; c++) {
                     const float4 kv = krow[c ^ (p & 7)];
 #pragma unroll
-                    for (int ql = 0; ql < ATTN_QC; ql++) {
+                    for (int j = 0; j < QT1; j++) {
+                        const int ql = w + 4 * j;
                         if (ql < nql) {
                             const float4 qv = qs[ql * NC + c];
-                            a2[ql] = __ffma2_rn(make_float2(qv.x, qv.y), make_float2(kv.x, kv.y), a2[ql]);
-                            a2[ql] = __ffma2_rn(make_float2(qv.z, qv.w), make_float2(kv.z, kv.w), a2[ql]);
+                            float s = a[j];
+                            s = fmaf(qv.x, kv.x, s);
+                            s = fmaf(qv.y, kv.y, s);
+                            s = fmaf(qv.z, kv.z, s);
+                            s = fmaf(qv.w, kv.w, s);
+                            a[j] = s;
                         }
                     }
                 }
-            }
 #pragma unroll
-            for (int ql = 0; ql < ATTN_QC; ql++) {
-                if (ql < nql) {
-                    float sv = a2[ql].x + a2[ql].y;
-                    sv += __shfl_xor_sync(0xffffffffu, sv, 1);
-                    sv += __shfl_xor_sync(0xffffffffu, sv, 2);
-                    if (valid && qd == (ql & 3)) {
+                for (int j = 0; j < QT1; j++) {
+                    const int ql = w + 4 * j;
+                    if (ql < nql) {
                         const int tq = (q0 + ql) / G;
-                        sc[ql * SLP + t0 + p] = (p0 + t0 + p <= base + tq) ? sv * scale : -INFINITY;
+                        sc[ql * SLP + t0 + p] = (pos <= base + tq) ? a[j] * scale : -INFINITY;
                     }
                 }
             }
-        } else if (gp < LG) {
+        } else if (qslot < QPW) {
+            // P.V: lane = (query slot, output chunk cc)
             const int t0 = (i - ntile) * ATTN_T;
             const int nt = min(ATTN_T, npos - t0);
-            for (int pp = gp; pp < 8; pp += LG) {
-                const int p = 8 * w + pp;
-                if (p >= nt) break;
+            for (int p = 0; p < nt; p++) {
                 const float4 vv = tile[p * NC + (cc ^ (p & 7))];
-                const float2 v01 = make_float2(vv.x, vv.y), v23 = make_float2(vv.z, vv.w);
 #pragma unroll
-                for (int ql = 0; ql < ATTN_QC; ql++) {
+                for (int j = 0; j < QT3; j++) {
+                    const int ql = (w * QPW + qslot) + j * 4 * QPW;
                     if (ql < nql) {
                         const float e = sc[ql * SLP + t0 + p];
-                        const float2 e2 = make_float2(e, e);
-                        acc[ql][0] = __ffma2_rn(e2, v01, acc[ql][0]);
-                        acc[ql][1] = __ffma2_rn(e2, v23, acc[ql][1]);
+                        acc[j].x = fmaf(e, vv.x, acc[j].x);
+                        acc[j].y = fmaf(e, vv.y, acc[j].y);
+                        acc[j].z = fmaf(e, vv.z, acc[j].z);
+                        acc[j].w = fmaf(e, vv.w, acc[j].w);
                     }
                 }
             }
@@ -376,41 +378,12 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
         __syncthreads();
     }
     cp_async_wait<0>();
-    // combine the lane groups, then the four warps (through the idle ring), in fixed order
+    if (qslot < QPW) {
 #pragma unroll
-    for (int o = NC; LG > 1 && o < 32; o <<= 1) {
-#pragma unroll
-        for (int ql = 0; ql < ATTN_QC; ql++) {
-            if (ql < nql) {
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    acc[ql][h].x += __shfl_xor_sync(0xffffffffu, acc[ql][h].x, o);
-                    acc[ql][h].y += __shfl_xor_sync(0xffffffffu, acc[ql][h].y, o);
-                }
-            }
+        for (int j = 0; j < QT3; j++) {
+            const int ql = (w * QPW + qslot) + j * 4 * QPW;
+            if (ql < nql) reinterpret_cast<float4 *>(part_ptr(q0 + ql) + 4)[cc] = acc[j];
         }
-    }
-    float4 *red = ring;   // [4 warps][QC][NC]
-    if (gp == 0 && lane < NC) {
-#pragma unroll
-        for (int ql = 0; ql < ATTN_QC; ql++)
-            if (ql < nql)
-                red[(w * ATTN_QC + ql) * NC + cc] =
-                    make_float4(acc[ql][0].x, acc[ql][0].y, acc[ql][1].x, acc[ql][1].y);
-    }
-    __syncthreads();
-    for (int e = tid; e < nql * NC; e += 128) {
-        const int ql = e / NC, c = e % NC;
-        float4 o = red[ql * NC + c];
-#pragma unroll
-        for (int ww = 1; ww < 4; ww++) {
-            const float4 r = red[(ww * ATTN_QC + ql) * NC + c];
-            o.x += r.x;
-            o.y += r.y;
-            o.z += r.z;
-            o.w += r.w;
-        }
-        reinterpret_cast<float4 *>(part_ptr(q0 + ql) + 4)[c] = o;
     }
     if (tid < nql) {
         float *pp = part_ptr(q0 + tid);
@@ -858,10 +831,12 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     const int E = c.n_embd, kvd = c.n_kv_heads * c.n_head_dim, F = c.n_ff, hd = c.n_head_dim;
     const int nch = (max_rows + 63) / 64;
     size_t kvn = (size_t)c.n_layers * n_slots * max_ctx * kvd;
-    // attention split length: at most 16 splits of >= 128 positions (whole tiles)
+    // attention split length: at most 16 splits of >= ATTN_SL_MIN positions (whole
+    // tiles).  Short splits and a 2-stage ring keep ~5 CTAs per SM resident, which
+    // measured faster on B200 than deeper rings (the kernel is latency-bound per CTA).
     int SL = (max_ctx + 15) / 16;
     SL = ((SL + ATTN_T - 1) / ATTN_T) * ATTN_T;
-    if (SL < 128) SL = 128;
+    if (SL < ATTN_SL_MIN) SL = ATTN_SL_MIN;
     s->attn_sl = SL;
     s->attn_splits = (max_ctx + SL - 1) / SL;
     size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 4);
