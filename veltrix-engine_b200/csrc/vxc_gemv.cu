@@ -9,6 +9,7 @@
 // in fp32; only the summation order differs from the reference.
 #include "vxc_common.cuh"
 #include "vxc_image.cuh"
+#include "vxc_ptx.cuh"
 #include "vxc_qmat.cuh"
 #include "vxc_internal.h"
 
@@ -224,6 +225,8 @@ __global__ void __launch_bounds__(128) k_qgemv_simt(const uint8_t *__restrict__ 
 __global__ void k_act_image(const float *__restrict__ x, int K, int N, uint8_t *__restrict__ img,
                             float *__restrict__ xs) {
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const float *xr = x + (size_t)m * K;
     float mx = 0.0f;
@@ -238,13 +241,33 @@ __global__ void k_act_image(const float *__restrict__ x, int K, int N, uint8_t *
     vxc_image_row(img, N, m, K, s, [&](int k) { return xr[k]; });
 }
 
+// Launch with programmatic dependent launch: the kernel may start while its
+// predecessor drains; both kernels here call griddepcontrol.wait before
+// touching memory.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*k)(KArgs...), unsigned grid, unsigned block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, ((KArgs)args)...);
+    vxc_count_launches(1);
+    return e;
+}
+
 int vxc_launch_act_image(const float *x, int M, int K, uint8_t *img, float *xs, cudaStream_t st) {
-    (k_act_image<<<M, 256, 0, st>>>(x, K, vxc_img_rows(M), img, xs), vxc_count_launches(1));
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_pdl(k_act_image, (unsigned)M, 256, st, x, K, vxc_img_rows(M), img, xs) == cudaSuccess ? 0 : -3;
 }
 
 // Deterministic split-K reduction: y[m][r] = sum_{s<ks} ws[s][m][r] in order.
 __global__ void k_splitk_reduce(const float *__restrict__ ws, int ks, int MR, float *__restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= MR) return;
     float acc = ws[i];
@@ -254,8 +277,7 @@ __global__ void k_splitk_reduce(const float *__restrict__ ws, int ks, int MR, fl
 
 int vxc_launch_splitk_reduce(const float *ws, int ks, int M, int R, float *y, cudaStream_t st) {
     int MR = M * R;
-    (k_splitk_reduce<<<(MR + 255) / 256, 256, 0, st>>>(ws, ks, MR, y), vxc_count_launches(1));
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_pdl(k_splitk_reduce, (unsigned)((MR + 255) / 256), 256, st, ws, ks, MR, y) == cudaSuccess ? 0 : -3;
 }
 
 static void simt_split(const vxc_qmat *w, int *ks, int *bps) {

@@ -407,9 +407,14 @@ bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p) {
         if (cps > w->ntile) cps = w->ntile;
         if (cps < 1) continue;
         const int tpc = (w->ntile + cps - 1) / cps;
+        // in units of one Q4_0 block-record time per SM: the busiest CTA's weight
+        // blocks, its pipeline fill per item, and the L2 traffic of the partial
+        // sums (written + read) and of the image slices (read by every CTA of a slice)
+        const double unit = (double)GM_SMS * (128 * 18);
         const double blocks = (double)tpc * nbs;
-        const double part = ks > 1 ? 0.5 * ks * (double)M * w->rows * 8.0 / ((double)GM_SMS * (128 * 18)) : 0.0;
-        const double cost = blocks + tpc * 2.0 * KB + part;
+        const double part = ks > 1 ? 0.5 * ks * (double)M * w->rows * 8.0 / unit : 0.0;
+        const double image = 0.3 * (double)ks * cps * nbs * 128.0 * N / unit;
+        const double cost = blocks + tpc * 2.0 * KB + part + image;
         if (cost < best - 1e-9) {
             best = cost;
             bks = ks;
