@@ -63,14 +63,20 @@
 // group IG and ring depth RS, such that TMEM holds the two groups' A buffers
 // (KB*32 columns each) plus 2*IG accumulators of 2N columns, and ~55-70 KB of
 // weights are in flight.
+#ifndef GM_KB_SMALL_N
+#define GM_KB_SMALL_N 4     // blocks per stage for N <= 32
+#endif
+#ifndef GM_RING_BLOCKS
+#define GM_RING_BLOCKS 24   // Q4_0 blocks in flight per CTA (Q8_0: two thirds)
+#endif
 template <int QT, int NT>
 struct GmCfg {
     static constexpr int QB = QT == 2 ? 16 : 32;
     static constexpr int REC = 128 * QB + 256;
-    static constexpr int KB = NT >= 3 ? 2 : 4;
-    static constexpr int IG = NT == 1 ? 4 : NT == 4 ? 1 : 2;
+    static constexpr int KB = NT >= 3 ? 2 : GM_KB_SMALL_N;
+    static constexpr int IG = NT == 1 ? (KB == 4 ? 4 : 2) : NT == 4 ? 1 : 2;
     static constexpr int STAGE = KB * REC;
-    static constexpr int RS = (QT == 2 ? 6 : 4) * (4 / KB);
+    static constexpr int RS = (QT == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / KB;
     static_assert(2 * KB * 32 + 2 * IG * 32 * NT <= 512, "TMEM budget");
 };
 
@@ -118,7 +124,8 @@ template <int QT, int NT>
 __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
     using C = GmCfg<QT, NT>;
     constexpr int N = 16 * NT, NP = 2 * N;   // B = [x_hi; x_lo]: NP rows
-    constexpr int KB = C::KB, RS = C::RS, IG = C::IG, ACOL = KB * 32, NACC = 2 * IG;
+    constexpr int KB = C::KB, RS = C::RS, IG = C::IG, ACOL = KB * 32, NACC = 2 * IG, RSG = RS / 2;
+    static_assert(RS % 2 == 0 && RS >= 2, "ring: two equal halves, one per converter group");
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t bars[2 * RS + 6 + GM_MAXG];
     __shared__ uint32_t tmem_slot;
@@ -174,21 +181,38 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
         if (lane == 0) {
+            // each converter group has its own RS/2 ring slots, used in order, so a
+            // group never waits on a slot phase that the other group still owns
             int q = 0;
+            int last_phase[RS];
+            for (int i = 0; i < RS; i++) last_phase[i] = -1;
+            auto slot_of = [&](int qq, int &slot, int &phase) {
+                const int item = qq / nst, gl = qq % nst, g = gl & 1;
+                const int u = item * ((nst - g + 1) / 2) + (gl >> 1);
+                slot = g * RSG + u % RSG;
+                phase = u / RSG;
+            };
             auto issue = [&](int qq) -> bool {
-                const int s = qq % RS;
-                if (qq >= RS && !mbar_wait(raw_empty(s), ((qq / RS) - 1) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA))
+                int sl, ph;
+                slot_of(qq, sl, ph);
+                if (ph >= 1 && !mbar_wait(raw_empty(sl), (ph - 1) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA))
                     return false;
                 const int item = qq / nst, g = qq % nst;
                 const int tile = r0 + item * cps;
                 const int kbn = min(KB, nb - g * KB);
                 const uint8_t *src = a.qs + ((size_t)tile * a.nblk + b0 + g * KB) * C::REC;
-                mbar_expect_tx(raw_full(s), (uint32_t)(kbn * C::REC));
-                bulk_g2s(smem_u32(Raw + (size_t)s * C::STAGE), src, (uint32_t)(kbn * C::REC), raw_full(s));
+                mbar_expect_tx(raw_full(sl), (uint32_t)(kbn * C::REC));
+                bulk_g2s(smem_u32(Raw + (size_t)sl * C::STAGE), src, (uint32_t)(kbn * C::REC), raw_full(sl));
+                last_phase[sl] = ph;
                 return true;
             };
-            // weights do not depend on the preceding kernel: start streaming now
-            for (; q < total && q < RS; q++) issue(q);
+            // weights do not depend on the preceding kernel: fill the free slots now
+            for (; q < total; q++) {
+                int sl, ph;
+                slot_of(q, sl, ph);
+                if (ph >= 1) break;
+                issue(q);
+            }
             pdl_wait();
             if (total > 0) {
                 // the image slice, one barrier per stage so the first MMAs need not wait for all of it
@@ -206,9 +230,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
                 if (!issue(q)) break;
             if (*abortp) {
                 // drain (bounded): the last stage issued into each slot, and the image
-                for (int qq = q - RS < 0 ? 0 : q - RS; qq < q; qq++) {
+                for (int sl = 0; sl < RS; sl++) {
+                    if (last_phase[sl] < 0) continue;
                     const uint64_t t0 = vxc_globaltimer();
-                    while (!mbar_try(raw_full(qq % RS), (qq / RS) & 1) && vxc_globaltimer() - t0 < 100000000ull) {}
+                    while (!mbar_try(raw_full(sl), last_phase[sl] & 1) && vxc_globaltimer() - t0 < 100000000ull) {}
                 }
                 for (int g = 0; total > 0 && g < nst; g++) {
                     const uint64_t t0 = vxc_globaltimer();
@@ -231,10 +256,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
         bool ok = true;
         for (int item = 0; item < nitems && ok; item++) {
             for (int gl = group; gl < nst; gl += 2) {
-                const int q = item * nst + gl, s = q % RS;
-                const int u = item * per_item + (gl >> 1);   // use count of this group's A buffer
+                const int u = item * per_item + (gl >> 1);   // this group's stage count (A buffer, ring slot)
+                const int s = group * RSG + u % RSG;
                 const int kbn = min(KB, nb - gl * KB);
-                bool w_ok = mbar_wait_warp(raw_full(s), (q / RS) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA);
+                bool w_ok = mbar_wait_warp(raw_full(s), (u / RSG) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA);
                 uint32_t qw[KB][C::QB / 4];
                 uint32_t dh[KB];
                 if (w_ok) {
@@ -379,9 +404,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static int gm_kb(int nt) { return nt >= 3 ? 2 : 4; }
+static int gm_kb(int nt) { return nt >= 3 ? 2 : GM_KB_SMALL_N; }
 static int gm_stage(int qt, int nt) { return gm_kb(nt) * (128 * (qt == 2 ? 16 : 32) + 256); }
-static int gm_rs(int qt, int nt) { return (qt == 2 ? 6 : 4) * (4 / gm_kb(nt)); }
+static int gm_rs(int qt, int nt) { return (qt == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / gm_kb(nt); }
 
 static size_t gm_smem(int qt, int nt, int nbs) {
     return (size_t)nbs * 128 * 16 * nt + (size_t)gm_rs(qt, nt) * gm_stage(qt, nt);
