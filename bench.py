@@ -287,6 +287,9 @@ def cpu_q4matvec(budget_s, threads, ship=True):
 SPEC_TARGET = (4096, 32, 32, 32, 11008, 32000, 2, 11)   # Llama-2-7B shape, Q4_0
 SPEC_DRAFT = (2048, 22, 32, 4, 5632, 32000, 8, 12)      # 1.1B shape (GQA 32/4), Q8_0
 SPEC = {"seqs_per_gpu": 8, "k": 4, "prompt": 512, "new": 256, "temp": 0.0, "seed": 1}
+# 2-layer versions of the same widths: the small case for ncu captures (well under 2 GB on the device)
+SPEC_TARGET_2L = (4096, 2, 32, 32, 11008, 32000, 2, 13)
+SPEC_DRAFT_2L = (2048, 2, 32, 4, 5632, 32000, 8, 14)
 
 
 def q_bytes(rows, cols, wtype):
@@ -319,7 +322,8 @@ def spec_fixtures(write):
     d = fixture_dir()
     os.makedirs(d, exist_ok=True)
     paths = []
-    for name, c in (("target7b_q4_0", SPEC_TARGET), ("draft1b_q8_0", SPEC_DRAFT)):
+    names = ("target7b_q4_0", "draft1b_q8_0") if SPEC_TARGET[1] == 32 else ("target7b2l_q4_0", "draft1b2l_q8_0")
+    for name, c in zip(names, (SPEC_TARGET, SPEC_DRAFT)):
         p = os.path.join(d, name + ".gguf")
         if write and not os.path.exists(p):
             E, L, H, KH, F, V, wt, seed = c
@@ -328,6 +332,22 @@ def spec_fixtures(write):
             os.replace(tmp, p)
         paths.append(p)
     return paths
+
+
+def shard(rank, world, per_rank):
+    """Global sequence ids of this rank: weak scaling, `per_rank` sequences per GPU."""
+    return rank * per_rank, per_rank
+
+
+def reduce_over_ranks(dist, maxes, sums, device):
+    """Max-over-ranks of the timings, sum-over-ranks of the counters (no-op on one rank)."""
+    import torch
+    t = torch.tensor(maxes, device=device, dtype=torch.float64)
+    n = torch.tensor(sums, device=device, dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    return t.tolist(), n.tolist()
 
 
 def spec_prompts(first_seq, n):
@@ -355,9 +375,10 @@ def run_spec7b_gpu(args, ws, rank, local):
     tpath, dpath = spec_fixtures(write=False)
     target = vxb200.Model(tpath)
     draft = vxb200.Model(dpath)
-    S, k = SPEC["seqs_per_gpu"], SPEC["k"]
-    sp = vxb200.Speculative(draft, target, k, temp=SPEC["temp"], seed=SPEC["seed"], seq_id_base=rank * S)
-    prompts = spec_prompts(rank * S, S)
+    k = SPEC["k"]
+    first, S = shard(rank, ws, SPEC["seqs_per_gpu"])
+    sp = vxb200.Speculative(draft, target, k, temp=SPEC["temp"], seed=SPEC["seed"], seq_id_base=first)
+    prompts = spec_prompts(first, S)
     new = SPEC["new"]
 
     def step():
@@ -407,13 +428,10 @@ def run_spec7b_gpu(args, ws, rank, local):
         vxb200.lib().vxc_profile_read(buf, 12)
         vxb200.lib().vxc_profile_enable(0)
         stages[key] = {nm: round(buf[i] / 6, 4) for i, nm in enumerate(names)}
-    t = torch.tensor([dec_ms, pre_ms, wall_s, v_ms, d_ms, a_ms], device="cuda", dtype=torch.float64)
-    n = torch.tensor([emitted, accepted, drafted, rounds, launches], device="cuda", dtype=torch.float64)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(n, op=dist.ReduceOp.SUM)
-    dec_ms, pre_ms, wall_s, v_ms_max, d_ms_max, a_ms_max = t.tolist()
-    emitted, accepted, drafted, rounds, launches = [int(x) for x in n.tolist()]
+    t, n = reduce_over_ranks(dist, [dec_ms, pre_ms, wall_s, v_ms, d_ms, a_ms],
+                             [emitted, accepted, drafted, rounds, launches], "cuda")
+    dec_ms, pre_ms, wall_s, v_ms_max, d_ms_max, a_ms_max = t
+    emitted, accepted, drafted, rounds, launches = [int(x) for x in n]
     h2d = S * SPEC["prompt"] * 4
     d2h = S * new * 4
     res = dict(emitted=emitted, accepted=accepted, drafted=drafted, rounds=rounds, dec_ms=dec_ms, pre_ms=pre_ms,
@@ -521,8 +539,9 @@ SPEC_METRIC = "accepted tok/s (7B-shape Q4_0 spec decode)"
 
 
 def spec_config(ws):
+    layers = "" if SPEC_TARGET[1] == 32 else f" ({SPEC_TARGET[1]}+{SPEC_DRAFT[1]} layers: profiling case)"
     return {"workload": "spec7b: Llama-2-7B-shape Q4_0 target + 1.1B-shape Q8_0 draft, k=4, greedy, "
-                        "512-id prompts, 256 new tokens",
+                        f"512-id prompts, {SPEC['new']} new tokens" + layers,
             "seqs_per_gpu": SPEC["seqs_per_gpu"], "global_seqs": SPEC["seqs_per_gpu"] * ws, "k": SPEC["k"],
             "prompt": SPEC["prompt"], "new_tokens": SPEC["new"], "temp": SPEC["temp"],
             "l2": "no flush: >= 4 GB of KV + 3.7 GB of weights per verify step, far above L2",
@@ -594,7 +613,8 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="spec7b", choices=["spec7b", "q4matvec"])
+    ap.add_argument("--workload", default="spec7b", choices=["spec7b", "spec2l", "q4matvec"],
+                    help="spec2l: spec7b with 2-layer models, the small case for profilers")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--new", type=int, default=SPEC["new"], help="spec7b: new tokens per sequence")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (profiling runs)")
@@ -604,7 +624,10 @@ def main():
     threads = host_threads()
     if args.impl == "reference" and rank != 0:
         return   # the CPU reference runs on rank 0 only
-    if args.workload == "spec7b":
+    if args.workload == "spec2l":
+        global SPEC_TARGET, SPEC_DRAFT
+        SPEC_TARGET, SPEC_DRAFT = SPEC_TARGET_2L, SPEC_DRAFT_2L
+    if args.workload in ("spec7b", "spec2l"):
         main_spec7b(args, ws, rank, threads)
     else:
         main_q4matvec(args, ws, rank, threads)
