@@ -104,3 +104,31 @@ def test_stream_single_token_prompt(models):
         assert tok == out[i], i
         lg = t.forward(np.array([tok]))
     sp.close()
+
+
+_EAGER_SCRIPT = r"""
+import sys
+sys.path[:0] = [{tests!r}, {pkg!r}]
+import numpy as np, vxb200, fixtures
+vxb200.check(vxb200.lib().vxc_device_init(0))
+t = vxb200.Model(fixtures.path("tiny_target")); d = vxb200.Model(fixtures.path("tiny_draft"))
+sp = vxb200.Speculative(d, t, 4, temp=0.8, seed=7)
+p = np.random.default_rng(3).integers(0, 4096, 32, dtype=np.int32)
+print(" ".join(str(int(x)) for x in sp.generate(p, 48)))
+"""
+
+
+def test_eager_rounds_equal_graph_rounds(models):
+    """VX_SPEC_EAGER=1 (plain launches, for profilers) emits the same tokens as the graph loop."""
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    pkg = os.path.join(os.path.dirname(here), "veltrix-engine_b200")
+    code = _EAGER_SCRIPT.format(tests=here, pkg=pkg)
+    outs = []
+    for eager in ("0", "1"):
+        env = dict(os.environ, VX_SPEC_EAGER=eager)
+        r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+        assert r.returncode == 0, r.stderr[-2000:]
+        outs.append(r.stdout.strip().splitlines()[-1])
+    assert outs[0] == outs[1] and len(outs[0].split()) == 48
