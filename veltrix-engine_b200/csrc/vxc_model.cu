@@ -66,7 +66,9 @@ struct vxc_seqs {
     int attn_sl, attn_splits;
 };
 
-#define ATTN_QC 16      // queries per attention CTA
+// queries per attention CTA: 8 when a kv head has <= 8 queries (verify rows x
+// heads per kv head), else 16; the predicated query loops then carry little waste
+#define ATTN_QC_MAX 16
 #define ATTN_T 32       // key positions per smem tile
 #ifndef ATTN_SL_MIN
 #define ATTN_SL_MIN 64  // shortest context split
@@ -189,7 +191,7 @@ __global__ void k_rope_kv(Part qkv, int T, const int *__restrict__ d_slot, const
 }
 
 // Decode/verify attention, split over the context (flash-decoding style).
-// CTA = (group g, kv head, chunk of <= ATTN_QC queries) x one split of SL
+// CTA = (group g, kv head, chunk of <= QC queries) x one split of SL
 // positions.  The queries are the rows of group g times the q heads that
 // share the kv head (GQA mapping kv_h = h*KH/H, src/model.c:303), so each K/V
 // byte of the split is read from HBM once for all of them.
@@ -219,7 +221,7 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int HD>
+template <int HD, int QC>
 __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qbuf, int T, const int *__restrict__ d_slot,
                                                     const int *__restrict__ d_pos, int H, int KH,
                                                     const float *__restrict__ kc, const float *__restrict__ vc,
@@ -227,22 +229,22 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
                                                     float *__restrict__ part) {
     constexpr int NC = HD / 4;                  // float4 chunks per row
     constexpr int QPW = 32 / NC;                // query slots per warp in P.V
-    constexpr int QT1 = ATTN_QC / 4;            // queries per thread in the score pass
-    constexpr int QT3 = (ATTN_QC + 4 * QPW - 1) / (4 * QPW);   // ... in the P.V pass
+    constexpr int QT1 = QC / 4;            // queries per thread in the score pass
+    constexpr int QT3 = (QC + 4 * QPW - 1) / (4 * QPW);   // ... in the P.V pass
     static_assert(HD % 32 == 0 && HD <= 128, "head dim");
     extern __shared__ __align__(16) float sm[];
     float4 *ring = reinterpret_cast<float4 *>(sm);                 // [NS][T][NC]
     float4 *qs = ring + ATTN_NS * ATTN_T * NC;                      // [QC][NC]
-    float *sc = reinterpret_cast<float *>(qs + ATTN_QC * NC);       // [QC][SL+1]
-    __shared__ float qmax[ATTN_QC], qsum[ATTN_QC];
+    float *sc = reinterpret_cast<float *>(qs + QC * NC);       // [QC][SL+1]
+    __shared__ float qmax[QC], qsum[QC];
     const int G = H / KH, nq = T * G;
     const int bx = blockIdx.x;
     const int qc = bx % nqc;
     const int kvh = (bx / nqc) % KH;
     const int g = bx / (nqc * KH);
     const int split = blockIdx.y, nsplit = gridDim.y;
-    const int q0 = qc * ATTN_QC;
-    const int nql = min(ATTN_QC, nq - q0);
+    const int q0 = qc * QC;
+    const int nql = min(QC, nq - q0);
     const int E = H * HD;
     pdl_trigger();
     pdl_wait();
@@ -537,8 +539,12 @@ __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__re
     const int rec = hd + 4;
     const int hpc = (H + ROW_CL - 1) / ROW_CL;
     const int h0 = min(H, blockIdx.x * hpc), h1 = min(H, h0 + hpc);
+    // warps take (head, part of the head's columns): with fewer heads than warps, P warps share a head
+    const int nh = h1 - h0;
+    const int P = nh > 0 && nh < nw ? nw / nh : 1;
     float mx = 0.0f;
-    for (int h = h0 + w; h < h1; h += nw) {
+    for (int it = w; it < nh * P; it += nw) {
+        const int h = h0 + it / P, cpart = it % P;
         const int kvh = h / G, q = t * G + (h % G);
         const float *pp = part + (((size_t)g * KH + kvh) * nq + q) * nsplit * rec;
         const float ms = lane < nsplit ? pp[(size_t)lane * rec] : -INFINITY;
@@ -546,7 +552,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__re
         const float e = (ms == -INFINITY) ? 0.0f : expf(ms - Mx);
         const float Ls = warp_sum(lane < nsplit ? e * pp[(size_t)lane * rec + 1] : 0.0f);
         const float inv = 1.0f / (Ls + 1e-10f);
-        for (int d = lane; d < hd; d += 32) {
+        for (int d = cpart * 32 + lane; d < hd; d += 32 * P) {
             float o = 0.0f;
             for (int sp = 0; sp < nsplit; sp++) {
                 const float es = __shfl_sync(0xffffffffu, e, sp);
@@ -733,19 +739,25 @@ extern "C" size_t vxc_net_weight_bytes(const vxc_net *n) { return n ? n->weight_
 // ---------------------------------------------------------------------------
 // host: sequences + forward
 // ---------------------------------------------------------------------------
-static size_t attn_smem(int hd, int SL) {
-    return ((size_t)ATTN_NS * ATTN_T * hd + (size_t)ATTN_QC * hd + (size_t)ATTN_QC * (SL + 1)) * sizeof(float);
+static size_t attn_smem(int hd, int SL, int qc) {
+    return ((size_t)ATTN_NS * ATTN_T * hd + (size_t)qc * hd + (size_t)qc * (SL + 1)) * sizeof(float);
 }
+
+static int attn_qc(int nq) { return nq <= 8 ? 8 : 16; }
 
 typedef void (*attn_kernel_t)(const float *, int, const int *, const int *, int, int, const float *, const float *,
                               int, int, int, int, float *);
 
-static attn_kernel_t attn_kernel(int hd) {
-    switch (hd) {
-        case 32: return k_attn_split<32>;
-        case 64: return k_attn_split<64>;
-        case 96: return k_attn_split<96>;
-        case 128: return k_attn_split<128>;
+static attn_kernel_t attn_kernel(int hd, int qc) {
+    switch (hd * 100 + qc) {
+        case 3208: return k_attn_split<32, 8>;
+        case 3216: return k_attn_split<32, 16>;
+        case 6408: return k_attn_split<64, 8>;
+        case 6416: return k_attn_split<64, 16>;
+        case 9608: return k_attn_split<96, 8>;
+        case 9616: return k_attn_split<96, 16>;
+        case 12808: return k_attn_split<128, 8>;
+        case 12816: return k_attn_split<128, 16>;
         default: return NULL;
     }
 }
@@ -856,18 +868,19 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     if (e == cudaSuccess) e = cudaMemset(s->k, 0, kvn * 4);
     if (e == cudaSuccess) e = cudaMemset(s->v, 0, kvn * 4);
     if (e == cudaSuccess) e = cudaMemset(s->img, 0, (size_t)nch * s->img_chunk);
-    if (e == cudaSuccess && !attn_kernel(hd)) {
+    if (e == cudaSuccess && !attn_kernel(hd, 16)) {
         vxc_set_error("vxc_seqs_create: head dim %d not supported (32, 64, 96 or 128)", hd);
         vxc_seqs_destroy(s);
         return -7;
     }
-    if (e == cudaSuccess && attn_smem(hd, SL) > 227 * 1024) {
+    if (e == cudaSuccess && attn_smem(hd, SL, ATTN_QC_MAX) > 227 * 1024) {
         vxc_set_error("vxc_seqs_create: context %d too long for the attention split", max_ctx);
         vxc_seqs_destroy(s);
         return -4;
     }
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_kernel(hd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem(hd, SL));
+    for (int qc = 8; qc <= 16 && e == cudaSuccess; qc += 8)
+        e = cudaFuncSetAttribute(attn_kernel(hd, qc), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)attn_smem(hd, SL, qc));
     if (e != cudaSuccess) {
         vxc_set_error("vxc_seqs_create: %s", cudaGetErrorString(e));
         vxc_seqs_destroy(s);
@@ -994,8 +1007,8 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     e = launch_pdl(k_embed, dim3(M), dim3(256), 0, st, n->embd, n->embd_type, n->embd_row_bytes,
                                n->embd_rows, E, d_tokens, s->x, err);
     prof_end(0, pe, st);
-    const int G = H / KH, nq = T * G, nqc = (nq + ATTN_QC - 1) / ATTN_QC;
-    const size_t asm_bytes = attn_smem(hd, s->attn_sl);
+    const int G = H / KH, nq = T * G, qcn = attn_qc(nq), nqc = (nq + qcn - 1) / qcn;
+    const size_t asm_bytes = attn_smem(hd, s->attn_sl, qcn);
     // local columns of a row kernel's CTA (norm: E / ROW_CL, SwiGLU: F / ROW_CL, merge: heads x hd)
     auto cols8 = [](int K) { return ((K + ROW_CL - 1) / ROW_CL + 7) / 8 * 8; };
     size_t row_smem = (size_t)cols8(E);
@@ -1025,7 +1038,7 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         prof_end(3, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
-        e = launch_pdl(attn_kernel(hd), dim3(n_groups * KH * nqc, s->attn_splits), dim3(128), asm_bytes, st,
+        e = launch_pdl(attn_kernel(hd, qcn), dim3(n_groups * KH * nqc, s->attn_splits), dim3(128), asm_bytes, st,
                        (const float *)s->qbuf, T, d_slot, d_pos, H, KH, (const float *)kc, (const float *)vc,
                        s->n_slots, s->max_ctx, s->attn_sl, nqc, s->attn_part);
         prof_end(4, pe, st);
