@@ -197,7 +197,7 @@ def run_q4matvec_gpu(args, ws, rank, local):
     clocks = clk.stop()
     ms_total = t0.elapsed_time(t1)
     per_case = {}
-    kern_ms, kern_bytes = 0.0, 0
+    kern_ms, kern_bytes, kern_wbytes, kern_launches = 0.0, 0, 0, 0
     for c in cases:
         (R, K), M = c
         tms = [evs[k][c][i][0].elapsed_time(evs[k][c][i][1]) for k in range(args.steps) for i in range(len(mats[c[0]]))]
@@ -206,6 +206,8 @@ def run_q4matvec_gpu(args, ws, rank, local):
         per_case[f"{R}x{K}_M{M}"] = round(b / (avg * 1e-3) / 1e9, 1)
         kern_ms += sum(tms)
         kern_bytes += b * len(tms)
+        kern_wbytes += R * (K // 32) * 18 * len(tms)
+        kern_launches += len(tms)
     step_bytes = sum(q4_bytes(s[0], s[1], M) * len(mats[s]) for (s, M) in cases)
     # e2e through the C-ABI with host buffers: pinned x in, y out, each call
     hx = {M: torch.randn(M, 4096).pin_memory() for M in MS}
@@ -232,7 +234,8 @@ def run_q4matvec_gpu(args, ws, rank, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_total, e2e_ms, kern_ms_max = t.tolist()
     res = dict(step_bytes=step_bytes, ms_total=ms_total, e2e_ms=e2e_ms, per_case=per_case,
-               kern_ms=kern_ms, kern_bytes=kern_bytes, clocks=clocks, launches=n_launch,
+               kern_ms=kern_ms, kern_bytes=kern_bytes, kern_wbytes=kern_wbytes, kern_launches=kern_launches,
+               clocks=clocks, launches=n_launch,
                h2d=h2d // args.steps, d2h=d2h // args.steps)
     if dist:
         dist.barrier()
@@ -525,7 +528,9 @@ def main_q4matvec(args, ws, rank, threads):
            "data": "synthetic", "config": config,
            "per_case_gbs": r["per_case"],
            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(achieved / peak, 4), "traffic": None,
+                        "frac": round(achieved / peak, 4),
+                        "traffic": int(TRAFFIC_Q4_PER_WEIGHT_BYTE * r["kern_wbytes"] / r["kern_launches"]),
+                        "traffic_note": "per GEMV launch: mean weight bytes x the ncu-measured 1.033 DRAM ratio",
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                         "kernel": "vxc_qgemv, per-call CUDA events"},
            "cpu_baseline": cpu,
@@ -536,6 +541,21 @@ def main_q4matvec(args, ws, rank, threads):
 
 
 SPEC_METRIC = "accepted tok/s (7B-shape Q4_0 spec decode)"
+
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) from ncu captures of the current
+# kernels on B200.  One verify forward of the 2-layer profiling case
+#   VX_SPEC_EAGER=1 ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum \
+#       --clock-control none -s 2808 -c 24 python bench.py --workload spec2l --steps 1 --warmup 0 --no-cpu --new 8
+# gave 170.3 MB per layer outside attention (1.52x its 111.9 MB of Q4_0 weights: image and
+# split-K partial traffic), attention at 0.99x its K/V bytes, and 111 MB for the embedding,
+# final norm and LM head.  Scaled to 32 layers: traffic = 32 * 170.3 MB + 0.99 * KV bytes + 111 MB.
+TRAFFIC_LAYER_NONATTN = 170.3e6
+TRAFFIC_HEAD = 111.0e6
+TRAFFIC_ATTN_PER_KV_BYTE = 0.99
+# A 4096x4096 Q4_0 GEMV launch read 9.745 MB (9,437,184 weight bytes + activations): 1.033x.
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none \
+#       -k regex:k_qgemv_mma -s 0 -c 4 python bench.py --workload q4matvec --steps 1 --warmup 0 --no-cpu
+TRAFFIC_Q4_PER_WEIGHT_BYTE = 9.745e6 / 9437184
 
 
 def spec_config(ws):
@@ -586,7 +606,10 @@ def main_spec7b(args, ws, rank, threads):
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
            "data": "synthetic (random N(0,0.02) weights, uniform random prompt ids)", "config": spec_config(ws),
            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                        "frac": round(achieved / peak, 4), "traffic": None,
+                        "frac": round(achieved / peak, 4),
+                        "traffic": int(SPEC_TARGET[1] * TRAFFIC_LAYER_NONATTN
+                                       + TRAFFIC_ATTN_PER_KV_BYTE * r["v_kv"] + TRAFFIC_HEAD),
+                        "traffic_note": "ncu DRAM bytes of the 2-layer case's verify, scaled per layer",
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                         "kernel": "one (k+1)-row target verify forward (all its kernels), CUDA events on the "
                                   "engine stream, 10 re-runs",
