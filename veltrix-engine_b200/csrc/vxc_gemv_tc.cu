@@ -63,6 +63,12 @@
 // group IG and ring depth RS, such that TMEM holds the two groups' A buffers
 // (KB*32 columns each) plus 2*IG accumulators of 2N columns, and ~55-70 KB of
 // weights are in flight.
+#ifndef GM_PART_COST
+#define GM_PART_COST 0.5    // planner weight of a partial-sum byte (written + read) vs an HBM weight byte
+#endif
+#ifndef GM_IMAGE_COST
+#define GM_IMAGE_COST 0.3   // ... of an image byte (read from L2 by every CTA of a slice)
+#endif
 #ifndef GM_KB_SMALL_N
 #define GM_KB_SMALL_N 4     // blocks per stage for N <= 32
 #endif
@@ -437,8 +443,8 @@ bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p) {
         // sums (written + read) and of the image slices (read by every CTA of a slice)
         const double unit = (double)GM_SMS * (128 * 18);
         const double blocks = (double)tpc * nbs;
-        const double part = ks > 1 ? 0.5 * ks * (double)M * w->rows * 8.0 / unit : 0.0;
-        const double image = 0.3 * (double)ks * cps * nbs * 128.0 * N / unit;
+        const double part = ks > 1 ? GM_PART_COST * ks * (double)M * w->rows * 8.0 / unit : 0.0;
+        const double image = GM_IMAGE_COST * (double)ks * cps * nbs * 128.0 * N / unit;
         const double cost = blocks + tpc * 2.0 * KB + part + image;
         if (cost < best - 1e-9) {
             best = cost;
