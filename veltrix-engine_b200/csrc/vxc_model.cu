@@ -401,8 +401,12 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
 // row-wide sum of squares and max|value| are combined through distributed
 // shared memory in fixed rank order (deterministic, identical in every CTA).
 // ---------------------------------------------------------------------------
+#ifndef ROW_CL
 #define ROW_CL 8
+#endif
+#ifndef ROW_THREADS
 #define ROW_THREADS 256
+#endif
 
 // Sum (op 0) or max (op 1) of one value per CTA over the cluster; `slot` is
 // this reduction's own shared word.  Ends with the values read, so the slot
@@ -877,6 +881,11 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
         vxc_set_error("vxc_seqs_create: context %d too long for the attention split", max_ctx);
         vxc_seqs_destroy(s);
         return -4;
+    }
+    if (ROW_CL > 8) {   // clusters above the portable size of 8 must be allowed per kernel
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_norm_image, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_swiglu_image, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_combine_image, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     }
     for (int qc = 8; qc <= 16 && e == cudaSuccess; qc += 8)
         e = cudaFuncSetAttribute(attn_kernel(hd, qc), cudaFuncAttributeMaxDynamicSharedMemorySize,
