@@ -73,6 +73,9 @@ struct vxc_seqs {
 #ifndef ATTN_SL_MIN
 #define ATTN_SL_MIN 64  // shortest context split
 #endif
+#ifndef ATTN_SL_MIN_WIDE
+#define ATTN_SL_MIN_WIDE 128  // ... for head dims >= 128 (fewer splits to merge)
+#endif
 
 // ---------------------------------------------------------------------------
 // kernels
@@ -852,7 +855,8 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     // measured faster on B200 than deeper rings (the kernel is latency-bound per CTA).
     int SL = (max_ctx + 15) / 16;
     SL = ((SL + ATTN_T - 1) / ATTN_T) * ATTN_T;
-    if (SL < ATTN_SL_MIN) SL = ATTN_SL_MIN;
+    const int sl_min = hd >= 128 ? ATTN_SL_MIN_WIDE : ATTN_SL_MIN;
+    if (SL < sl_min) SL = sl_min;
     s->attn_sl = SL;
     s->attn_splits = (max_ctx + SL - 1) / SL;
     size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 4);
