@@ -208,7 +208,7 @@ __global__ void k_rope_kv(Part qkv, int T, const int *__restrict__ d_slot, const
 //   P.V     lane = chunk of the output row, loop over positions.
 // Per query the CTA writes its split's record [m, l, -, -, o[hd]] (16-byte
 // aligned): max m, sum l of exp(s - m) and o = sum exp(s - m) v;
-// k_attn_combine merges the splits.
+// k_combine_image merges the splits.
 #ifndef ATTN_NS
 #define ATTN_NS 2
 #endif
@@ -587,10 +587,6 @@ __global__ void k_part_out(Part p, int n_rows, float *__restrict__ out) {
         out[i] = p.get((int)(i / p.R), (int)(i % p.R));
 }
 
-__global__ void k_fill(float *__restrict__ p, size_t n, float v) {
-    size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) p[i] = v;
-}
 
 // ---------------------------------------------------------------------------
 // host: upload
