@@ -27,7 +27,7 @@
 typedef unsigned long long u64;
 typedef unsigned __int128 u128;
 
-#define SMP_THREADS 512
+#define SMP_THREADS 1024
 
 // ---------------------------------------------------------------------------
 // block-wide helpers (blockDim.x == SMP_THREADS)
@@ -408,9 +408,10 @@ struct vxc_spec {
     float *dlog;       // [k][S][V]
     float *vlog;       // [S][k+1][V]
     void *acc_ws;
-    int *prefill_buf;  // staging for prefill tokens/meta
-    int prefill_rows;
+    int *prefill_meta; // per prompt chunk: sequence slot, first position
+    int prefill_cap;   // ints in prefill_meta
     cudaStream_t st;
+    cudaStream_t st2;  // the draft's prompt pass runs here, beside the target's
     cudaGraph_t graph;
     cudaGraphExec_t exec;
     int *h_ndone;      // pinned
@@ -439,7 +440,7 @@ extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int 
     e->V = tc.n_vocab;
     int trows = n_seq * (k + 1) > 64 ? n_seq * (k + 1) : 64;
     int drows = 2 * n_seq > 64 ? 2 * n_seq : 64;
-    e->prefill_rows = 64;
+    e->prefill_cap = 2 * 2 * n_seq * ((max_ctx + 63) / 64);
     if ((rc = vxc_seqs_create(target, n_seq, max_ctx, trows, &e->ts)) ||
         (rc = vxc_seqs_create(draft, n_seq, max_ctx, drows, &e->ds))) {
         vxc_spec_destroy(e);
@@ -476,10 +477,11 @@ extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int 
     DALLOC(e->dlog, (size_t)k * S * e->V * sizeof(float));
     DALLOC(e->vlog, (size_t)S * (k + 1) * e->V * sizeof(float));
     DALLOC(e->acc_ws, accept_ws(S, k));
-    DALLOC(e->prefill_buf, (size_t)(64 + 3 * S + 8) * sizeof(int));
+    DALLOC(e->prefill_meta, (size_t)e->prefill_cap * sizeof(int));
 #undef DALLOC
     if (err == cudaSuccess) err = cudaMemset(e->acc_ws, 0, accept_ws(S, k));
     if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->st2, cudaStreamNonBlocking);
     if (err == cudaSuccess) err = cudaMallocHost((void **)&e->h_ndone, 4 * sizeof(int));
     if (err == cudaSuccess) {
         std::vector<int> sl(S);
@@ -504,11 +506,12 @@ extern "C" void vxc_spec_destroy(vxc_spec *e) {
     SpecDev &D = e->D;
     void *ptrs[] = {D.c, D.L, D.gen, D.done, D.seq_id, D.slot, D.out, D.tok0, D.pos0, D.lrow0, D.dpos, D.dtok,
                     D.vtok, D.vpos, D.vrows, D.dseq, D.apos, D.n_acc, D.next, D.ctr, D.n_done, e->dlog, e->vlog,
-                    e->acc_ws, e->prefill_buf};
+                    e->acc_ws, e->prefill_meta};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (e->h_ndone) cudaFreeHost(e->h_ndone);
     if (e->st) cudaStreamDestroy(e->st);
+    if (e->st2) cudaStreamDestroy(e->st2);
     free(e);
 }
 
@@ -625,30 +628,47 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     }
     cudaEvent_t ev[4];
     for (int i = 0; i < 4; i++) cudaEventCreate(&ev[i]);
-    // ---- prefill: target 0..L-2, draft 0..L-3 (one sequence at a time) ----
+    // ---- prompt pass: target rows 0..L-2, draft rows 0..L-3, in chunks of 64 rows
+    // read straight from the committed tokens; the draft's chunks run on st2
+    // beside the target's, with no host round trip between chunks ----
     cudaEventRecord(ev[0], st);
     {
-        size_t off = 0;
-        int *buf = e->prefill_buf;
-        for (int s = 0; s < S; s++) {
-            const int *p = prompts + off;
-            off += prompt_len[s];
-            for (int which = 0; which < 2; which++) {
-                int n = prompt_len[s] - (which == 0 ? 1 : 2);
-                vxc_seqs *q = which == 0 ? e->ts : e->ds;
-                for (int done = 0; done < n;) {
-                    int ch = n - done < 64 ? n - done : 64;
-                    int meta[2] = {s, done};
-                    cudaMemcpyAsync(buf, p + done, ch * sizeof(int), cudaMemcpyHostToDevice, st);
-                    cudaMemcpyAsync(buf + 64, meta, sizeof meta, cudaMemcpyHostToDevice, st);
-                    int rc = vxc_forward(q, buf, buf + 64, buf + 65, 1, ch, NULL, 0, NULL, st);
-                    if (rc) return rc;
-                    // staging buffer is reused: finish before the next chunk overwrites it
-                    cudaStreamSynchronize(st);
-                    done += ch;
+        std::vector<int> meta;
+        std::vector<int> which_of, len_of;
+        for (int which = 0; which < 2; which++)
+            for (int sq = 0; sq < S; sq++) {
+                const int n = prompt_len[sq] - (which == 0 ? 1 : 2);
+                for (int done = 0; done < n; done += 64) {
+                    meta.push_back(sq);
+                    meta.push_back(done);
+                    which_of.push_back(which);
+                    len_of.push_back(n - done < 64 ? n - done : 64);
                 }
             }
+        if ((int)meta.size() > e->prefill_cap) {
+            vxc_set_error("vxc_spec_generate: prompt chunks exceed the engine's context");
+            return -4;
         }
+        cudaEvent_t up, join;
+        cudaEventCreateWithFlags(&up, cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
+        if (!meta.empty())
+            err = cudaMemcpyAsync(e->prefill_meta, meta.data(), meta.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+        cudaEventRecord(up, st);
+        cudaStreamWaitEvent(e->st2, up, 0);
+        int rc = 0;
+        for (size_t i = 0; i < which_of.size() && rc == 0 && err == cudaSuccess; i++) {
+            const int sq = meta[2 * i], done = meta[2 * i + 1];
+            const bool tgt = which_of[i] == 0;
+            rc = vxc_forward(tgt ? e->ts : e->ds, D.c + (size_t)sq * D.cap + done, e->prefill_meta + 2 * i,
+                             e->prefill_meta + 2 * i + 1, 1, len_of[i], NULL, 0, NULL, tgt ? st : e->st2);
+        }
+        cudaEventRecord(join, e->st2);
+        cudaStreamWaitEvent(st, join, 0);
+        cudaEventDestroy(up);
+        cudaEventDestroy(join);
+        if (rc) return rc;
+        if (err != cudaSuccess) { vxc_set_error("vxc_spec_generate: %s", cudaGetErrorString(err)); return -3; }
     }
     cudaEventRecord(ev[1], st);
     // ---- round loop: first round eager, then a captured graph ----
