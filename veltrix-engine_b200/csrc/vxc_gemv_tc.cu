@@ -47,6 +47,7 @@
 // error code, all roles stop, in-flight copies and MMAs are drained (bounded)
 // and TMEM is freed.
 #include "vxc_common.cuh"
+#include "vxc_image.cuh"
 #include "vxc_ptx.cuh"
 #include "vxc_qmat.cuh"
 #include "vxc_internal.h"
@@ -89,8 +90,9 @@ struct GmCfg {
 struct GmArgs {
     const uint8_t *qs;      // weight records
     int R, nblk, ntile;
-    const uint8_t *img;     // activation image, N rows
-    const float *xs;        // [M] prescales
+    const uint8_t *img;     // activation image, N rows (when x == NULL)
+    const float *xs;        // [M] prescales of the image
+    const float *x;         // or fp32 activation rows [M][K]: each CTA builds its slice's image
     int M;
     float *part;            // [ks][M][R]
     int ks, nbs;
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
                 issue(q);
             }
             pdl_wait();
-            if (total > 0) {
+            if (total > 0 && !a.x) {
                 // the image slice, one barrier per stage so the first MMAs need not wait for all of it
                 for (int g = 0; g < nst; g++) {
                     const int kbn = min(KB, nb - g * KB);
@@ -369,8 +371,39 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(acc_empty);
-        pdl_wait();   // xs comes from the preceding kernel; part may still be read by it
-        for (int m = tid - 320; m < N; m += 128) xinv[m] = m < M ? a.wscale / a.xs[m] : 0.0f;
+        pdl_wait();   // xs / x come from the preceding kernel; part may still be read by it
+        if (a.x) {
+            // fp32 rows in: build this slice's image in shared memory with a prescale of
+            // its own per row (the partials are divided by it, so slices may differ)
+            const int K = a.nblk * 32, k0 = b0 * 32, kl = nb * 32;
+            const int et = tid - 320;
+            for (int m = warp - 10; m < M; m += 4) {
+                const float *xr = a.x + (size_t)m * K + k0;
+                float mx = 0.0f;
+                for (int k = lane; k < kl; k += 32) mx = fmaxf(mx, fabsf(xr[k]));
+                mx = warp_max(mx);
+                if (lane == 0) xinv[m] = vxc_prescale(mx);   // the prescale for now
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            for (int it = et; it < nb * 4 * M; it += 128) {
+                const int m = it % M, rest = it / M, c = rest & 3, b = rest >> 2;
+                const float4 *src = reinterpret_cast<const float4 *>(a.x + (size_t)m * K + k0 + b * 32 + c * 8);
+                const float4 v0 = src[0], v1 = src[1];
+                const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                uint4 hi, lo;
+                vxc_hilo8(v, xinv[m], hi, lo);
+                uint8_t *chunk = Bs + (size_t)(b * 4 + c) * NP * 16;
+                *reinterpret_cast<uint4 *>(chunk + (size_t)m * 16) = hi;
+                *reinterpret_cast<uint4 *>(chunk + (size_t)(N + m) * 16) = lo;
+            }
+            fence_proxy_async();   // generic-proxy stores -> the MMAs' async-proxy reads
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (et == 0)
+                for (int g = 0; g < nst && total > 0; g++) mbar_arrive(b_full(g));
+            for (int m = et; m < N; m += 128) xinv[m] = m < M ? a.wscale / xinv[m] : 0.0f;
+        } else {
+            for (int m = tid - 320; m < N; m += 128) xinv[m] = m < M ? a.wscale / a.xs[m] : 0.0f;
+        }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         for (int item = 0; item < nitems; item++) {
             bool ok = mbar_wait_warp(acc_full, item & 1, abortp, err, VXC_DERR_TIMEOUT_EPI);
@@ -487,7 +520,7 @@ static cudaError_t launch_mma(const GmArgs &ga, const VxcGemvPlan &p, cudaStream
 }
 
 int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, float *part,
-                 const VxcGemvPlan &p, cudaStream_t st) {
+                 const VxcGemvPlan &p, cudaStream_t st, const float *x) {
     if (p.nt != (M + 15) / 16 || p.ks < 1 || p.grid < p.ks || p.smem > GM_SMEM_DYN) {
         vxc_set_error("vxc_gemv_run: plan does not match M = %d", M);
         return -4;
@@ -499,6 +532,7 @@ int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, 
     ga.ntile = w->ntile;
     ga.img = img;
     ga.xs = xs;
+    ga.x = x;
     ga.M = M;
     ga.part = part;
     ga.ks = p.ks;
@@ -528,14 +562,13 @@ int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, 
     return 0;
 }
 
-// Workspace of the public entry point for one chunk of M <= 64 rows:
-// [image 128*N per block][prescales, 256 B][partials ks*M*R fp32 when ks > 1]
-static size_t img_bytes(const vxc_qmat *w, int M) { return (size_t)w->nblk * vxc_img_block_bytes(vxc_img_rows(M)); }
+// Workspace of the public entry point for one chunk of M <= 64 rows: the
+// split-K partial sums, ks*M*R fp32 (none when ks == 1)
 
 static size_t chunk_ws_bytes(const vxc_qmat *w, int M) {
     VxcGemvPlan p;
     if (!vxc_gemv_plan(w, M, &p)) return 0;
-    return img_bytes(w, M) + 256 + (p.ks > 1 ? (size_t)p.ks * M * w->rows * sizeof(float) : 0);
+    return p.ks > 1 ? (size_t)p.ks * M * w->rows * sizeof(float) : 0;
 }
 
 extern "C" size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M) {
@@ -562,15 +595,13 @@ extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, voi
         VxcGemvPlan p;
         if (!vxc_gemv_plan(w, mc, &p)) { vxc_set_error("vxc_qgemv: no plan for %d x %d", w->rows, w->cols); return -7; }
         const size_t need = chunk_ws_bytes(w, mc);
-        if (!workspace || need > workspace_bytes) {
+        if ((need && !workspace) || need > workspace_bytes) {
             vxc_set_error("vxc_qgemv: workspace %zu < %zu bytes", workspace_bytes, need);
             return -4;
         }
-        uint8_t *img = (uint8_t *)workspace;
-        float *xs = (float *)(img + img_bytes(w, mc));
-        float *part = p.ks > 1 ? xs + 64 : y + (size_t)m0 * w->rows;
-        int rc = vxc_launch_act_image(x + (size_t)m0 * w->cols, mc, w->cols, img, xs, st);
-        if (rc == 0) rc = vxc_gemv_run(w, img, xs, mc, part, p, st);
+        // the GEMV builds its K-slices' operand from the fp32 rows itself
+        float *part = p.ks > 1 ? (float *)workspace : y + (size_t)m0 * w->rows;
+        int rc = vxc_gemv_run(w, NULL, NULL, mc, part, p, st, x + (size_t)m0 * w->cols);
         if (rc == 0 && p.ks > 1) rc = vxc_launch_splitk_reduce(part, p.ks, mc, w->rows, y + (size_t)m0 * w->rows, st);
         if (rc) return rc;
     }

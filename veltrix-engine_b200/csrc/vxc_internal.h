@@ -25,8 +25,10 @@ struct VxcGemvPlan {
 bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p);
 // Launches the GEMV (programmatic dependent launch) reading an activation
 // image + prescales, writing part[ks][M][R] (ks == 1: the output itself).
+// With x != NULL the GEMV reads fp32 rows x[M][K] instead and builds each
+// K-slice's operand itself (img and xs unused).
 int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, float *part,
-                 const VxcGemvPlan &p, cudaStream_t st);
+                 const VxcGemvPlan &p, cudaStream_t st, const float *x = NULL);
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
 // Library-wide count of kernel launches (a CUDA-graph replay adds its kernels).
 void vxc_count_launches(long long n);
