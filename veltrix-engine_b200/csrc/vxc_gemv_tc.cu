@@ -562,13 +562,22 @@ int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, 
     return 0;
 }
 
-// Workspace of the public entry point for one chunk of M <= 64 rows: the
-// split-K partial sums, ks*M*R fp32 (none when ks == 1)
+// Up to this many rows the GEMV builds its K-slices' operand from the fp32
+// rows itself (measured faster: no separate image kernel); above it a
+// separate kernel writes the image once for all CTAs.
+#define GM_SELF_IMAGE_ROWS 16
+
+// Workspace of the public entry point for one chunk of M <= 64 rows:
+// [image 128*N per block][prescales, 256 B] when M > GM_SELF_IMAGE_ROWS, then
+// the split-K partial sums ks*M*R fp32 when ks > 1.
+static size_t img_bytes(const vxc_qmat *w, int M) {
+    return M > GM_SELF_IMAGE_ROWS ? (size_t)w->nblk * vxc_img_block_bytes(vxc_img_rows(M)) + 256 : 0;
+}
 
 static size_t chunk_ws_bytes(const vxc_qmat *w, int M) {
     VxcGemvPlan p;
     if (!vxc_gemv_plan(w, M, &p)) return 0;
-    return p.ks > 1 ? (size_t)p.ks * M * w->rows * sizeof(float) : 0;
+    return img_bytes(w, M) + (p.ks > 1 ? (size_t)p.ks * M * w->rows * sizeof(float) : 0);
 }
 
 extern "C" size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M) {
@@ -599,9 +608,18 @@ extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, voi
             vxc_set_error("vxc_qgemv: workspace %zu < %zu bytes", workspace_bytes, need);
             return -4;
         }
-        // the GEMV builds its K-slices' operand from the fp32 rows itself
-        float *part = p.ks > 1 ? (float *)workspace : y + (size_t)m0 * w->rows;
-        int rc = vxc_gemv_run(w, NULL, NULL, mc, part, p, st, x + (size_t)m0 * w->cols);
+        const float *xm = x + (size_t)m0 * w->cols;
+        const size_t ib = img_bytes(w, mc);
+        float *part = p.ks > 1 ? (float *)((uint8_t *)workspace + ib) : y + (size_t)m0 * w->rows;
+        int rc;
+        if (mc <= GM_SELF_IMAGE_ROWS) {
+            rc = vxc_gemv_run(w, NULL, NULL, mc, part, p, st, xm);
+        } else {
+            uint8_t *img = (uint8_t *)workspace;
+            float *xs = (float *)(img + ib - 256);
+            rc = vxc_launch_act_image(xm, mc, w->cols, img, xs, st);
+            if (rc == 0) rc = vxc_gemv_run(w, img, xs, mc, part, p, st);
+        }
         if (rc == 0 && p.ks > 1) rc = vxc_launch_splitk_reduce(part, p.ks, mc, w->rows, y + (size_t)m0 * w->rows, st);
         if (rc) return rc;
     }
