@@ -58,8 +58,9 @@ int vxc_profile_read(double *ms, int n);
 typedef struct vxc_qmat vxc_qmat;
 
 /* Upload a GGUF-layout matrix of `rows` x `cols` (cols % 32 == 0) held in
- * host memory and repack it for the device (quant plane + scale plane, 128-row
- * tiles).  type: 2 = Q4_0 (18-byte blocks), 8 = Q8_0 (34-byte blocks).
+ * host memory and repack it for the device (one record of quants + scales
+ * per 128-row tile and 32-column block, records of a tile contiguous along
+ * K).  type: 2 = Q4_0 (18-byte blocks), 8 = Q8_0 (34-byte blocks).
  * Replaces the reference's tensor load + whole-matrix dequant buffer
  * (src/gguf.c:236-287, src/model.c:74-87). */
 int vxc_qmat_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out);
@@ -67,7 +68,8 @@ void vxc_qmat_destroy(vxc_qmat *w);
 int vxc_qmat_shape(const vxc_qmat *w, int *type, int *rows, int *cols);
 
 /* Bytes of scratch vxc_qgemv (and vxc_qgemv_simt) needs for M activation
- * rows: the activation image, its prescales and the split-K partial sums. */
+ * rows: the split-K partial sums and, above 16 rows, the activation image
+ * and its prescales.  Nothing in it has to be initialised. */
 size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M);
 
 /* y[m][r] = sum_k W[r][k] * x[m][k] for m < M (fp32 in, fp32 out, device
