@@ -8,6 +8,11 @@
  *                   the logits of the LAST token into the caller's host buffer
  *                   (n_vocab floats; entries the LM head does not cover hold
  *                   -1e30, reference src/model.c:604).
+ * vx_model_create_tp (additive) loads this rank's shard of a model split over
+ *                   `world` GPUs, one process each (tensor parallelism over
+ *                   NCCL; nccl_id from vxc_tp_unique_id on rank 0).  Every
+ *                   rank then makes the same calls in the same order and
+ *                   gets the full logits.
  */
 #ifndef VX_MODEL_H
 #define VX_MODEL_H
@@ -21,6 +26,7 @@ extern "C" {
 vx_error vx_model_create(const char *path, vx_model **model);
 void vx_model_destroy(vx_model *model);
 vx_error vx_model_forward(vx_model *model, const int *tokens, int n_tokens, float *logits);
+vx_error vx_model_create_tp(const char *path, int rank, int world, const void *nccl_id, vx_model **model);
 
 #ifdef __cplusplus
 }

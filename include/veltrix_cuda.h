@@ -131,6 +131,27 @@ typedef struct vxc_seqs vxc_seqs;
 int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd, const vxc_tensor_view *out_norm,
                    const vxc_tensor_view *output, const vxc_layer_views *layers, vxc_net **out);
 void vxc_net_destroy(vxc_net *net);
+
+/* ---- tensor parallelism (one process per GPU, NCCL over NVLink) ----------- */
+
+/* A communicator over `world` GPUs, one per process.  Rank 0 makes the id
+ * (VXC_TP_ID_BYTES bytes) and hands it to the others out of band. */
+typedef struct vxc_tp vxc_tp;
+#define VXC_TP_ID_BYTES 128
+int vxc_tp_unique_id(void *id_out);
+int vxc_tp_create(const void *id, int rank, int world, vxc_tp **out);
+void vxc_tp_destroy(vxc_tp *tp);
+/* Upload this rank's shard of a model split over tp's GPUs (Megatron-style):
+ * rank r keeps heads [r*H/w, (r+1)*H/w) of Q, the matching KV heads, rows
+ * [r*F/w, ...) of gate/up, the matching columns of wo and wd, and rows
+ * [r*V/w, ...) of the LM head; embeddings and norms are replicated.  Each
+ * forward then sums the wo and wd outputs over the GPUs (all-reduce) and
+ * gathers the logits (all-gather), so every rank sees the full logits.
+ * H, KV heads, n_ff and n_vocab must divide by the world size.  tp == NULL
+ * is vxc_net_create.  The net borrows tp, which must outlive it. */
+int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd, const vxc_tensor_view *out_norm,
+                      const vxc_tensor_view *output, const vxc_layer_views *layers, const vxc_tp *tp,
+                      vxc_net **out);
 int vxc_net_config_get(const vxc_net *net, vxc_net_config *cfg);
 /* Device bytes of weights read by one forward pass (all matrices + norms). */
 size_t vxc_net_weight_bytes(const vxc_net *net);

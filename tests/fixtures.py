@@ -15,6 +15,8 @@ CONFIGS = {
     # config 4 shapes, fewer layers (parity at 7B width)
     "l7b_2layer": (4096, 2, 32, 32, 11008, 32000, 2, 3, 10000.0),
     "d11b_2layer": (2048, 2, 32, 4, 5632, 32000, 8, 4, 10000.0),
+    # config 5 target width (Llama-3-70B: 64/8 heads of 128, FFN 28672, vocab 128256), 2 layers
+    "l70b_2layer": (8192, 2, 64, 8, 28672, 128256, 2, 5, 500000.0),
     # config 4 full models
     "llama7b_q4": (4096, 32, 32, 32, 11008, 32000, 2, 11, 10000.0),
     "draft11b_q8": (2048, 22, 32, 4, 5632, 32000, 8, 12, 10000.0),

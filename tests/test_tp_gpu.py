@@ -1,0 +1,100 @@
+"""Configuration 5's tensor parallelism on 2 GPUs, through the public C API
+(vx_model_create_tp, vx_speculative_*): each rank is its own process
+(tests/tp_worker.py), NCCL over NVLink.
+
+- 70B width (dim 8192, 64/8 heads of 128, FFN 28672, vocab 128256, theta
+  5e5, Q4_0), 2 layers: both ranks return the same logits bit for bit
+  (they are gathered), equal to the single-GPU forward within 1e-4 x
+  max|logit| (only the fp32 summation order of the output and down
+  projections differs) and to the CPU oracle within 2e-3 x max|logit|
+  (the north_star tolerance).
+- Tiny target split over 2 GPUs, draft whole on each: speculative decoding,
+  greedy and sampled (T = 0.8, seeded Philox), emits the same tokens on both
+  ranks and as the single-GPU run.
+Skipped with fewer than 2 GPUs.
+"""
+import ctypes
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+from _paths import oracle
+import fixtures
+import tp_worker
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+f32p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+
+
+def rel_err(a, b):
+    return float(np.max(np.abs(a - b)) / np.max(np.abs(b)))
+
+
+@pytest.fixture(scope="module")
+def tp_results(cuda, tmp_path_factory):
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor parallelism needs 2 GPUs")
+    for name in ("l70b_2layer", "tiny_target", "tiny_draft"):
+        fixtures.path(name)            # written once, before the ranks start
+    out = str(tmp_path_factory.mktemp("tp"))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "tp_worker.py"), str(r), "2", out], env=env,
+                              stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+             for r in range(2)]
+    logs = []
+    for p in procs:
+        try:
+            logs.append(p.communicate(timeout=600)[0])
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            pytest.fail("tensor-parallel ranks did not finish")
+    for p, log in zip(procs, logs):
+        assert p.returncode == 0, log[-4000:]
+    return [dict(np.load(os.path.join(out, f"rank{r}.npz"))) for r in range(2)]
+
+
+def test_ranks_agree_bitwise(tp_results):
+    a, b = tp_results
+    for k in a:
+        assert np.array_equal(a[k], b[k]), k
+
+
+def test_70b_width_logits_vs_single_gpu_and_oracle(tp_results):
+    import vxb200
+    got = tp_results[0]
+    m = vxb200.Model(fixtures.path("l70b_2layer"))
+    one = [m.forward(tp_worker.PROMPT70), m.forward(tp_worker.NEXT70)]
+    m.close()
+    assert rel_err(got["l70_prefill"], one[0]) <= 1e-4
+    assert rel_err(got["l70_decode"], one[1]) <= 1e-4
+    O = oracle()
+    om = O.vxo_model_load(fixtures.path("l70b_2layer").encode(), 0)
+    want = np.zeros(128256, np.float32)
+    assert O.vxo_forward(om, f32p(tp_worker.PROMPT70), len(tp_worker.PROMPT70), f32p(want)) == 0
+    assert rel_err(got["l70_prefill"], want) <= 2e-3
+    assert O.vxo_forward(om, f32p(tp_worker.NEXT70), 1, f32p(want)) == 0
+    assert rel_err(got["l70_decode"], want) <= 2e-3
+    O.vxo_model_free(om)
+
+
+def test_spec_tokens_equal_single_gpu(tp_results):
+    import vxb200
+    got = tp_results[0]
+    t = vxb200.Model(fixtures.path("tiny_target"))
+    d = vxb200.Model(fixtures.path("tiny_draft"))
+    sp = vxb200.Speculative(d, t, 4, temp=0.0)
+    greedy = np.asarray(sp.generate(tp_worker.PROMPT_TINY, 64), np.int32)
+    sp.close()
+    sp = vxb200.Speculative(d, t, 4, temp=0.8, seed=1234)
+    sampled = np.asarray(sp.generate(tp_worker.PROMPT_TINY, 96), np.int32)
+    sp.close()
+    t.close()
+    d.close()
+    assert np.array_equal(got["tiny_greedy"], greedy)
+    assert np.array_equal(got["tiny_sampled"], sampled)

@@ -32,3 +32,12 @@ int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, 
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
 // Library-wide count of kernel launches (a CUDA-graph replay adds its kernels).
 void vxc_count_launches(long long n);
+
+// Tensor parallelism (vxc_tp.cu).  rank/world of NULL are 0/1; the exchanges
+// are enqueued on st (NCCL) and return 0 or -3 with the error set.
+int vxc_tp_rank(const vxc_tp *t);
+// GPUs a net is split over (1 without tensor parallelism).
+int vxc_net_world(const vxc_net *n);
+int vxc_tp_world(const vxc_tp *t);
+int vxc_tp_allreduce_sum(const vxc_tp *t, float *buf, size_t n, cudaStream_t st);
+int vxc_tp_allgather(const vxc_tp *t, const float *send, float *recv, size_t n, cudaStream_t st);

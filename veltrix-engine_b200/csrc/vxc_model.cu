@@ -45,6 +45,10 @@ struct vxc_net {
     vxc_layer_dev *layers;
     float2 *rope;            // [max_pos][hd/2]
     size_t weight_bytes;
+    // tensor parallelism (tp == NULL: the whole model on this GPU)
+    const vxc_tp *tp;
+    int rank, world;
+    int Hl, KHl, Fl, Vl;     // this GPU's q heads, kv heads, FFN columns, vocabulary rows
 };
 
 namespace cg = cooperative_groups;
@@ -64,6 +68,8 @@ struct vxc_seqs {
     size_t part_slot;        // floats per chunk slot
     float *attn_part;
     int attn_sl, attn_splits;
+    float *ar;               // [max_rows][E] all-reduced projection output (tensor parallel)
+    float *lg_local, *lg_all;   // local logits [rows][Vl], gathered [world][rows][Vl]
 };
 
 // queries per attention CTA: 8 when a kv head has <= 8 queries (verify rows x
@@ -578,6 +584,17 @@ __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__re
     cl.sync();
 }
 
+// logits[m][w*Vl + v] = gathered[w][m][v]: the vocabulary shards of the GPUs side by side
+__global__ void k_vocab_gather(const float *__restrict__ all, int world, int n_rows, int Vl, float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    const size_t V = (size_t)world * Vl, tot = (size_t)n_rows * V;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < tot; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t m = i / V, c = i % V, w = c / Vl, v = c % Vl;
+        out[i] = all[(w * n_rows + m) * Vl + v];
+    }
+}
+
 // logits[m][r] = sum of the LM head's partials
 __global__ void k_part_out(Part p, int n_rows, float *__restrict__ out) {
     pdl_trigger();
@@ -636,20 +653,61 @@ static int upload_fused(const vxc_tensor_view *const *parts, int n, vxc_qmat **o
 
 static size_t qmat_bytes(const vxc_qmat *w) { return w ? w->qs_bytes : 0; }
 
+// Rows [r0, r0 + n) of a GGUF matrix (a pointer offset).
+static vxc_tensor_view rows_of(const vxc_tensor_view &t, int r0, int n) {
+    vxc_tensor_view v = t;
+    v.data = (const uint8_t *)t.data + (size_t)r0 * row_bytes_of(t.type, t.cols);
+    v.rows = n;
+    return v;
+}
+
+// Columns [c0, c0 + n) (multiples of 32) of a GGUF matrix, gathered block by
+// block into `buf`.
+static vxc_tensor_view cols_of(const vxc_tensor_view &t, int c0, int n, std::vector<uint8_t> &buf) {
+    const size_t rb = row_bytes_of(t.type, t.cols), bb = rb / (t.cols / 32);
+    const size_t nb = (size_t)n / 32, b0 = (size_t)c0 / 32;
+    buf.resize((size_t)t.rows * nb * bb);
+    for (int r = 0; r < t.rows; r++)
+        memcpy(buf.data() + (size_t)r * nb * bb, (const uint8_t *)t.data + (size_t)r * rb + b0 * bb, nb * bb);
+    vxc_tensor_view v = t;
+    v.data = buf.data();
+    v.cols = n;
+    return v;
+}
+
 extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
                               const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
                               const vxc_layer_views *layers, vxc_net **out) {
+    return vxc_net_create_tp(cfg, tok_embd, out_norm, output, layers, NULL, out);
+}
+
+extern "C" int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
+                                 const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
+                                 const vxc_layer_views *layers, const vxc_tp *tp, vxc_net **out) {
     int rc = vxc_require_device();
     if (rc) return rc;
+    const int world = vxc_tp_world(tp), rank = vxc_tp_rank(tp);
     if (!cfg || !tok_embd || !tok_embd->data || !layers || !out || cfg->n_layers <= 0 || cfg->n_heads <= 0 ||
         cfg->n_kv_heads <= 0 || cfg->n_heads % cfg->n_kv_heads || cfg->n_head_dim % 32 || cfg->n_head_dim > 128 ||
         cfg->n_embd != cfg->n_heads * cfg->n_head_dim || cfg->n_embd % 32 || cfg->n_ff % 32) {
         vxc_set_error("vxc_net_create: unsupported configuration");
         return -4;
     }
+    if (cfg->n_heads % world || cfg->n_kv_heads % world || cfg->n_ff % (32 * world) || cfg->n_vocab % world) {
+        vxc_set_error("vxc_net_create: heads %d/%d, FFN %d and vocab %d must split evenly over %d GPUs",
+                      cfg->n_heads, cfg->n_kv_heads, cfg->n_ff, cfg->n_vocab, world);
+        return -4;
+    }
     vxc_net *n = (vxc_net *)calloc(1, sizeof(vxc_net));
     n->cfg = *cfg;
-    const int E = cfg->n_embd, L = cfg->n_layers;
+    n->tp = tp;
+    n->rank = rank;
+    n->world = world;
+    n->Hl = cfg->n_heads / world;
+    n->KHl = cfg->n_kv_heads / world;
+    n->Fl = cfg->n_ff / world;
+    n->Vl = cfg->n_vocab / world;
+    const int E = cfg->n_embd, L = cfg->n_layers, hd = cfg->n_head_dim;
     // embedding rows (raw)
     n->embd_type = tok_embd->type;
     n->embd_rows = tok_embd->rows;
@@ -667,7 +725,9 @@ extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *
     }
     const vxc_tensor_view *ow = (output && output->data) ? output : tok_embd;   // src/format.c:238
     {
-        const vxc_tensor_view *p[1] = {ow};
+        // tensor parallel: this GPU's vocabulary rows of the LM head
+        const vxc_tensor_view oh = rows_of(*ow, rank * n->Vl, world > 1 ? n->Vl : ow->rows);
+        const vxc_tensor_view *p[1] = {&oh};
         if ((rc = upload_fused(p, 1, &n->out))) { vxc_net_destroy(n); return rc; }
     }
     n->layers = (vxc_layer_dev *)calloc((size_t)L, sizeof(vxc_layer_dev));
@@ -677,10 +737,29 @@ extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *
         vxc_layer_dev *d = &n->layers[l];
         if ((rc = upload_f32_or_ones(&lv->attn_norm, E, &d->attn_norm)) ||
             (rc = upload_f32_or_ones(&lv->ffn_norm, E, &d->ffn_norm))) { vxc_net_destroy(n); return rc; }
-        const vxc_tensor_view *qkv[3] = {&lv->wq, &lv->wk, &lv->wv};
-        const vxc_tensor_view *o[1] = {&lv->wo};
-        const vxc_tensor_view *gu[2] = {&lv->wg, &lv->wu};
-        const vxc_tensor_view *dn[1] = {&lv->wd};
+        // tensor parallel (Megatron-style): q/k/v rows of this GPU's heads and gate/up rows of
+        // its FFN columns (column-parallel); output and down projections keep every row but
+        // only the matching input columns (row-parallel, summed over GPUs afterwards)
+        vxc_tensor_view wq = lv->wq, wk = lv->wk, wv = lv->wv, wo = lv->wo, wg = lv->wg, wu = lv->wu, wd = lv->wd;
+        std::vector<uint8_t> obuf, dbuf;
+        if (world > 1) {
+            if (!wq.data || !wk.data || !wv.data || !wo.data || !wg.data || !wu.data || !wd.data) {
+                vxc_set_error("vxc_net_create: layer %d lacks a projection the tensor-parallel split needs", l);
+                vxc_net_destroy(n);
+                return -7;
+            }
+            wq = rows_of(lv->wq, rank * n->Hl * hd, n->Hl * hd);
+            wk = rows_of(lv->wk, rank * n->KHl * hd, n->KHl * hd);
+            wv = rows_of(lv->wv, rank * n->KHl * hd, n->KHl * hd);
+            wg = rows_of(lv->wg, rank * n->Fl, n->Fl);
+            wu = rows_of(lv->wu, rank * n->Fl, n->Fl);
+            wo = cols_of(lv->wo, rank * n->Hl * hd, n->Hl * hd, obuf);
+            wd = cols_of(lv->wd, rank * n->Fl, n->Fl, dbuf);
+        }
+        const vxc_tensor_view *qkv[3] = {&wq, &wk, &wv};
+        const vxc_tensor_view *o[1] = {&wo};
+        const vxc_tensor_view *gu[2] = {&wg, &wu};
+        const vxc_tensor_view *dn[1] = {&wd};
         if ((rc = upload_fused(qkv, 3, &d->wqkv)) || (rc = upload_fused(o, 1, &d->wo)) ||
             (rc = upload_fused(gu, 2, &d->wgu)) || (rc = upload_fused(dn, 1, &d->wd))) {
             vxc_net_destroy(n);
@@ -690,7 +769,7 @@ extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *
     }
     n->weight_bytes = wb;
     // RoPE table exactly as src/tensor.c:180-187 computes it per call
-    const int hd = cfg->n_head_dim, np = hd / 2, P = cfg->max_pos > 0 ? cfg->max_pos : 4096;
+    const int np = hd / 2, P = cfg->max_pos > 0 ? cfg->max_pos : 4096;
     n->cfg.max_pos = P;
     std::vector<float2> tab((size_t)P * np);
     std::vector<float> freq(np);
@@ -709,6 +788,8 @@ extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *
     *out = n;
     return 0;
 }
+
+int vxc_net_world(const vxc_net *n) { return n ? n->world : 1; }
 
 extern "C" void vxc_net_destroy(vxc_net *n) {
     if (!n) return;
@@ -843,7 +924,8 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     s->n_slots = n_slots;
     s->max_ctx = max_ctx;
     s->max_rows = max_rows;
-    const int E = c.n_embd, kvd = c.n_kv_heads * c.n_head_dim, F = c.n_ff, hd = c.n_head_dim;
+    // this GPU's share under tensor parallelism (everything when net->tp == NULL)
+    const int E = c.n_embd, kvd = net->KHl * c.n_head_dim, F = net->Fl, hd = c.n_head_dim;
     const int nch = (max_rows + 63) / 64;
     size_t kvn = (size_t)c.n_layers * n_slots * max_ctx * kvd;
     // attention split length: at most 16 splits of >= ATTN_SL_MIN positions (whole
@@ -855,7 +937,7 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     if (SL < sl_min) SL = sl_min;
     s->attn_sl = SL;
     s->attn_splits = (max_ctx + SL - 1) / SL;
-    size_t part = (size_t)max_rows * c.n_heads * s->attn_splits * (hd + 4);
+    size_t part = (size_t)max_rows * net->Hl * s->attn_splits * (hd + 4);
     s->img_chunk = (size_t)(E > F ? E : F) / 32 * vxc_img_block_bytes(64);
     s->part_slot = part_slot_floats(net);
     cudaError_t e = cudaSuccess;
@@ -868,6 +950,11 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     ALLOC(s->xs, (size_t)nch * 64 * 4);
     ALLOC(s->part, (size_t)nch * s->part_slot * 4);
     ALLOC(s->attn_part, part * 4);
+    if (net->tp) {
+        ALLOC(s->ar, (size_t)max_rows * E * 4);
+        ALLOC(s->lg_local, (size_t)max_rows * net->Vl * 4);
+        ALLOC(s->lg_all, (size_t)net->world * max_rows * net->Vl * 4);
+    }
 #undef ALLOC
     if (e == cudaSuccess) e = cudaMemset(s->k, 0, kvn * 4);
     if (e == cudaSuccess) e = cudaMemset(s->v, 0, kvn * 4);
@@ -901,7 +988,7 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
 
 extern "C" void vxc_seqs_destroy(vxc_seqs *s) {
     if (!s) return;
-    void *ptrs[] = {s->k, s->v, s->x, s->qbuf, s->img, s->xs, s->part, s->attn_part};
+    void *ptrs[] = {s->k, s->v, s->x, s->qbuf, s->img, s->xs, s->part, s->attn_part, s->ar, s->lg_local, s->lg_all};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     free(s);
@@ -998,13 +1085,14 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     }
     const vxc_net *n = s->net;
     const vxc_net_config &c = n->cfg;
-    const int E = c.n_embd, H = c.n_heads, KH = c.n_kv_heads, hd = c.n_head_dim, F = c.n_ff;
+    // heads, kv heads and FFN columns of this GPU (all of them without tensor parallelism)
+    const int E = c.n_embd, H = n->Hl, KH = n->KHl, hd = c.n_head_dim, F = n->Fl;
     const int kvd = KH * hd;
     if (n_logit_rows > 0 && !n->out_norm) {
         vxc_set_error("vxc_forward: models without output_norm are not supported");
         return -7;
     }
-    if (n_logit_rows > 0 && n->out->rows != c.n_vocab) {
+    if (n_logit_rows > 0 && n->out->rows != n->Vl) {
         vxc_set_error("vxc_forward: LM head rows %d != vocab %d not supported", n->out->rows, c.n_vocab);
         return -7;
     }
@@ -1012,6 +1100,21 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     unsigned int *err = vxc_device_error_ptr();
     int rc;
     cudaError_t e;
+    // tensor parallel: sum a row-parallel projection's output over the GPUs
+    // (its split-K partials first summed here into s->ar), then read it as one slice
+    auto tp_sum = [&](Part &p) -> cudaError_t {
+        const size_t tot = (size_t)M * E;
+        cudaError_t er = launch_pdl(k_part_out, dim3(nblk(tot, 256) < 1184 ? nblk(tot, 256) : 1184), dim3(256), 0,
+                                    st, p, M, s->ar);
+        if (er != cudaSuccess) return er;
+        if (vxc_tp_allreduce_sum(n->tp, s->ar, tot, st)) return cudaErrorUnknown;
+        p.base = s->ar;
+        p.slot = (size_t)64 * E;
+        p.R = E;
+        p.M = M;
+        p.ks_full = p.ks_last = 1;
+        return cudaSuccess;
+    };
     cudaEvent_t pe = prof_begin(st);
     e = launch_pdl(k_embed, dim3(M), dim3(256), 0, st, n->embd, n->embd_type, n->embd_row_bytes,
                                n->embd_rows, E, d_tokens, s->x, err);
@@ -1060,6 +1163,7 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wo, M, &pp, st))) return rc;
+        if (n->tp && (e = tp_sum(pp)) != cudaSuccess) break;
         prof_end(6, pe, st);
         pe = prof_begin(st);
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, pp,
@@ -1076,6 +1180,7 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wd, M, &prev, st))) return rc;
+        if (n->tp && (e = tp_sum(prev)) != cudaSuccess) break;
         prof_end(10, pe, st);
     }
     if (e == cudaSuccess && n_logit_rows > 0) {
@@ -1087,9 +1192,16 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
                                s->xs);
         if (e == cudaSuccess) {
             if ((rc = gemv_rows(s, n->out, n_logit_rows, &pp, st))) return rc;
-            const size_t tot = (size_t)n_logit_rows * V;
+            const size_t tot = (size_t)n_logit_rows * n->Vl;
             e = launch_pdl(k_part_out, dim3(nblk(tot, 256) < 1184 ? nblk(tot, 256) : 1184), dim3(256), 0, st, pp,
-                           n_logit_rows, d_logits);
+                           n_logit_rows, n->tp ? s->lg_local : d_logits);
+            if (e == cudaSuccess && n->tp) {
+                // vocabulary-parallel LM head: gather every GPU's rows of the logits
+                if (vxc_tp_allgather(n->tp, s->lg_local, s->lg_all, tot, st)) return -3;
+                const size_t all = (size_t)n_logit_rows * V;
+                e = launch_pdl(k_vocab_gather, dim3(nblk(all, 256) < 1184 ? nblk(all, 256) : 1184), dim3(256), 0, st,
+                               (const float *)s->lg_all, n->world, n_logit_rows, n->Vl, d_logits);
+            }
         }
         prof_end(11, pe, st);
     }

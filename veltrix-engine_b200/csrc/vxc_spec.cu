@@ -711,6 +711,12 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     cudaEvent_t rev[2];
     cudaEventCreateWithFlags(&rev[0], cudaEventDisableTiming);
     cudaEventCreateWithFlags(&rev[1], cudaEventDisableTiming);
+    // Two rounds stay in flight, and the older one's count decides whether to
+    // stop; the newer round may already have written that count, so the number
+    // of rounds run can vary by one with timing.  A tensor-parallel target runs
+    // collectives in every round, which all GPUs must run equally often: there
+    // each round's own count decides, one round in flight.
+    const int depth = vxc_net_world(e->tnet) > 1 ? 1 : 2;
     int pending = 0;
     while (launched < max_new + 1) {
         err = cudaGraphLaunch(e->exec, st);
@@ -719,10 +725,10 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
         cudaEventRecord(rev[launched & 1], st);
         launched++;
         pending++;
-        if (pending == 2) {
-            // wait for the older of the two rounds in flight and read its count
-            cudaEventSynchronize(rev[launched & 1]);
-            pending = 1;
+        if (pending == depth) {
+            // wait for the oldest round in flight and read its count
+            cudaEventSynchronize(rev[(launched - depth) & 1]);
+            pending = depth - 1;
             checked++;
             if (*(volatile int *)e->h_ndone >= S) break;
         }

@@ -75,13 +75,10 @@ static int arch_supported(const char *a) {
     return 1;
 }
 
-vx_error vx_model_create(const char *path, vx_model **out) {
-    if (!path || !out) return VX_ERR_PARAM;
+/* Load `path` onto the current device; with tp != NULL only this rank's
+ * shard of the weights (the handle then owns tp). */
+static vx_error model_create(const char *path, vxc_tp *tp, vx_model **out) {
     int dev = vxc_device_current();
-    if (dev < 0 || vxc_device_init(dev) != 0) {
-        fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
-        return VX_ERR_UNSUPPORTED;
-    }
     vxh_gguf g;
     int rc = vxh_gguf_open(path, &g);
     if (rc) return (vx_error)rc;
@@ -134,7 +131,7 @@ vx_error vx_model_create(const char *path, vx_model **out) {
     nc.max_pos = 16384;
     vxc_tensor_view ve = view_of(te), vo = view_of(to), vn = view_of(tn);
     vxc_net *net = NULL;
-    rc = vxc_net_create(&nc, &ve, tn ? &vn : NULL, to ? &vo : NULL, lv, &net);
+    rc = vxc_net_create_tp(&nc, &ve, tn ? &vn : NULL, to ? &vo : NULL, lv, tp, &net);
     free(lv);
     vxh_gguf_close(&g);
     if (rc) {
@@ -144,6 +141,7 @@ vx_error vx_model_create(const char *path, vx_model **out) {
     vxb_model *m = (vxb_model *)calloc(1, sizeof(vxb_model));
     if (!m) { vxc_net_destroy(net); return VX_ERR_MEMORY; }
     m->net = net;
+    m->tp = tp;
     m->device = dev;
     vx_model_config *c = &m->pub.config;
     c->n_layers = L;
@@ -164,11 +162,40 @@ vx_error vx_model_create(const char *path, vx_model **out) {
     return VX_OK;
 }
 
+vx_error vx_model_create(const char *path, vx_model **out) {
+    if (!path || !out) return VX_ERR_PARAM;
+    int dev = vxc_device_current();
+    if (dev < 0 || vxc_device_init(dev) != 0) {
+        fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+        return VX_ERR_UNSUPPORTED;
+    }
+    return model_create(path, NULL, out);
+}
+
+vx_error vx_model_create_tp(const char *path, int rank, int world, const void *nccl_id, vx_model **out) {
+    if (!path || !out || !nccl_id || world < 1 || rank < 0 || rank >= world) return VX_ERR_PARAM;
+    int dev = vxc_device_current();
+    if (dev < 0 || vxc_device_init(dev) != 0) {
+        fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+        return VX_ERR_UNSUPPORTED;
+    }
+    vxc_tp *tp = NULL;
+    int rc = vxc_tp_create(nccl_id, rank, world, &tp);
+    if (rc) {
+        fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+        return rc == -4 ? VX_ERR_PARAM : VX_ERR_UNSUPPORTED;
+    }
+    vx_error e = model_create(path, tp, out);
+    if (e != VX_OK) vxc_tp_destroy(tp);
+    return e;
+}
+
 void vx_model_destroy(vx_model *model) {
     if (!model) return;
     vxb_model *m = vxb_of(model);
     vxc_seqs_destroy(m->seqs);
     vxc_net_destroy(m->net);
+    vxc_tp_destroy(m->tp);
     free(m);
 }
 

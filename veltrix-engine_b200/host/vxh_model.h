@@ -9,6 +9,7 @@
 typedef struct {
     vx_model pub;
     vxc_net *net;
+    vxc_tp *tp;       /* communicator of a tensor-parallel model (owned), else NULL */
     vxc_seqs *seqs;   /* one-sequence KV cache of the drop-in API, created at the first forward */
     int seqs_ctx;     /* n_ctx the cache was created with */
     int device;

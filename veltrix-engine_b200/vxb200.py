@@ -35,6 +35,10 @@ PROTOTYPES = {
     "vxc_profile_enable": (None, [ctypes.c_int]),
     "vxc_profile_read": (ctypes.c_int, [_vp, ctypes.c_int]),
     "vxc_net_create": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_vp)]),
+    "vxc_net_create_tp": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_vp)]),
+    "vxc_tp_unique_id": (ctypes.c_int, [_vp]),
+    "vxc_tp_create": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
+    "vxc_tp_destroy": (None, [_vp]),
     "vxc_net_destroy": (None, [_vp]),
     "vxc_net_config_get": (ctypes.c_int, [_vp, _vp]),
     "vxc_net_weight_bytes": (ctypes.c_size_t, [_vp]),
@@ -44,6 +48,7 @@ PROTOTYPES = {
     "vxc_forward_host": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp]),
     # model.h / veltrix.h
     "vx_model_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "vx_model_create_tp": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _vp, ctypes.POINTER(_vp)]),
     "vx_model_destroy": (None, [_vp]),
     "vx_model_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
     "vx_model_kv_truncate": (None, [_vp, ctypes.c_int]),
@@ -166,12 +171,25 @@ class Speculative:
             pass
 
 
+def tp_unique_id():
+    """NCCL unique id (128 bytes) for vx_model_create_tp, made on rank 0."""
+    buf = ctypes.create_string_buffer(128)
+    check(lib().vxc_tp_unique_id(buf), "vxc_tp_unique_id")
+    return buf.raw
+
+
 class Model:
     """vx_model handle of the B200 back end (include/model.h)."""
 
-    def __init__(self, path):
+    def __init__(self, path, tp=None):
+        """tp = (rank, world, nccl_id bytes) loads this rank's tensor-parallel shard."""
         h = _vp()
-        rc = lib().vx_model_create(path.encode(), ctypes.byref(h))
+        if tp is None:
+            rc = lib().vx_model_create(path.encode(), ctypes.byref(h))
+        else:
+            rank, world, uid = tp
+            idbuf = ctypes.create_string_buffer(bytes(uid), 128)
+            rc = lib().vx_model_create_tp(path.encode(), rank, world, idbuf, ctypes.byref(h))
         if rc != 0:
             raise VxError(f"vx_model_create({path}) = {rc}: {lib().vxc_error_string()}")
         self.h = h
