@@ -2,13 +2,13 @@
 """Benchmark of the Veltrix B200 speculative-decoding hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spec7b|q4matvec]
+                    [--workload spec7b|spec2l|spec70b|q4matvec]
 
 Prints ONE JSON line on rank 0.  For N > 1 launch it with
 torch.distributed.run (one rank per GPU, NCCL for the barrier and the
 max-over-ranks timing only).
 
-Workload `spec7b` (default; BASELINE config 4, the headline metric
+Workload `spec7b` (default; benchmark configuration 4, the headline metric
 "accepted tok/s"): a Llama-2-7B-shaped Q4_0 target and a 1.1B-shaped Q8_0
 draft (random N(0,0.02) weights written by the library's own GGUF writer),
 8 independent sequences per GPU with 512-id uniform random prompts, k = 4,
@@ -21,7 +21,15 @@ metric defines); `e2e` = the same tokens / wall time of the whole API calls
 (prompt pass, H2D and D2H included).  The KV cache of every step is far
 larger than L2 (>= 4 GB per verify), so no flush is needed.
 
-Workload `q4matvec`: Q4_0 verify matmuls 4096x4096 and
+Workload `spec70b` (benchmark configuration 5): a Llama-3-70B-shaped Q4_0 target
+(80 layers, 64/8 heads of 128, FFN 28672, vocabulary 128256, RoPE theta 5e5)
+split over the N GPUs by tensor parallelism (NCCL all-reduce after the
+output and down projections, all-gather of the vocabulary-split logits) and
+a 1B-shaped Q8_0 draft on every GPU; 32 sequences of 4096-id prompts, k = 6,
+T = 0.8 with seeded Philox sampling, 128 new tokens.  Every GPU runs every
+sequence on its shard (strong scaling); tokens are counted once.
+
+Workload `q4matvec` (benchmark configuration 2): Q4_0 verify matmuls 4096x4096 and
 11008x4096 at M = 1, 2, 5, 8 activation rows, fp32 activations and
 accumulation.  One step = one GEMV over every rotated weight copy for each of
 the 8 (shape, M) cases; the copies of each shape exceed 2x the 126 MB L2, so
@@ -286,11 +294,18 @@ def cpu_q4matvec(budget_s, threads, ship=True):
 # ---------------------------------------------------------------------------
 # spec7b
 # ---------------------------------------------------------------------------
-# (n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab, wtype, seed)
+# (n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab, wtype, seed): benchmark configuration 4
 SPEC_TARGET = (4096, 32, 32, 32, 11008, 32000, 2, 11)   # Llama-2-7B shape, Q4_0
 SPEC_DRAFT = (2048, 22, 32, 4, 5632, 32000, 8, 12)      # 1.1B shape (GQA 32/4), Q8_0
 SPEC = {"seqs_per_gpu": 8, "k": 4, "prompt": 512, "new": 256, "temp": 0.0, "seed": 1}
 # 2-layer versions of the same widths: the small case for ncu captures (well under 2 GB on the device)
+# configuration 5: Llama-3-70B-shape Q4_0 target split over the GPUs (tensor parallel,
+# NCCL all-reduce after the output and down projections), 1B-shape Q8_0 draft on every GPU
+SPEC70_TARGET = (8192, 80, 64, 8, 28672, 128256, 2, 21)
+SPEC70_DRAFT = (2048, 16, 32, 8, 8192, 128256, 8, 22)
+SPEC70 = {"seqs_per_gpu": 32, "k": 6, "prompt": 4096, "new": 128, "temp": 0.8, "seed": 1}
+ROPE_THETA = {False: 10000.0, True: 500000.0}
+TP = False   # set by --workload spec70b
 SPEC_TARGET_2L = (4096, 2, 32, 32, 11008, 32000, 2, 13)
 SPEC_DRAFT_2L = (2048, 2, 32, 4, 5632, 32000, 8, 14)
 
@@ -308,12 +323,13 @@ def model_bytes(cfg):
     return L * per_layer + q_bytes(V, E, wt)
 
 
-def fixture_dir():
+def fixture_dir(need=8 << 30):
     d = os.environ.get("VX_BENCH_DIR")
     if d:
         return d
     import shutil
-    if os.path.isdir("/dev/shm") and shutil.disk_usage("/dev/shm").free > 8 << 30:
+    if os.path.isdir("/dev/shm") and (os.path.isdir("/dev/shm/vx_bench") or
+                                      shutil.disk_usage("/dev/shm").free > need + (4 << 30)):
         return "/dev/shm/vx_bench"
     import tempfile
     return os.path.join(tempfile.gettempdir(), "vx_bench")
@@ -322,16 +338,21 @@ def fixture_dir():
 def spec_fixtures(write):
     """Paths of the two synthetic GGUFs; written once by the caller that passes write=True."""
     import vxb200
-    d = fixture_dir()
+    d = fixture_dir(model_bytes(SPEC_TARGET) + model_bytes(SPEC_DRAFT) + 2 * q_bytes(SPEC_TARGET[5], 8192, 2))
     os.makedirs(d, exist_ok=True)
     paths = []
-    names = ("target7b_q4_0", "draft1b_q8_0") if SPEC_TARGET[1] == 32 else ("target7b2l_q4_0", "draft1b2l_q8_0")
+    if TP:
+        names = ("target70b_q4_0", "draft1b70_q8_0")
+    elif SPEC_TARGET[1] == 32:
+        names = ("target7b_q4_0", "draft1b_q8_0")
+    else:
+        names = ("target7b2l_q4_0", "draft1b2l_q8_0")
     for name, c in zip(names, (SPEC_TARGET, SPEC_DRAFT)):
         p = os.path.join(d, name + ".gguf")
         if write and not os.path.exists(p):
             E, L, H, KH, F, V, wt, seed = c
             tmp = p + ".tmp%d" % os.getpid()
-            vxb200.write_synth(tmp, E, L, H, KH, F, V, wt, seed)
+            vxb200.write_synth(tmp, E, L, H, KH, F, V, wt, seed, ROPE_THETA[TP])
             os.replace(tmp, p)
         paths.append(p)
     return paths
@@ -376,10 +397,18 @@ def run_spec7b_gpu(args, ws, rank, local):
     if dist:
         dist.barrier()
     tpath, dpath = spec_fixtures(write=False)
-    target = vxb200.Model(tpath)
+    if TP:
+        # one tensor-parallel group over all GPUs: rank 0's NCCL id reaches the others
+        ids = [vxb200.tp_unique_id() if rank == 0 else None]
+        if dist:
+            dist.broadcast_object_list(ids, src=0)
+        target = vxb200.Model(tpath, tp=(rank, ws, ids[0]))
+        first, S = 0, SPEC["seqs_per_gpu"]          # every GPU runs every sequence, on its shard
+    else:
+        target = vxb200.Model(tpath)
+        first, S = shard(rank, ws, SPEC["seqs_per_gpu"])
     draft = vxb200.Model(dpath)
     k = SPEC["k"]
-    first, S = shard(rank, ws, SPEC["seqs_per_gpu"])
     sp = vxb200.Speculative(draft, target, k, temp=SPEC["temp"], seed=SPEC["seed"], seq_id_base=first)
     prompts = spec_prompts(first, S)
     new = SPEC["new"]
@@ -435,6 +464,8 @@ def run_spec7b_gpu(args, ws, rank, local):
                              [emitted, accepted, drafted, rounds, launches], "cuda")
     dec_ms, pre_ms, wall_s, v_ms_max, d_ms_max, a_ms_max = t
     emitted, accepted, drafted, rounds, launches = [int(x) for x in n]
+    if TP:   # every rank emitted the same tokens: count them once
+        emitted, accepted, drafted, rounds = [x // ws for x in (emitted, accepted, drafted, rounds)]
     h2d = S * SPEC["prompt"] * 4
     d2h = S * new * 4
     res = dict(emitted=emitted, accepted=accepted, drafted=drafted, rounds=rounds, dec_ms=dec_ms, pre_ms=pre_ms,
@@ -558,7 +589,20 @@ TRAFFIC_ATTN_PER_KV_BYTE = 0.99
 TRAFFIC_Q4_PER_WEIGHT_BYTE = 9.745e6 / 9437184
 
 
+SPEC70_METRIC = "accepted tok/s (70B-shape Q4_0 tensor-parallel spec decode)"
+
+
 def spec_config(ws):
+    if TP:
+        return {"workload": "spec70b: Llama-3-70B-shape Q4_0 target (80 layers) split over the GPUs, 1B-shape "
+                            f"Q8_0 draft on each, k={SPEC['k']}, T={SPEC['temp']} Philox sampling, "
+                            f"{SPEC['seqs_per_gpu']} sequences of {SPEC['prompt']}-id prompts, "
+                            f"{SPEC['new']} new tokens",
+                "global_seqs": SPEC["seqs_per_gpu"], "k": SPEC["k"], "prompt": SPEC["prompt"],
+                "new_tokens": SPEC["new"], "temp": SPEC["temp"],
+                "l2": "no flush: >= 20 GB of weights and KV per GPU per verify step, far above L2",
+                "parallelism": f"tp{ws}: heads, FFN columns and vocabulary split over {ws} GPU(s), "
+                               "NCCL all-reduce after the output and down projections, all-gather of the logits"}
     layers = "" if SPEC_TARGET[1] == 32 else f" ({SPEC_TARGET[1]}+{SPEC_DRAFT[1]} layers: profiling case)"
     return {"workload": "spec7b: Llama-2-7B-shape Q4_0 target + 1.1B-shape Q8_0 draft, k=4, greedy, "
                         f"512-id prompts, {SPEC['new']} new tokens" + layers,
@@ -569,6 +613,10 @@ def spec_config(ws):
 
 
 def main_spec7b(args, ws, rank, threads):
+    if args.impl == "reference" and TP:
+        print(json.dumps({"impl": "reference", "unavailable": "spec70b: the reference's CPU forward streams 39 GB "
+                          "of weights per token; only the configuration 4 sample is timed"}))
+        return
     if args.impl == "reference":
         toks, kind, sample, det = cpu_spec7b_reference(threads)
         toks *= 1.0
@@ -588,32 +636,38 @@ def main_spec7b(args, ws, rank, threads):
     e2e = r["emitted"] / r["wall_s"]
     peak, peak_kind = peaks()
     tw, dw = model_bytes(SPEC_TARGET), model_bytes(SPEC_DRAFT)
-    v_bytes = tw + r["v_kv"]
+    # bytes one GPU must move: its shard of the target (weights and KV) under tensor parallelism
+    v_bytes = (tw + r["v_kv"]) / (ws if TP else 1)
     achieved = v_bytes / (r["v_ms"] * 1e-3) / 1e9
-    rounds_per_step = r["rounds"] / max(1, ws * args.steps)
+    rounds_per_step = r["rounds"] / max(1, (1 if TP else ws) * args.steps)
     round_ms = r["dec_ms"] / args.steps / rounds_per_step
     round_bytes = v_bytes + SPEC["k"] * (dw + r["d_kv"])
     cpu = None
-    if ws == 1 and not args.no_cpu:
+    if TP:
+        traffic, traffic_note = None, "not captured for the 70B workload"
+    else:
+        traffic = int(SPEC_TARGET[1] * TRAFFIC_LAYER_NONATTN + TRAFFIC_ATTN_PER_KV_BYTE * r["v_kv"] + TRAFFIC_HEAD)
+        traffic_note = "ncu DRAM bytes of the 2-layer case's verify, scaled per layer"
+    if ws == 1 and not args.no_cpu and not TP:
         try:
             toks, kind, sample, _ = cpu_spec7b_reference(threads)
             cpu = {"value": round(toks, 4), "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample}
         except Exception as ex:   # the reference build is absent: say so, never substitute
             cpu = {"value": None, "unit": "tok/s", "cores": threads, "kind": "reference",
                    "sample": f"not run: {ex}"}
-    out = {"metric": SPEC_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+    out = {"metric": SPEC70_METRIC if TP else SPEC_METRIC, "value": round(value, 2), "unit": "tok/s",
+           "n_gpus": ws, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round((r["dec_ms"] + r["pre_ms"]) / args.steps, 3),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "higher_is_better": True, "scaling": "strong" if TP else "weak", "vs_baseline": None, "dtype": "f32",
            "data": "synthetic (random N(0,0.02) weights, uniform random prompt ids)", "config": spec_config(ws),
            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(achieved / peak, 4),
-                        "traffic": int(SPEC_TARGET[1] * TRAFFIC_LAYER_NONATTN
-                                       + TRAFFIC_ATTN_PER_KV_BYTE * r["v_kv"] + TRAFFIC_HEAD),
-                        "traffic_note": "ncu DRAM bytes of the 2-layer case's verify, scaled per layer",
+                        "traffic": traffic, "traffic_note": traffic_note,
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                         "kernel": "one (k+1)-row target verify forward (all its kernels), CUDA events on the "
-                                  "engine stream, 10 re-runs",
-                        "algorithmic_bytes": int(v_bytes), "weight_bytes": tw, "kv_bytes": int(r["v_kv"]),
+                                  "engine stream, 10 re-runs" + (", per GPU (max over GPUs)" if TP else ""),
+                        "algorithmic_bytes": int(v_bytes), "weight_bytes": tw // (ws if TP else 1),
+                        "kv_bytes": int(r["v_kv"] / (ws if TP else 1)),
                         "verify_ms": round(r["v_ms"], 4)},
            "round": {"ms": round(round_ms, 3), "roofline_ms": round(round_bytes / (peak * 1e9) * 1e3, 3),
                      "frac": round(round_bytes / (peak * 1e9) * 1e3 / round_ms, 4),
@@ -636,21 +690,27 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="spec7b", choices=["spec7b", "spec2l", "q4matvec"],
-                    help="spec2l: spec7b with 2-layer models, the small case for profilers")
+    ap.add_argument("--workload", default="spec7b", choices=["spec7b", "spec2l", "spec70b", "q4matvec"],
+                    help="spec2l: spec7b with 2-layer models, the small case for profilers; "
+                         "spec70b: configuration 5, the 70B-shape target tensor-parallel over --gpus")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--new", type=int, default=SPEC["new"], help="spec7b: new tokens per sequence")
+    ap.add_argument("--new", type=int, default=None, help="new tokens per sequence (spec workloads)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (profiling runs)")
     args = ap.parse_args()
-    SPEC["new"] = args.new
+    global SPEC_TARGET, SPEC_DRAFT, TP
+    if args.workload == "spec70b":
+        TP = True
+        SPEC_TARGET, SPEC_DRAFT = SPEC70_TARGET, SPEC70_DRAFT
+        SPEC.update(SPEC70)
+    if args.new is not None:
+        SPEC["new"] = args.new
     ws, rank, _ = dist_setup(args)
     threads = host_threads()
     if args.impl == "reference" and rank != 0:
         return   # the CPU reference runs on rank 0 only
     if args.workload == "spec2l":
-        global SPEC_TARGET, SPEC_DRAFT
         SPEC_TARGET, SPEC_DRAFT = SPEC_TARGET_2L, SPEC_DRAFT_2L
-    if args.workload in ("spec7b", "spec2l"):
+    if args.workload in ("spec7b", "spec2l", "spec70b"):
         main_spec7b(args, ws, rank, threads)
     else:
         main_q4matvec(args, ws, rank, threads)

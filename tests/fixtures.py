@@ -1,4 +1,4 @@
-"""Synthetic checkpoints of the BASELINE configurations, written by the
+"""Synthetic checkpoints of the benchmark configurations, written by the
 library's own GGUF writer (vx_synth_write_gguf) into a cache directory."""
 import os
 import tempfile

@@ -2,7 +2,7 @@
 sampler (vxc_sample_rows) against the CPU oracle, bit-exact: same accepted
 lengths, same correction/bonus tokens, same sampled tokens.
 
-Inputs follow BASELINE config 3: 64 sequences, k = 5, V = 32000, target
+Inputs follow benchmark configuration 3: 64 sequences, k = 5, V = 32000, target
 logits ~ N(0, 2^2) (k+1 rows, the last one for the bonus token), draft
 logits = target + N(0, 0.5^2), temperature 0.8, draft tokens drawn from q
 with the same Philox stream (purpose DRAFT)."""

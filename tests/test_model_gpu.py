@@ -2,7 +2,7 @@
 (vx_model_create / vx_model_forward) against the reference goldens and the
 CPU oracle.
 
-Tolerance: logits within 2e-3 * max|logit|; greedy
+Tolerance (the benchmark definition): logits within 2e-3 * max|logit|; greedy
 tokens identical wherever the reference's top-2 margin exceeds 1e-3.
 """
 import ctypes

@@ -7,7 +7,7 @@
   (they are gathered), equal to the single-GPU forward within 1e-4 x
   max|logit| (only the fp32 summation order of the output and down
   projections differs) and to the CPU oracle within 2e-3 x max|logit|
-  (the north_star tolerance).
+  (the benchmark definition).
 - Tiny target split over 2 GPUs, draft whole on each: speculative decoding,
   greedy and sampled (T = 0.8, seeded Philox), emits the same tokens on both
   ranks and as the single-GPU run.
