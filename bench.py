@@ -180,6 +180,7 @@ def run_q4matvec_gpu(args, ws, rank, local):
 
     for _ in range(args.warmup):
         step()
+        progress("warm-up step done")
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -392,8 +393,15 @@ def run_spec7b_gpu(args, ws, rank, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900),
                                 device_id=torch.device("cuda", local))
+    t_start = time.time()
+
+    def progress(what):
+        if rank == 0:
+            print(f"[bench] {time.time() - t_start:7.1f} s  {what}", file=sys.stderr, flush=True)
+
     if local == 0:
         spec_fixtures(write=True)
+    progress("checkpoints written")
     if dist:
         dist.barrier()
     tpath, dpath = spec_fixtures(write=False)
@@ -408,6 +416,7 @@ def run_spec7b_gpu(args, ws, rank, local):
         target = vxb200.Model(tpath)
         first, S = shard(rank, ws, SPEC["seqs_per_gpu"])
     draft = vxb200.Model(dpath)
+    progress("models loaded")
     k = SPEC["k"]
     sp = vxb200.Speculative(draft, target, k, temp=SPEC["temp"], seed=SPEC["seed"], seq_id_base=first)
     prompts = spec_prompts(first, S)
@@ -422,6 +431,7 @@ def run_spec7b_gpu(args, ws, rank, local):
 
     for _ in range(args.warmup):
         step()
+        progress("warm-up step done")
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -445,6 +455,7 @@ def run_spec7b_gpu(args, ws, rank, local):
     if dist:
         dist.barrier()
     clocks = clk.stop()
+    progress("timed steps done")
     # per-piece device time of the last round (verify forward, draft step, acceptance)
     v_ms, v_kv = sp.probe(0, 10)
     d_ms, d_kv = sp.probe(1, 10)

@@ -1,6 +1,7 @@
 /* vxh_synth.c — synthetic llama-architecture GGUF writer (see veltrix_synth.h). */
 #define _GNU_SOURCE
 #include <math.h>
+#include <omp.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -155,7 +156,10 @@ int vx_synth_write_gguf(const char *path, const vx_synth_config *c, uint64_t see
         } else {
             const int64_t nblk = (int64_t)(t[i].ne0 * t[i].ne1 / 32);
             const size_t bb = t[i].type == 8 ? 34 : 18;
-#pragma omp parallel for schedule(static)
+            /* every core the process may run on, whatever OMP_NUM_THREADS says
+             * (launchers such as torch.distributed.run set it to 1): a 70B-shape
+             * checkpoint is ~70 G normals */
+#pragma omp parallel for schedule(static) num_threads(omp_get_num_procs())
             for (int64_t b = 0; b < nblk; b++) {
                 float x[32];
                 for (int q = 0; q < 8; q++) normals4(seed, (uint32_t)i, (uint64_t)b * 8 + q, 0.02f, x + 4 * q);
