@@ -152,6 +152,14 @@ void vxc_tp_destroy(vxc_tp *tp);
 int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd, const vxc_tensor_view *out_norm,
                       const vxc_tensor_view *output, const vxc_layer_views *layers, const vxc_tp *tp,
                       vxc_net **out);
+/* A net whose weights are generated on the device: N(0, 0.02) from
+ * Philox4x32-10 keyed by (seed, tensor, element) and quantised to `wtype`
+ * (2 Q4_0, 8 Q8_0), norms 1.0 -- the weights vx_synth_write_gguf would
+ * write for the same configuration and seed, up to the device's rounding of
+ * double-precision log/sqrt/cos/sin.  With tp, only this GPU's shard is
+ * generated.  For timing runs of shapes whose checkpoint files would be tens
+ * of GB. */
+int vxc_net_create_synth(const vxc_net_config *cfg, int wtype, uint64_t seed, const vxc_tp *tp, vxc_net **out);
 int vxc_net_config_get(const vxc_net *net, vxc_net_config *cfg);
 /* Device bytes of weights read by one forward pass (all matrices + norms). */
 size_t vxc_net_weight_bytes(const vxc_net *net);

@@ -14,6 +14,8 @@
 
 #include <stdint.h>
 
+#include "veltrix.h"
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -26,6 +28,14 @@ typedef struct {
 
 /* Writes `path`; returns 0 or a vx_error code. */
 int vx_synth_write_gguf(const char *path, const vx_synth_config *cfg, uint64_t seed);
+
+/* The same model created on the current device without a file: the weights
+ * are generated in device memory (up to the device's rounding of
+ * double-precision log/sqrt/cos/sin, the numbers the writer puts in the
+ * file).  world == 1 and nccl_id == NULL load the whole model; otherwise
+ * this rank's tensor-parallel shard, as vx_model_create_tp (model.h). */
+vx_error vx_model_create_synth(const vx_synth_config *cfg, uint64_t seed, int rank, int world,
+                               const void *nccl_id, vx_model **model);
 
 #ifdef __cplusplus
 }

@@ -8,6 +8,8 @@
   max|logit| (only the fp32 summation order of the output and down
   projections differs) and to the CPU oracle within 2e-3 x max|logit|
   (the benchmark definition).
+- The same 70B-width shards generated on each GPU (vx_model_create_synth)
+  give the file's logits to 1e-5 x max|logit|.
 - Tiny target split over 2 GPUs, draft whole on each: speculative decoding,
   greedy and sampled (T = 0.8, seeded Philox), emits the same tokens on both
   ranks and as the single-GPU run.
@@ -81,6 +83,12 @@ def test_70b_width_logits_vs_single_gpu_and_oracle(tp_results):
     assert O.vxo_forward(om, f32p(tp_worker.NEXT70), 1, f32p(want)) == 0
     assert rel_err(got["l70_decode"], want) <= 2e-3
     O.vxo_model_free(om)
+
+
+def test_device_generated_shards_match_file(tp_results):
+    got = tp_results[0]
+    a, b = got["l70_prefill"], got["l70_synth_prefill"]
+    assert float(np.max(np.abs(a - b))) <= 1e-5 * float(np.max(np.abs(a)))
 
 
 def test_spec_tokens_equal_single_gpu(tp_results):

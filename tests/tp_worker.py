@@ -46,11 +46,15 @@ def unique_ids(rank, out, n=2, wait_s=120.0):
 def main():
     rank, world, out = int(sys.argv[1]), int(sys.argv[2]), sys.argv[3]
     vxb200.check(vxb200.lib().vxc_device_init(rank), "vxc_device_init")
-    uid70, uidt = unique_ids(rank, out)
+    uid70, uidt, uids = unique_ids(rank, out, n=3)
     res = {}
     m = vxb200.Model(fixtures.path("l70b_2layer"), tp=(rank, world, uid70))
     res["l70_prefill"] = m.forward(PROMPT70)
     res["l70_decode"] = m.forward(NEXT70)
+    m.close()
+    # the same shard generated on the device instead of read from the file
+    m = vxb200.Model(None, tp=(rank, world, uids), synth=fixtures.CONFIGS["l70b_2layer"])
+    res["l70_synth_prefill"] = m.forward(PROMPT70)
     m.close()
     t = vxb200.Model(fixtures.path("tiny_target"), tp=(rank, world, uidt))
     d = vxb200.Model(fixtures.path("tiny_draft"))

@@ -68,20 +68,83 @@ __global__ void k_repack_q8_0(const uint8_t *__restrict__ src, uint8_t *__restri
     for (int j = 0; j < 32; j++) dst[j] = blk[2 + j];
 }
 
-// wshift such that max|d| * qmax * 2^wshift <= 2^14 over the whole matrix.
-static int choose_wshift(int type, const uint8_t *blocks, size_t nblocks) {
-    const size_t bs = type == 2 ? 18 : 34;
-    uint16_t mx = 0;
-    for (size_t i = 0; i < nblocks; i++) {
-        uint16_t h = (uint16_t)((blocks[i * bs] | (blocks[i * bs + 1] << 8)) & 0x7FFF);
-        if (h < 0x7C00 && h > mx) mx = h;   // finite magnitudes order like their bits
+// Largest finite |d| of a matrix's blocks, as fp16 bits (finite magnitudes
+// order like their bits).
+__global__ void k_max_scale_bits(const uint8_t *__restrict__ blocks, long long nblocks, int bs,
+                                 unsigned int *__restrict__ out) {
+    unsigned int mx = 0;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < nblocks;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint8_t *b = blocks + (size_t)i * bs;
+        const unsigned int h = (unsigned int)(b[0] | (b[1] << 8)) & 0x7FFFu;
+        if (h < 0x7C00u && h > mx) mx = h;
     }
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    if ((threadIdx.x & 31) == 0 && mx) atomicMax(out, mx);
+}
+
+// wshift such that max|d| * qmax * 2^wshift <= 2^14 over the whole matrix.
+static int wshift_of(int type, unsigned int mx) {
     if (mx == 0) return 0;
-    const float maxd = __half2float(__ushort_as_half(mx));
+    const float maxd = __half2float(__ushort_as_half((unsigned short)mx));
     int e;
     frexpf(maxd * (type == 2 ? 8.0f : 128.0f), &e);
     int S = 14 - e;
     return S < -60 ? -60 : S > 60 ? 60 : S;
+}
+
+int vxc_qmat_from_device(int type, const uint8_t *dev_blocks, int rows, int cols, vxc_qmat **out) {
+    if (!out || !dev_blocks || rows <= 0 || cols <= 0 || (cols % 32) != 0 || (type != 2 && type != 8)) {
+        vxc_set_error("vxc_qmat_create: bad arguments (type %d, %d x %d)", type, rows, cols);
+        return -4;
+    }
+    vxc_qmat *w = (vxc_qmat *)calloc(1, sizeof(vxc_qmat));
+    if (!w) { vxc_set_error("vxc_qmat_create: out of host memory"); return -3; }
+    w->type = type;
+    w->rows = rows;
+    w->cols = cols;
+    w->nblk = cols / 32;
+    w->ntile = (rows + VXC_TILE_ROWS - 1) / VXC_TILE_ROWS;
+    w->qb = type == 2 ? 16 : 32;
+    w->rec = VXC_TILE_ROWS * w->qb + 256;
+    w->qs_bytes = (size_t)w->ntile * w->nblk * w->rec;
+    const long long total = (long long)rows * w->nblk;
+    unsigned int *d_mx = NULL, mx = 0;
+    cudaError_t e = cudaMalloc((void **)&d_mx, sizeof(unsigned int));
+    if (e == cudaSuccess) e = cudaMemset(d_mx, 0, sizeof(unsigned int));
+    if (e == cudaSuccess) {
+        const long long want = (total + 255) / 256;
+        k_max_scale_bits<<<(unsigned)(want < 4 * 148 ? want : 4 * 148), 256>>>(dev_blocks, total,
+                                                                                type == 2 ? 18 : 34, d_mx);
+        vxc_count_launches(1);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(&mx, d_mx, sizeof mx, cudaMemcpyDeviceToHost);
+    if (d_mx) cudaFree(d_mx);
+    w->wshift = wshift_of(type, mx);
+    w->wscale = ldexpf(1.0f, -w->wshift);
+    if (e == cudaSuccess) e = cudaMalloc((void **)&w->qs, w->qs_bytes);
+    if (e == cudaSuccess) e = cudaMemset(w->qs, 0, w->qs_bytes);
+    if (e == cudaSuccess) {
+        int th = 256;
+        unsigned gb = (unsigned)((total + th - 1) / th);
+        const float mul = ldexpf(1.0f, w->wshift);
+        if (type == 2) (k_repack_q4_0<<<gb, th>>>(dev_blocks, w->qs, rows, w->nblk, mul), vxc_count_launches(1));
+        else (k_repack_q8_0<<<gb, th>>>(dev_blocks, w->qs, rows, w->nblk, mul), vxc_count_launches(1));
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        vxc_set_error("vxc_qmat_create: %s", cudaGetErrorString(e));
+        vxc_qmat_destroy(w);
+        return -3;
+    }
+    *out = w;
+    return 0;
 }
 
 extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out) {
@@ -91,41 +154,18 @@ extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int 
     }
     int rc = vxc_require_device();
     if (rc) return rc;
-    vxc_qmat *w = (vxc_qmat *)calloc(1, sizeof(vxc_qmat));
-    w->type = type;
-    w->rows = rows;
-    w->cols = cols;
-    w->nblk = cols / 32;
-    w->ntile = (rows + VXC_TILE_ROWS - 1) / VXC_TILE_ROWS;
-    w->qb = type == 2 ? 16 : 32;
-    w->rec = VXC_TILE_ROWS * w->qb + 256;
-    w->wshift = choose_wshift(type, (const uint8_t *)host_blocks, (size_t)rows * w->nblk);
-    w->wscale = ldexpf(1.0f, -w->wshift);
-    w->qs_bytes = (size_t)w->ntile * w->nblk * w->rec;
-    size_t src_bytes = (size_t)rows * w->nblk * (type == 2 ? 18 : 34);
+    const size_t src_bytes = (size_t)rows * (cols / 32) * (type == 2 ? 18 : 34);
     uint8_t *staging = NULL;
-    cudaError_t e = cudaMalloc((void **)&w->qs, w->qs_bytes);
-    if (e == cudaSuccess) e = cudaMalloc((void **)&staging, src_bytes);
-    if (e == cudaSuccess) e = cudaMemset(w->qs, 0, w->qs_bytes);
+    cudaError_t e = cudaMalloc((void **)&staging, src_bytes);
     if (e == cudaSuccess) e = cudaMemcpy(staging, host_blocks, src_bytes, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) {
-        long long total = (long long)rows * w->nblk;
-        int th = 256;
-        unsigned gb = (unsigned)((total + th - 1) / th);
-        const float mul = ldexpf(1.0f, w->wshift);
-        if (type == 2) (k_repack_q4_0<<<gb, th>>>(staging, w->qs, rows, w->nblk, mul), vxc_count_launches(1));
-        else (k_repack_q8_0<<<gb, th>>>(staging, w->qs, rows, w->nblk, mul), vxc_count_launches(1));
-        e = cudaGetLastError();
-    }
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (staging) cudaFree(staging);
     if (e != cudaSuccess) {
+        if (staging) cudaFree(staging);
         vxc_set_error("vxc_qmat_create: %s", cudaGetErrorString(e));
-        vxc_qmat_destroy(w);
         return -3;
     }
-    *out = w;
-    return 0;
+    rc = vxc_qmat_from_device(type, staging, rows, cols, out);
+    cudaFree(staging);
+    return rc;
 }
 
 extern "C" void vxc_qmat_destroy(vxc_qmat *w) {

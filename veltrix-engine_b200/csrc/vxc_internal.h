@@ -14,6 +14,16 @@ int vxc_launch_splitk_reduce(const float *ws, int ks, int M, int R, float *y, cu
 // Activation image of x[M][K] (layout in vxc_qmat.cuh) and its prescales xs[M].
 int vxc_launch_act_image(const float *x, int M, int K, uint8_t *img, float *xs, cudaStream_t st);
 
+// A quantised matrix from GGUF blocks already in device memory (row-major,
+// rows x cols/32 blocks); the blocks are only read.
+int vxc_qmat_from_device(int type, const uint8_t *dev_blocks, int rows, int cols, vxc_qmat **out);
+
+// Synthetic GGUF blocks of tensor ti (vxc_synth.cu): rows row0.. and column
+// blocks blk0.. of a tensor whose rows hold nblk_full blocks, row-major into
+// dev_out.  Enqueued on the legacy default stream.
+int vxc_synth_blocks(int type, uint64_t seed, uint32_t ti, long long row0, int nrows, int nblk_full, int blk0,
+                     int nblk, uint8_t *dev_out);
+
 // Tensor-core GEMV plan for M <= 64 activation rows (vxc_gemv_tc.cu).
 struct VxcGemvPlan {
     int nt;       // N / 16 (N = padded rows of the image)

@@ -622,73 +622,161 @@ static int upload_f32_or_ones(const vxc_tensor_view *t, int n, float **out) {
     return 0;
 }
 
-// Concatenate matrices by rows (same type and cols) and upload as one qmat.
-static int upload_fused(const vxc_tensor_view *const *parts, int n, vxc_qmat **out) {
-    int type = parts[0]->type, cols = parts[0]->cols, rows = 0;
+static size_t qmat_bytes(const vxc_qmat *w) { return w ? w->qs_bytes : 0; }
+
+// Where a net's weights come from.  Tensors are numbered as in the GGUF files
+// this library writes: 9 per layer (attn_norm, q, k, v, output, ffn_norm,
+// gate, up, down), then token_embd (9L), output_norm (9L + 1) and the LM head
+// (9L + 2).
+struct NetSource {
+    virtual ~NetSource() {}
+    // GGUF type (0 F32, 2 Q4_0, 8 Q8_0), rows and cols; type -1 when absent
+    virtual void shape(int ti, int *type, int *rows, int *cols) const = 0;
+    // rows [r0, r0 + nr) x column blocks [b0, b0 + nb) of a Q4_0/Q8_0 tensor
+    // as GGUF blocks in device memory (row-major); 0 or an error code
+    virtual int blocks(int ti, int r0, int nr, int b0, int nb, uint8_t *dev) const = 0;
+    // fp32 vector of n weights, NULL when absent (ones)
+    virtual const vxc_tensor_view *f32(int ti) const = 0;
+    // the token-embedding table in its GGUF type, rows x row_bytes at dev
+    virtual int embedding(uint8_t *dev) const = 0;
+};
+
+static size_t block_bytes(int type) { return type == 2 ? 18 : 34; }
+
+// Weights in host memory (GGUF views, e.g. an mmap'd file).
+struct HostSource : NetSource {
+    const vxc_tensor_view *tok, *onorm, *output;
+    const vxc_layer_views *layers;
+    int L;
+    const vxc_tensor_view *view(int ti) const {
+        if (ti == 9 * L) return tok;
+        if (ti == 9 * L + 1) return onorm;
+        if (ti == 9 * L + 2) return (output && output->data) ? output : tok;   // tied head, src/format.c:238
+        const vxc_layer_views &v = layers[ti / 9];
+        const vxc_tensor_view *all[9] = {&v.attn_norm, &v.wq, &v.wk, &v.wv, &v.wo, &v.ffn_norm, &v.wg, &v.wu, &v.wd};
+        return all[ti % 9];
+    }
+    void shape(int ti, int *type, int *rows, int *cols) const override {
+        const vxc_tensor_view *t = view(ti);
+        *type = (t && t->data) ? t->type : -1;
+        *rows = t ? t->rows : 0;
+        *cols = t ? t->cols : 0;
+    }
+    int blocks(int ti, int r0, int nr, int b0, int nb, uint8_t *dev) const override {
+        const vxc_tensor_view *t = view(ti);
+        const size_t bb = block_bytes(t->type), nbf = (size_t)t->cols / 32, rb = nbf * bb;
+        const uint8_t *src = (const uint8_t *)t->data;
+        cudaError_t e;
+        if (b0 == 0 && (size_t)nb == nbf) {
+            e = cudaMemcpy(dev, src + (size_t)r0 * rb, (size_t)nr * rb, cudaMemcpyHostToDevice);
+        } else {
+            // a column slice: gather the blocks of each row
+            std::vector<uint8_t> buf((size_t)nr * nb * bb);
+            for (int r = 0; r < nr; r++)
+                memcpy(buf.data() + (size_t)r * nb * bb, src + (size_t)(r0 + r) * rb + (size_t)b0 * bb,
+                       (size_t)nb * bb);
+            e = cudaMemcpy(dev, buf.data(), buf.size(), cudaMemcpyHostToDevice);
+        }
+        if (e != cudaSuccess) { vxc_set_error("weight upload: %s", cudaGetErrorString(e)); return -3; }
+        return 0;
+    }
+    const vxc_tensor_view *f32(int ti) const override {
+        const vxc_tensor_view *t = view(ti);
+        return (t && t->data) ? t : NULL;
+    }
+    int embedding(uint8_t *dev) const override {
+        const size_t eb = row_bytes_of(tok->type, tok->cols) * tok->rows;
+        if (cudaMemcpy(dev, tok->data, eb, cudaMemcpyHostToDevice) != cudaSuccess) {
+            vxc_set_error("vxc_net_create: embedding upload failed");
+            return -3;
+        }
+        return 0;
+    }
+};
+
+// Weights generated on the device (vxc_synth.cu), as the GGUF writer would
+// have written them for this configuration and seed.
+struct SynthSource : NetSource {
+    vxc_net_config c;
+    int wtype;
+    uint64_t seed;
+    void shape(int ti, int *type, int *rows, int *cols) const override {
+        const int L = c.n_layers, E = c.n_embd, kvd = c.n_kv_heads * c.n_head_dim, F = c.n_ff;
+        if (ti >= 9 * L) {
+            const int k = ti - 9 * L;
+            *type = k == 1 ? 0 : wtype;
+            *rows = k == 1 ? 1 : c.n_vocab;
+            *cols = E;
+            return;
+        }
+        const int k = ti % 9;
+        static const int rows_kind[9] = {0, 1, 2, 2, 1, 0, 3, 3, 1};   // 0 norm, 1 E, 2 kvd, 3 F
+        const int rk = rows_kind[k];
+        *type = rk == 0 ? 0 : wtype;
+        *rows = rk == 0 ? 1 : rk == 1 ? E : rk == 2 ? kvd : F;
+        *cols = k == 8 ? F : E;
+    }
+    int blocks(int ti, int r0, int nr, int b0, int nb, uint8_t *dev) const override {
+        int type, rows, cols;
+        shape(ti, &type, &rows, &cols);
+        return vxc_synth_blocks(type, seed, (uint32_t)ti, r0, nr, cols / 32, b0, nb, dev);
+    }
+    const vxc_tensor_view *f32(int) const override { return NULL; }
+    int embedding(uint8_t *dev) const override {
+        return vxc_synth_blocks(wtype, seed, (uint32_t)(9 * c.n_layers), 0, c.n_vocab, c.n_embd / 32, 0,
+                                c.n_embd / 32, dev);
+    }
+};
+
+// Slice of one tensor inside a fused matrix: rows [r0, r0 + nr), column
+// blocks [b0, b0 + nb).
+struct Piece {
+    int ti, r0, nr, b0, nb;
+};
+
+// Concatenate pieces by rows (same type, same number of column blocks) and
+// build one device matrix from them.
+static int upload_pieces(const NetSource &src, const Piece *p, int n, vxc_qmat **out) {
+    int type = -1, rows = 0;
     for (int i = 0; i < n; i++) {
-        if (!parts[i]->data || parts[i]->type != type || parts[i]->cols != cols) {
+        int t, r, c;
+        src.shape(p[i].ti, &t, &r, &c);
+        if (t < 0) { vxc_set_error("fused matrix parts differ in type/shape or are missing"); return -7; }
+        if (t != 2 && t != 8) {
+            vxc_set_error("weight type %d not supported on the device (Q4_0 / Q8_0 only)", t);
+            return -7;
+        }
+        if ((i > 0 && (t != type || p[i].nb != p[0].nb)) || p[i].r0 + p[i].nr > r || p[i].b0 + p[i].nb > c / 32) {
             vxc_set_error("fused matrix parts differ in type/shape or are missing");
             return -7;
         }
-        rows += parts[i]->rows;
+        type = t;
+        rows += p[i].nr;
     }
-    if (type != 2 && type != 8) {
-        vxc_set_error("weight type %d not supported on the device (Q4_0 / Q8_0 only)", type);
-        return -7;
+    const size_t bb = block_bytes(type);
+    uint8_t *staging = NULL;
+    if (cudaMalloc((void **)&staging, (size_t)rows * p[0].nb * bb) != cudaSuccess) {
+        vxc_set_error("vxc_net_create: out of device memory");
+        return -3;
     }
-    size_t rb = row_bytes_of(type, cols);
-    std::vector<uint8_t> buf;
-    const void *src = parts[0]->data;
-    if (n > 1) {
-        buf.resize(rb * rows);
-        size_t off = 0;
-        for (int i = 0; i < n; i++) {
-            memcpy(buf.data() + off, parts[i]->data, rb * parts[i]->rows);
-            off += rb * parts[i]->rows;
-        }
-        src = buf.data();
+    int rc = 0;
+    size_t off = 0;
+    for (int i = 0; i < n && rc == 0; i++) {
+        rc = src.blocks(p[i].ti, p[i].r0, p[i].nr, p[i].b0, p[i].nb, staging + off);
+        off += (size_t)p[i].nr * p[i].nb * bb;
     }
-    return vxc_qmat_create(type, src, rows, cols, out);
+    if (rc == 0) rc = vxc_qmat_from_device(type, staging, rows, p[0].nb * 32, out);
+    cudaFree(staging);
+    return rc;
 }
 
-static size_t qmat_bytes(const vxc_qmat *w) { return w ? w->qs_bytes : 0; }
-
-// Rows [r0, r0 + n) of a GGUF matrix (a pointer offset).
-static vxc_tensor_view rows_of(const vxc_tensor_view &t, int r0, int n) {
-    vxc_tensor_view v = t;
-    v.data = (const uint8_t *)t.data + (size_t)r0 * row_bytes_of(t.type, t.cols);
-    v.rows = n;
-    return v;
-}
-
-// Columns [c0, c0 + n) (multiples of 32) of a GGUF matrix, gathered block by
-// block into `buf`.
-static vxc_tensor_view cols_of(const vxc_tensor_view &t, int c0, int n, std::vector<uint8_t> &buf) {
-    const size_t rb = row_bytes_of(t.type, t.cols), bb = rb / (t.cols / 32);
-    const size_t nb = (size_t)n / 32, b0 = (size_t)c0 / 32;
-    buf.resize((size_t)t.rows * nb * bb);
-    for (int r = 0; r < t.rows; r++)
-        memcpy(buf.data() + (size_t)r * nb * bb, (const uint8_t *)t.data + (size_t)r * rb + b0 * bb, nb * bb);
-    vxc_tensor_view v = t;
-    v.data = buf.data();
-    v.cols = n;
-    return v;
-}
-
-extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
-                              const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
-                              const vxc_layer_views *layers, vxc_net **out) {
-    return vxc_net_create_tp(cfg, tok_embd, out_norm, output, layers, NULL, out);
-}
-
-extern "C" int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
-                                 const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
-                                 const vxc_layer_views *layers, const vxc_tp *tp, vxc_net **out) {
+// Build a net from a weight source; tp != NULL keeps this GPU's shard only.
+static int net_build(const vxc_net_config *cfg, const NetSource &src, const vxc_tp *tp, vxc_net **out) {
     int rc = vxc_require_device();
     if (rc) return rc;
     const int world = vxc_tp_world(tp), rank = vxc_tp_rank(tp);
-    if (!cfg || !tok_embd || !tok_embd->data || !layers || !out || cfg->n_layers <= 0 || cfg->n_heads <= 0 ||
-        cfg->n_kv_heads <= 0 || cfg->n_heads % cfg->n_kv_heads || cfg->n_head_dim % 32 || cfg->n_head_dim > 128 ||
+    if (!cfg || !out || cfg->n_layers <= 0 || cfg->n_heads <= 0 || cfg->n_kv_heads <= 0 ||
+        cfg->n_heads % cfg->n_kv_heads || cfg->n_head_dim % 32 || cfg->n_head_dim > 128 ||
         cfg->n_embd != cfg->n_heads * cfg->n_head_dim || cfg->n_embd % 32 || cfg->n_ff % 32) {
         vxc_set_error("vxc_net_create: unsupported configuration");
         return -4;
@@ -696,6 +784,13 @@ extern "C" int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_vie
     if (cfg->n_heads % world || cfg->n_kv_heads % world || cfg->n_ff % (32 * world) || cfg->n_vocab % world) {
         vxc_set_error("vxc_net_create: heads %d/%d, FFN %d and vocab %d must split evenly over %d GPUs",
                       cfg->n_heads, cfg->n_kv_heads, cfg->n_ff, cfg->n_vocab, world);
+        return -4;
+    }
+    const int E = cfg->n_embd, L = cfg->n_layers, hd = cfg->n_head_dim;
+    int et, er, ec;
+    src.shape(9 * L, &et, &er, &ec);
+    if (et < 0 || ec != E || er <= 0) {
+        vxc_set_error("vxc_net_create: token embedding missing or not %d wide", E);
         return -4;
     }
     vxc_net *n = (vxc_net *)calloc(1, sizeof(vxc_net));
@@ -707,61 +802,75 @@ extern "C" int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_vie
     n->KHl = cfg->n_kv_heads / world;
     n->Fl = cfg->n_ff / world;
     n->Vl = cfg->n_vocab / world;
-    const int E = cfg->n_embd, L = cfg->n_layers, hd = cfg->n_head_dim;
-    // embedding rows (raw)
-    n->embd_type = tok_embd->type;
-    n->embd_rows = tok_embd->rows;
-    n->embd_cols = tok_embd->cols;
-    n->embd_row_bytes = row_bytes_of(tok_embd->type, tok_embd->cols);
-    size_t eb = n->embd_row_bytes * tok_embd->rows;
-    if (cudaMalloc((void **)&n->embd, eb) != cudaSuccess ||
-        cudaMemcpy(n->embd, tok_embd->data, eb, cudaMemcpyHostToDevice) != cudaSuccess) {
+    // embedding rows (raw GGUF, every GPU)
+    n->embd_type = et;
+    n->embd_rows = er;
+    n->embd_cols = ec;
+    n->embd_row_bytes = row_bytes_of(et, ec);
+    if (cudaMalloc((void **)&n->embd, n->embd_row_bytes * er) != cudaSuccess) {
         vxc_set_error("vxc_net_create: embedding upload failed");
         vxc_net_destroy(n);
         return -3;
     }
-    if (out_norm && out_norm->data) {
-        if ((rc = upload_f32_or_ones(out_norm, E, &n->out_norm))) { vxc_net_destroy(n); return rc; }
+    if ((rc = src.embedding(n->embd))) { vxc_net_destroy(n); return rc; }
+    {
+        int t, r, c;
+        src.shape(9 * L + 1, &t, &r, &c);
+        if (t >= 0 && (rc = upload_f32_or_ones(src.f32(9 * L + 1), E, &n->out_norm))) {
+            vxc_net_destroy(n);
+            return rc;
+        }
     }
-    const vxc_tensor_view *ow = (output && output->data) ? output : tok_embd;   // src/format.c:238
     {
         // tensor parallel: this GPU's vocabulary rows of the LM head
-        const vxc_tensor_view oh = rows_of(*ow, rank * n->Vl, world > 1 ? n->Vl : ow->rows);
-        const vxc_tensor_view *p[1] = {&oh};
-        if ((rc = upload_fused(p, 1, &n->out))) { vxc_net_destroy(n); return rc; }
+        int t, r, c;
+        src.shape(9 * L + 2, &t, &r, &c);
+        const Piece p = {9 * L + 2, world > 1 ? rank * n->Vl : 0, world > 1 ? n->Vl : r, 0, c / 32};
+        if ((rc = upload_pieces(src, &p, 1, &n->out))) { vxc_net_destroy(n); return rc; }
     }
     n->layers = (vxc_layer_dev *)calloc((size_t)L, sizeof(vxc_layer_dev));
     size_t wb = qmat_bytes(n->out) + (size_t)E * 4;
     for (int l = 0; l < L; l++) {
-        const vxc_layer_views *lv = &layers[l];
         vxc_layer_dev *d = &n->layers[l];
-        if ((rc = upload_f32_or_ones(&lv->attn_norm, E, &d->attn_norm)) ||
-            (rc = upload_f32_or_ones(&lv->ffn_norm, E, &d->ffn_norm))) { vxc_net_destroy(n); return rc; }
-        // tensor parallel (Megatron-style): q/k/v rows of this GPU's heads and gate/up rows of
-        // its FFN columns (column-parallel); output and down projections keep every row but
-        // only the matching input columns (row-parallel, summed over GPUs afterwards)
-        vxc_tensor_view wq = lv->wq, wk = lv->wk, wv = lv->wv, wo = lv->wo, wg = lv->wg, wu = lv->wu, wd = lv->wd;
-        std::vector<uint8_t> obuf, dbuf;
+        const int t0 = 9 * l;
+        if ((rc = upload_f32_or_ones(src.f32(t0 + 0), E, &d->attn_norm)) ||
+            (rc = upload_f32_or_ones(src.f32(t0 + 5), E, &d->ffn_norm))) { vxc_net_destroy(n); return rc; }
+        int ty[9], rw[9], cl[9];
+        for (int k = 1; k < 9; k++) src.shape(t0 + k, &ty[k], &rw[k], &cl[k]);
+        // whole tensors on one GPU; tensor parallel (Megatron-style): q/k/v rows of this GPU's
+        // heads and gate/up rows of its FFN columns (column-parallel); output and down
+        // projections keep every row but only the matching input columns (row-parallel,
+        // summed over the GPUs afterwards)
+        Piece qkv[3] = {{t0 + 1, 0, rw[1], 0, cl[1] / 32}, {t0 + 2, 0, rw[2], 0, cl[2] / 32},
+                        {t0 + 3, 0, rw[3], 0, cl[3] / 32}};
+        Piece o = {t0 + 4, 0, rw[4], 0, cl[4] / 32};
+        Piece gu[2] = {{t0 + 6, 0, rw[6], 0, cl[6] / 32}, {t0 + 7, 0, rw[7], 0, cl[7] / 32}};
+        Piece dn = {t0 + 8, 0, rw[8], 0, cl[8] / 32};
         if (world > 1) {
-            if (!wq.data || !wk.data || !wv.data || !wo.data || !wg.data || !wu.data || !wd.data) {
-                vxc_set_error("vxc_net_create: layer %d lacks a projection the tensor-parallel split needs", l);
+            const int kvd = cfg->n_kv_heads * hd, F = cfg->n_ff;
+            const bool ok = rw[1] == E && cl[1] == E && rw[2] == kvd && cl[2] == E && rw[3] == kvd && cl[3] == E &&
+                            rw[4] == E && cl[4] == E && rw[6] == F && cl[6] == E && rw[7] == F && cl[7] == E &&
+                            rw[8] == E && cl[8] == F;
+            bool present = true;
+            for (int k = 1; k < 9; k++)
+                if (k != 5 && ty[k] < 0) present = false;
+            if (!present || !ok) {
+                vxc_set_error("vxc_net_create: layer %d lacks a projection the tensor-parallel split needs "
+                              "or has an unexpected shape", l);
                 vxc_net_destroy(n);
                 return -7;
             }
-            wq = rows_of(lv->wq, rank * n->Hl * hd, n->Hl * hd);
-            wk = rows_of(lv->wk, rank * n->KHl * hd, n->KHl * hd);
-            wv = rows_of(lv->wv, rank * n->KHl * hd, n->KHl * hd);
-            wg = rows_of(lv->wg, rank * n->Fl, n->Fl);
-            wu = rows_of(lv->wu, rank * n->Fl, n->Fl);
-            wo = cols_of(lv->wo, rank * n->Hl * hd, n->Hl * hd, obuf);
-            wd = cols_of(lv->wd, rank * n->Fl, n->Fl, dbuf);
+            const int qh = n->Hl * hd, kh = n->KHl * hd;
+            qkv[0] = {t0 + 1, rank * qh, qh, 0, E / 32};
+            qkv[1] = {t0 + 2, rank * kh, kh, 0, E / 32};
+            qkv[2] = {t0 + 3, rank * kh, kh, 0, E / 32};
+            o = {t0 + 4, 0, E, rank * qh / 32, qh / 32};
+            gu[0] = {t0 + 6, rank * n->Fl, n->Fl, 0, E / 32};
+            gu[1] = {t0 + 7, rank * n->Fl, n->Fl, 0, E / 32};
+            dn = {t0 + 8, 0, E, rank * n->Fl / 32, n->Fl / 32};
         }
-        const vxc_tensor_view *qkv[3] = {&wq, &wk, &wv};
-        const vxc_tensor_view *o[1] = {&wo};
-        const vxc_tensor_view *gu[2] = {&wg, &wu};
-        const vxc_tensor_view *dn[1] = {&wd};
-        if ((rc = upload_fused(qkv, 3, &d->wqkv)) || (rc = upload_fused(o, 1, &d->wo)) ||
-            (rc = upload_fused(gu, 2, &d->wgu)) || (rc = upload_fused(dn, 1, &d->wd))) {
+        if ((rc = upload_pieces(src, qkv, 3, &d->wqkv)) || (rc = upload_pieces(src, &o, 1, &d->wo)) ||
+            (rc = upload_pieces(src, gu, 2, &d->wgu)) || (rc = upload_pieces(src, &dn, 1, &d->wd))) {
             vxc_net_destroy(n);
             return rc;
         }
@@ -787,6 +896,41 @@ extern "C" int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_vie
     }
     *out = n;
     return 0;
+}
+
+extern "C" int vxc_net_create(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
+                              const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
+                              const vxc_layer_views *layers, vxc_net **out) {
+    return vxc_net_create_tp(cfg, tok_embd, out_norm, output, layers, NULL, out);
+}
+
+extern "C" int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd,
+                                 const vxc_tensor_view *out_norm, const vxc_tensor_view *output,
+                                 const vxc_layer_views *layers, const vxc_tp *tp, vxc_net **out) {
+    if (!cfg || !tok_embd || !tok_embd->data || !layers || !out) {
+        vxc_set_error("vxc_net_create: unsupported configuration");
+        return -4;
+    }
+    HostSource src;
+    src.tok = tok_embd;
+    src.onorm = out_norm;
+    src.output = output;
+    src.layers = layers;
+    src.L = cfg->n_layers;
+    return net_build(cfg, src, tp, out);
+}
+
+extern "C" int vxc_net_create_synth(const vxc_net_config *cfg, int wtype, uint64_t seed, const vxc_tp *tp,
+                                    vxc_net **out) {
+    if (!cfg || !out || (wtype != 2 && wtype != 8)) {
+        vxc_set_error("vxc_net_create_synth: bad arguments");
+        return -4;
+    }
+    SynthSource src;
+    src.c = *cfg;
+    src.wtype = wtype;
+    src.seed = seed;
+    return net_build(cfg, src, tp, out);
 }
 
 int vxc_net_world(const vxc_net *n) { return n ? n->world : 1; }

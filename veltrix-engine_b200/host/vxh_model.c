@@ -31,6 +31,7 @@
 #include "veltrix_cuda.h"
 #include "vxh_gguf.h"
 #include "vxh_model.h"
+#include "veltrix_synth.h"
 
 static vx_compute_level g_level = VX_COMPUTE_EXACT;
 static int g_threads = 1;
@@ -73,6 +74,32 @@ static int arch_supported(const char *a) {
     for (size_t i = 0; i < sizeof bad / sizeof bad[0]; i++)
         if (strcmp(a, bad[i]) == 0) return 0;
     return 1;
+}
+
+/* A model handle around a device net (the handle owns net and tp). */
+static vx_error wrap_net(vxc_net *net, vxc_tp *tp, int dev, const vxc_net_config *nc, vx_model **out) {
+    vxb_model *m = (vxb_model *)calloc(1, sizeof(vxb_model));
+    if (!m) { vxc_net_destroy(net); return VX_ERR_MEMORY; }
+    m->net = net;
+    m->tp = tp;
+    m->device = dev;
+    vx_model_config *c = &m->pub.config;
+    c->n_layers = nc->n_layers;
+    c->n_heads = nc->n_heads;
+    c->n_kv_heads = nc->n_kv_heads;
+    c->n_embd = nc->n_embd;
+    c->n_head_dim = nc->n_head_dim;
+    c->n_ff = nc->n_ff;
+    c->n_vocab = nc->n_vocab;
+    c->n_ctx = 4096;
+    c->rope_theta = nc->rope_theta;
+    c->n_threads = g_threads;
+    c->arch = VX_ARCH_LLAMA;
+    c->mlp_type = VX_MLP_SWIGLU;
+    c->norm_type = VX_NORM_RMS;
+    m->pub.cache_len = 0;
+    *out = &m->pub;
+    return VX_OK;
 }
 
 /* Load `path` onto the current device; with tp != NULL only this rank's
@@ -138,28 +165,7 @@ static vx_error model_create(const char *path, vxc_tp *tp, vx_model **out) {
         fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
         return rc == -3 ? VX_ERR_MEMORY : (vx_error)rc;
     }
-    vxb_model *m = (vxb_model *)calloc(1, sizeof(vxb_model));
-    if (!m) { vxc_net_destroy(net); return VX_ERR_MEMORY; }
-    m->net = net;
-    m->tp = tp;
-    m->device = dev;
-    vx_model_config *c = &m->pub.config;
-    c->n_layers = L;
-    c->n_heads = H;
-    c->n_kv_heads = KH;
-    c->n_embd = E;
-    c->n_head_dim = E / H;
-    c->n_ff = F;
-    c->n_vocab = V;
-    c->n_ctx = 4096;
-    c->rope_theta = nc.rope_theta;
-    c->n_threads = g_threads;
-    c->arch = VX_ARCH_LLAMA;
-    c->mlp_type = VX_MLP_SWIGLU;
-    c->norm_type = VX_NORM_RMS;
-    m->pub.cache_len = 0;
-    *out = &m->pub;
-    return VX_OK;
+    return wrap_net(net, tp, dev, &nc, out);
 }
 
 vx_error vx_model_create(const char *path, vx_model **out) {
@@ -186,6 +192,47 @@ vx_error vx_model_create_tp(const char *path, int rank, int world, const void *n
         return rc == -4 ? VX_ERR_PARAM : VX_ERR_UNSUPPORTED;
     }
     vx_error e = model_create(path, tp, out);
+    if (e != VX_OK) vxc_tp_destroy(tp);
+    return e;
+}
+
+vx_error vx_model_create_synth(const vx_synth_config *cfg, uint64_t seed, int rank, int world,
+                               const void *nccl_id, vx_model **out) {
+    if (!cfg || !out || world < 1 || rank < 0 || rank >= world || (world > 1 && !nccl_id) || cfg->n_heads <= 0 ||
+        cfg->n_embd % cfg->n_heads)
+        return VX_ERR_PARAM;
+    int dev = vxc_device_current();
+    if (dev < 0 || vxc_device_init(dev) != 0) {
+        fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+        return VX_ERR_UNSUPPORTED;
+    }
+    vxc_tp *tp = NULL;
+    if (nccl_id) {
+        int rc = vxc_tp_create(nccl_id, rank, world, &tp);
+        if (rc) {
+            fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+            return rc == -4 ? VX_ERR_PARAM : VX_ERR_UNSUPPORTED;
+        }
+    }
+    vxc_net_config nc;
+    memset(&nc, 0, sizeof nc);
+    nc.n_layers = cfg->n_layers;
+    nc.n_heads = cfg->n_heads;
+    nc.n_kv_heads = cfg->n_kv_heads;
+    nc.n_embd = cfg->n_embd;
+    nc.n_head_dim = cfg->n_embd / cfg->n_heads;
+    nc.n_ff = cfg->n_ff;
+    nc.n_vocab = cfg->n_vocab;
+    nc.rope_theta = cfg->rope_theta;
+    nc.max_pos = 16384;
+    vxc_net *net = NULL;
+    int rc = vxc_net_create_synth(&nc, cfg->wtype, seed, tp, &net);
+    if (rc) {
+        fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+        vxc_tp_destroy(tp);
+        return rc == -3 ? VX_ERR_MEMORY : (vx_error)rc;
+    }
+    vx_error e = wrap_net(net, tp, dev, &nc, out);
     if (e != VX_OK) vxc_tp_destroy(tp);
     return e;
 }

@@ -36,6 +36,9 @@ PROTOTYPES = {
     "vxc_profile_read": (ctypes.c_int, [_vp, ctypes.c_int]),
     "vxc_net_create": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_vp)]),
     "vxc_net_create_tp": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.POINTER(_vp)]),
+    "vxc_net_create_synth": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_uint64, _vp, ctypes.POINTER(_vp)]),
+    "vx_model_create_synth": (ctypes.c_int, [_vp, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _vp,
+                                             ctypes.POINTER(_vp)]),
     "vxc_tp_unique_id": (ctypes.c_int, [_vp]),
     "vxc_tp_create": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
     "vxc_tp_destroy": (None, [_vp]),
@@ -181,10 +184,19 @@ def tp_unique_id():
 class Model:
     """vx_model handle of the B200 back end (include/model.h)."""
 
-    def __init__(self, path, tp=None):
-        """tp = (rank, world, nccl_id bytes) loads this rank's tensor-parallel shard."""
+    def __init__(self, path, tp=None, synth=None):
+        """tp = (rank, world, nccl_id bytes) loads this rank's tensor-parallel shard.
+        synth = (n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab, wtype, seed, rope_theta)
+        generates the weights on the device instead of reading `path` (None)."""
         h = _vp()
-        if tp is None:
+        if synth is not None:
+            e, L, hh, kv, ff, v, wt, seed, th = synth
+            c = SynthConfig(e, L, hh, kv, ff, v, th, wt)
+            rank, world, uid = tp if tp is not None else (0, 1, None)
+            idbuf = ctypes.create_string_buffer(bytes(uid), 128) if uid is not None else None
+            rc = lib().vx_model_create_synth(ctypes.byref(c), seed, rank, world, idbuf, ctypes.byref(h))
+            path = "<synthetic>"
+        elif tp is None:
             rc = lib().vx_model_create(path.encode(), ctypes.byref(h))
         else:
             rank, world, uid = tp
