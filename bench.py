@@ -180,7 +180,6 @@ def run_q4matvec_gpu(args, ws, rank, local):
 
     for _ in range(args.warmup):
         step()
-        progress("warm-up step done")
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -399,23 +398,25 @@ def run_spec7b_gpu(args, ws, rank, local):
         if rank == 0:
             print(f"[bench] {time.time() - t_start:7.1f} s  {what}", file=sys.stderr, flush=True)
 
-    if local == 0:
-        spec_fixtures(write=True)
-    progress("checkpoints written")
-    if dist:
-        dist.barrier()
-    tpath, dpath = spec_fixtures(write=False)
     if TP:
-        # one tensor-parallel group over all GPUs: rank 0's NCCL id reaches the others
+        # one tensor-parallel group over all GPUs: rank 0's NCCL id reaches the others.  The
+        # weights are generated on each GPU (its shard only): the writer's numbers, no 41 GB file
         ids = [vxb200.tp_unique_id() if rank == 0 else None]
         if dist:
             dist.broadcast_object_list(ids, src=0)
-        target = vxb200.Model(tpath, tp=(rank, ws, ids[0]))
+        synth = lambda c: c[:7] + (c[7], ROPE_THETA[True])
+        target = vxb200.Model(None, tp=(rank, ws, ids[0]), synth=synth(SPEC_TARGET))
+        draft = vxb200.Model(None, synth=synth(SPEC_DRAFT))
         first, S = 0, SPEC["seqs_per_gpu"]          # every GPU runs every sequence, on its shard
     else:
+        if local == 0:
+            spec_fixtures(write=True)
+        if dist:
+            dist.barrier()
+        tpath, dpath = spec_fixtures(write=False)
         target = vxb200.Model(tpath)
+        draft = vxb200.Model(dpath)
         first, S = shard(rank, ws, SPEC["seqs_per_gpu"])
-    draft = vxb200.Model(dpath)
     progress("models loaded")
     k = SPEC["k"]
     sp = vxb200.Speculative(draft, target, k, temp=SPEC["temp"], seed=SPEC["seed"], seq_id_base=first)
@@ -605,10 +606,11 @@ SPEC70_METRIC = "accepted tok/s (70B-shape Q4_0 tensor-parallel spec decode)"
 
 def spec_config(ws):
     if TP:
-        return {"workload": "spec70b: Llama-3-70B-shape Q4_0 target (80 layers) split over the GPUs, 1B-shape "
-                            f"Q8_0 draft on each, k={SPEC['k']}, T={SPEC['temp']} Philox sampling, "
+        small = "" if (SPEC_TARGET[1], SPEC["prompt"]) == (80, 4096) else " (reduced: functional/profiling case)"
+        return {"workload": f"spec70b: Llama-3-70B-shape Q4_0 target ({SPEC_TARGET[1]} layers) split over the "
+                            f"GPUs, 1B-shape Q8_0 draft on each, k={SPEC['k']}, T={SPEC['temp']} Philox sampling, "
                             f"{SPEC['seqs_per_gpu']} sequences of {SPEC['prompt']}-id prompts, "
-                            f"{SPEC['new']} new tokens",
+                            f"{SPEC['new']} new tokens, weights generated on the device" + small,
                 "global_seqs": SPEC["seqs_per_gpu"], "k": SPEC["k"], "prompt": SPEC["prompt"],
                 "new_tokens": SPEC["new"], "temp": SPEC["temp"],
                 "l2": "no flush: >= 20 GB of weights and KV per GPU per verify step, far above L2",
@@ -707,12 +709,19 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--new", type=int, default=None, help="new tokens per sequence (spec workloads)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg (profiling runs)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="spec70b: target layers (fewer than 80 = a small functional/profiling case)")
+    ap.add_argument("--prompt", type=int, default=None, help="spec70b: prompt ids per sequence")
     args = ap.parse_args()
     global SPEC_TARGET, SPEC_DRAFT, TP
     if args.workload == "spec70b":
         TP = True
         SPEC_TARGET, SPEC_DRAFT = SPEC70_TARGET, SPEC70_DRAFT
         SPEC.update(SPEC70)
+        if args.layers is not None:
+            SPEC_TARGET = SPEC_TARGET[:1] + (args.layers,) + SPEC_TARGET[2:]
+        if args.prompt is not None:
+            SPEC["prompt"] = args.prompt
     if args.new is not None:
         SPEC["new"] = args.new
     ws, rank, _ = dist_setup(args)
