@@ -149,6 +149,11 @@ void vxc_tp_destroy(vxc_tp *tp);
  * gathers the logits (all-gather), so every rank sees the full logits.
  * H, KV heads, n_ff and n_vocab must divide by the world size.  tp == NULL
  * is vxc_net_create.  The net borrows tp, which must outlive it. */
+/* The split vxc_net_create_tp applies, for inspection and host-side tests
+ * (no device needed): out[8][4] = {first row, rows, first column, columns}
+ * of this rank's slice of Wq, Wk, Wv, Wo, W_gate, W_up, W_down and the LM
+ * head, in elements of the GGUF [rows][cols] matrices. */
+int vxc_tp_shard_ranges(const vxc_net_config *cfg, int rank, int world, int *out);
 int vxc_net_create_tp(const vxc_net_config *cfg, const vxc_tensor_view *tok_embd, const vxc_tensor_view *out_norm,
                       const vxc_tensor_view *output, const vxc_layer_views *layers, const vxc_tp *tp,
                       vxc_net **out);

@@ -770,6 +770,29 @@ static int upload_pieces(const NetSource &src, const Piece *p, int n, vxc_qmat *
     return rc;
 }
 
+extern "C" int vxc_tp_shard_ranges(const vxc_net_config *cfg, int rank, int world, int *out) {
+    if (!cfg || !out || world < 1 || rank < 0 || rank >= world || cfg->n_heads % world ||
+        cfg->n_kv_heads % world || cfg->n_ff % (32 * world) || cfg->n_vocab % world || cfg->n_head_dim % 32) {
+        vxc_set_error("vxc_tp_shard_ranges: heads, FFN and vocab must split evenly over %d GPUs", world);
+        return -4;
+    }
+    const int E = cfg->n_embd, hd = cfg->n_head_dim, F = cfg->n_ff;
+    const int qh = cfg->n_heads / world * hd, kh = cfg->n_kv_heads / world * hd, fl = F / world;
+    const int vl = cfg->n_vocab / world;
+    const int r[8][4] = {
+        {rank * qh, qh, 0, E},   // q: rows of this GPU's heads
+        {rank * kh, kh, 0, E},   // k: rows of its kv heads
+        {rank * kh, kh, 0, E},   // v
+        {0, E, rank * qh, qh},   // output projection: the matching input columns
+        {rank * fl, fl, 0, E},   // gate: rows of its FFN columns
+        {rank * fl, fl, 0, E},   // up
+        {0, E, rank * fl, fl},   // down: the matching input columns
+        {rank * vl, vl, 0, E},   // LM head: its vocabulary rows
+    };
+    memcpy(out, r, sizeof r);
+    return 0;
+}
+
 // Build a net from a weight source; tp != NULL keeps this GPU's shard only.
 static int net_build(const vxc_net_config *cfg, const NetSource &src, const vxc_tp *tp, vxc_net **out) {
     int rc = vxc_require_device();
@@ -823,9 +846,14 @@ static int net_build(const vxc_net_config *cfg, const NetSource &src, const vxc_
     }
     {
         // tensor parallel: this GPU's vocabulary rows of the LM head
-        int t, r, c;
+        int t, r, c, sr[8][4];
         src.shape(9 * L + 2, &t, &r, &c);
-        const Piece p = {9 * L + 2, world > 1 ? rank * n->Vl : 0, world > 1 ? n->Vl : r, 0, c / 32};
+        Piece p = {9 * L + 2, 0, r, 0, c / 32};
+        if (world > 1) {
+            vxc_tp_shard_ranges(cfg, rank, world, &sr[0][0]);
+            p.r0 = sr[7][0];
+            p.nr = sr[7][1];
+        }
         if ((rc = upload_pieces(src, &p, 1, &n->out))) { vxc_net_destroy(n); return rc; }
     }
     n->layers = (vxc_layer_dev *)calloc((size_t)L, sizeof(vxc_layer_dev));
@@ -860,14 +888,16 @@ static int net_build(const vxc_net_config *cfg, const NetSource &src, const vxc_
                 vxc_net_destroy(n);
                 return -7;
             }
-            const int qh = n->Hl * hd, kh = n->KHl * hd;
-            qkv[0] = {t0 + 1, rank * qh, qh, 0, E / 32};
-            qkv[1] = {t0 + 2, rank * kh, kh, 0, E / 32};
-            qkv[2] = {t0 + 3, rank * kh, kh, 0, E / 32};
-            o = {t0 + 4, 0, E, rank * qh / 32, qh / 32};
-            gu[0] = {t0 + 6, rank * n->Fl, n->Fl, 0, E / 32};
-            gu[1] = {t0 + 7, rank * n->Fl, n->Fl, 0, E / 32};
-            dn = {t0 + 8, 0, E, rank * n->Fl / 32, n->Fl / 32};
+            int sr[8][4];
+            vxc_tp_shard_ranges(cfg, rank, world, &sr[0][0]);
+            auto piece = [&](int ti, const int *g) { return Piece{ti, g[0], g[1], g[2] / 32, g[3] / 32}; };
+            qkv[0] = piece(t0 + 1, sr[0]);
+            qkv[1] = piece(t0 + 2, sr[1]);
+            qkv[2] = piece(t0 + 3, sr[2]);
+            o = piece(t0 + 4, sr[3]);
+            gu[0] = piece(t0 + 6, sr[4]);
+            gu[1] = piece(t0 + 7, sr[5]);
+            dn = piece(t0 + 8, sr[6]);
         }
         if ((rc = upload_pieces(src, qkv, 3, &d->wqkv)) || (rc = upload_pieces(src, &o, 1, &d->wo)) ||
             (rc = upload_pieces(src, gu, 2, &d->wgu)) || (rc = upload_pieces(src, &dn, 1, &d->wd))) {

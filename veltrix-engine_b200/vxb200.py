@@ -40,6 +40,7 @@ PROTOTYPES = {
     "vx_model_create_synth": (ctypes.c_int, [_vp, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _vp,
                                              ctypes.POINTER(_vp)]),
     "vxc_tp_unique_id": (ctypes.c_int, [_vp]),
+    "vxc_tp_shard_ranges": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
     "vxc_tp_create": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_vp)]),
     "vxc_tp_destroy": (None, [_vp]),
     "vxc_net_destroy": (None, [_vp]),
@@ -91,6 +92,22 @@ class SynthConfig(ctypes.Structure):
     _fields_ = [("n_embd", ctypes.c_int), ("n_layers", ctypes.c_int), ("n_heads", ctypes.c_int),
                 ("n_kv_heads", ctypes.c_int), ("n_ff", ctypes.c_int), ("n_vocab", ctypes.c_int),
                 ("rope_theta", ctypes.c_float), ("wtype", ctypes.c_int)]
+
+
+class NetConfig(ctypes.Structure):
+    """vxc_net_config (include/veltrix_cuda.h)."""
+    _fields_ = [("n_layers", ctypes.c_int), ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int),
+                ("n_embd", ctypes.c_int), ("n_head_dim", ctypes.c_int), ("n_ff", ctypes.c_int),
+                ("n_vocab", ctypes.c_int), ("max_pos", ctypes.c_int), ("rope_theta", ctypes.c_float)]
+
+
+def tp_shard_ranges(n_embd, n_heads, n_kv_heads, n_ff, n_vocab, rank, world):
+    """[(first row, rows, first col, cols)] of Wq, Wk, Wv, Wo, W_gate, W_up, W_down, LM head
+    that rank `rank` of `world` keeps (the split vxc_net_create_tp applies)."""
+    c = NetConfig(1, n_heads, n_kv_heads, n_embd, n_embd // n_heads, n_ff, n_vocab, 4096, 10000.0)
+    out = (ctypes.c_int * 32)()
+    check(lib().vxc_tp_shard_ranges(ctypes.byref(c), rank, world, out), "vxc_tp_shard_ranges")
+    return [tuple(out[4 * i:4 * i + 4]) for i in range(8)]
 
 
 class ModelConfig(ctypes.Structure):
