@@ -12,7 +12,9 @@
  *                   `world` GPUs, one process each (tensor parallelism over
  *                   NCCL; nccl_id from vxc_tp_unique_id on rank 0).  Every
  *                   rank then makes the same calls in the same order and
- *                   gets the full logits.
+ *                   gets the full logits.  Destroy speculative states that
+ *                   use such a model before the model: their CUDA graphs
+ *                   hold the model's NCCL operations.
  */
 #ifndef VX_MODEL_H
 #define VX_MODEL_H

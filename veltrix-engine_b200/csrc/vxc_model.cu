@@ -1276,18 +1276,22 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     cudaError_t e;
     // tensor parallel: sum a row-parallel projection's output over the GPUs
     // (its split-K partials first summed here into s->ar), then read it as one slice
-    auto tp_sum = [&](Part &p) -> cudaError_t {
+    // 0, or the error code with the message set
+    auto tp_sum = [&](Part &p) -> int {
         const size_t tot = (size_t)M * E;
         cudaError_t er = launch_pdl(k_part_out, dim3(nblk(tot, 256) < 1184 ? nblk(tot, 256) : 1184), dim3(256), 0,
                                     st, p, M, s->ar);
-        if (er != cudaSuccess) return er;
-        if (vxc_tp_allreduce_sum(n->tp, s->ar, tot, st)) return cudaErrorUnknown;
+        if (er != cudaSuccess) {
+            vxc_set_error("vxc_forward: %s", cudaGetErrorString(er));
+            return -3;
+        }
+        if (int r = vxc_tp_allreduce_sum(n->tp, s->ar, tot, st)) return r;
         p.base = s->ar;
         p.slot = (size_t)64 * E;
         p.R = E;
         p.M = M;
         p.ks_full = p.ks_last = 1;
-        return cudaSuccess;
+        return 0;
     };
     cudaEvent_t pe = prof_begin(st);
     e = launch_pdl(k_embed, dim3(M), dim3(256), 0, st, n->embd, n->embd_type, n->embd_row_bytes,
@@ -1337,7 +1341,7 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wo, M, &pp, st))) return rc;
-        if (n->tp && (e = tp_sum(pp)) != cudaSuccess) break;
+        if (n->tp && (rc = tp_sum(pp))) return rc;
         prof_end(6, pe, st);
         pe = prof_begin(st);
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, pp,
@@ -1354,7 +1358,7 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         if ((rc = gemv_rows(s, d->wd, M, &prev, st))) return rc;
-        if (n->tp && (e = tp_sum(prev)) != cudaSuccess) break;
+        if (n->tp && (rc = tp_sum(prev))) return rc;
         prof_end(10, pe, st);
     }
     if (e == cudaSuccess && n_logit_rows > 0) {
