@@ -195,6 +195,18 @@ int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *
  * the tokens in chunks of max_rows and synchronises. */
 int vxc_forward_host(vxc_seqs *s, int slot, int pos0, const int *h_tokens, int n_tokens, float *h_logits);
 
+/* Greedy decoding of one sequence (the loop of the reference's CLI,
+ * src/main.c:283-324): forward the prompt at positions pos0.., then emit the
+ * argmax token (first index of the maximum, src/main.c:307-311) and forward
+ * it, until max_tokens are emitted or the argmax is eos_id (not emitted;
+ * eos_id < 0: none).  The reference forwards the last prompt token a second
+ * time before its loop (src/main.c:283,300-304); this loop does not.  Each
+ * token is one CUDA-graph replay with no host round trip.  *n_out = tokens
+ * written to h_out; *pos_out = positions now cached (the last emitted token
+ * is not yet in the cache).  Returns 0 or an error code. */
+int vxc_greedy_generate(vxc_seqs *seqs, int slot, int pos0, const int *h_prompt, int n_prompt, int *h_out,
+                        int max_tokens, int eos_id, int *n_out, int *pos_out);
+
 /* ---- sampling ----------------------------------------------------------------
  * Canonical sampler shared with the CPU oracle (bit-exact given the same fp32
  * logits): T <= 0 is greedy (first maximum, reference src/speculative.c:93-98);

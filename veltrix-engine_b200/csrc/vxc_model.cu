@@ -16,6 +16,7 @@
 // does (freq = 1/powf(theta, 2i/hd), val = pos*freq, cosf/sinf), and the
 // rotation is written with explicitly rounded ops, so it matches the
 // reference bit-for-bit.  The KV cache is fp32 ([layer][slot][pos][kv_dim]).
+#include <climits>
 #include "vxc_common.cuh"
 #include "vxc_image.cuh"
 #include "vxc_ptx.cuh"
@@ -593,6 +594,59 @@ __global__ void k_vocab_gather(const float *__restrict__ all, int world, int n_r
         const size_t m = i / V, c = i % V, w = c / Vl, v = c % Vl;
         out[i] = all[(w * n_rows + m) * Vl + v];
     }
+}
+
+// Greedy token of one logits row, the reference's rule (src/main.c:307-311):
+// scanning upward from max = -1e30, the first index whose value is strictly
+// greater than every earlier one (NaN never wins; 0 when none exceeds -1e30).
+__global__ void __launch_bounds__(1024) k_argmax_row(const float *__restrict__ lg, int V, int *__restrict__ tok) {
+    pdl_trigger();
+    pdl_wait();
+    float best = -1e30f;
+    int bi = INT_MAX;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {   // ascending within a thread: > keeps the first
+        const float v = lg[j];
+        if (v > best) { best = v; bi = j; }
+    }
+    auto merge = [&]() {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        }
+    };
+    merge();
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+    if (l == 0) { sv[w] = best; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        best = l < nw ? sv[l] : -1e30f;
+        bi = l < nw ? si[l] : INT_MAX;
+        merge();
+        if (l == 0) *tok = bi == INT_MAX ? 0 : bi;
+    }
+}
+
+// One step of the greedy loop after the argmax: the token just forwarded is
+// now cached (pos + 1); the new token ends the loop if it is eos, else it is
+// emitted.  st = {emitted, next position, done}.
+__global__ void k_greedy_record(const int *__restrict__ tok, int *__restrict__ st, int *__restrict__ out, int eos,
+                                int max_tokens) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x != 0 || st[2]) return;
+    st[1] += 1;
+    const int t = *tok;
+    if (t == eos) {
+        st[2] = 1;
+        return;
+    }
+    out[st[0]] = t;
+    st[0] += 1;
+    if (st[0] >= max_tokens) st[2] = 1;
 }
 
 // logits[m][r] = sum of the LM head's partials
@@ -1430,5 +1484,120 @@ extern "C" int vxc_forward_host(vxc_seqs *s, int slot, int pos0, const int *h_to
     if (rc == 0) rc = vxc_check_device_error(NULL);
     cudaFree(d_i);
     cudaFree(d_l);
+    return rc;
+}
+
+// ---------------------------------------------------------------------------
+// greedy decoding on the device (the loop of the reference's CLI,
+// src/main.c:283-324, without its second forward of the last prompt token)
+// ---------------------------------------------------------------------------
+extern "C" int vxc_greedy_generate(vxc_seqs *s, int slot, int pos0, const int *h_prompt, int n_prompt, int *h_out,
+                                   int max_tokens, int eos_id, int *n_out, int *pos_out) {
+    if (!s || !h_prompt || n_prompt <= 0 || !h_out || max_tokens <= 0 || slot < 0 || slot >= s->n_slots ||
+        pos0 < 0) {
+        vxc_set_error("vxc_greedy_generate: bad arguments");
+        return -4;
+    }
+    if ((long long)pos0 + n_prompt + max_tokens > s->max_ctx) {
+        vxc_set_error("vxc_greedy_generate: %d + %d + %d positions exceed the context of %d", pos0, n_prompt,
+                      max_tokens, s->max_ctx);
+        return -4;
+    }
+    const int V = s->net->cfg.n_vocab, chunk = s->max_rows;
+    // ints: prompt chunk | chunk meta {slot, pos, last row} | tok | state {n, pos, done} | slot | row 0 | out
+    const int o_meta = chunk, o_tok = chunk + 3, o_st = o_tok + 1, o_slot = o_st + 3, o_row = o_slot + 1,
+              o_out = o_row + 1;
+    int *d_i = NULL;
+    float *d_l = NULL;
+    cudaStream_t st = NULL;
+    cudaGraph_t graph = NULL;
+    cudaGraphExec_t exec = NULL;
+    cudaError_t e = cudaMalloc((void **)&d_i, (size_t)(o_out + max_tokens) * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc((void **)&d_l, (size_t)V * sizeof(float));
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    int rc = e == cudaSuccess ? 0 : -3;
+    if (rc) vxc_set_error("vxc_greedy_generate: %s", cudaGetErrorString(e));
+    // prompt pass, logits of its last row only
+    for (int done = 0; done < n_prompt && rc == 0; done += chunk) {
+        const int n = n_prompt - done < chunk ? n_prompt - done : chunk;
+        const int meta[3] = {slot, pos0 + done, n - 1};
+        e = cudaMemcpyAsync(d_i, h_prompt + done, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(d_i + o_meta, meta, sizeof meta, cudaMemcpyHostToDevice, st);
+        // the host arrays are reused next chunk
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) {
+            vxc_set_error("vxc_greedy_generate: %s", cudaGetErrorString(e));
+            rc = -3;
+            break;
+        }
+        const bool last = done + n >= n_prompt;
+        rc = vxc_forward(s, d_i, d_i + o_meta, d_i + o_meta + 1, 1, n, last ? d_i + o_meta + 2 : NULL, last ? 1 : 0,
+                         last ? d_l : NULL, st);
+    }
+    int state[3] = {0, pos0 + n_prompt - 1, 0};
+    if (rc == 0) {
+        const int init[6] = {state[0], state[1], state[2], slot, 0, 0};
+        e = cudaMemcpyAsync(d_i + o_st, init, 5 * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = launch_pdl(k_argmax_row, dim3(1), dim3(1024), 0, st, (const float *)d_l, V, d_i + o_tok);
+        if (e == cudaSuccess)
+            e = launch_pdl(k_greedy_record, dim3(1), dim3(32), 0, st, (const int *)(d_i + o_tok), d_i + o_st,
+                           d_i + o_out, eos_id, max_tokens);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(state, d_i + o_st, sizeof state, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) { vxc_set_error("vxc_greedy_generate: %s", cudaGetErrorString(e)); rc = -3; }
+    }
+    // one captured graph per token: forward the last token, argmax, record
+    if (rc == 0 && !state[2]) {
+        const long long before = vxc_launch_count();
+        e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
+        if (e == cudaSuccess) {
+            rc = vxc_forward(s, d_i + o_tok, d_i + o_slot, d_i + o_st + 1, 1, 1, d_i + o_row, 1, d_l, st);
+            cudaError_t e1 = cudaSuccess, e2 = cudaSuccess;
+            if (rc == 0) e1 = launch_pdl(k_argmax_row, dim3(1), dim3(1024), 0, st, (const float *)d_l, V, d_i + o_tok);
+            if (rc == 0 && e1 == cudaSuccess)
+                e1 = launch_pdl(k_greedy_record, dim3(1), dim3(32), 0, st, (const int *)(d_i + o_tok), d_i + o_st,
+                                d_i + o_out, eos_id, max_tokens);
+            e2 = cudaStreamEndCapture(st, &graph);
+            e = e1 != cudaSuccess ? e1 : e2;
+        }
+        const long long per_step = vxc_launch_count() - before;
+        vxc_count_launches(-per_step);   // captured, not run; each replay counts them
+        if (rc == 0 && e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+        if (rc == 0 && e != cudaSuccess) { vxc_set_error("vxc_greedy_generate: graph: %s", cudaGetErrorString(e)); rc = -3; }
+        // each replay emits one token until done: max_tokens - 1 replays at most; the
+        // host looks at the done flag every 8 replays (a few extra forwards after
+        // eos write only positions past the cache length)
+        for (int i = 0; rc == 0 && i < max_tokens - 1; i++) {
+            e = cudaGraphLaunch(exec, st);
+            if (e != cudaSuccess) break;
+            vxc_count_launches(per_step);
+            if ((i & 7) == 7 || i == max_tokens - 2) {
+                e = cudaMemcpyAsync(state, d_i + o_st, sizeof state, cudaMemcpyDeviceToHost, st);
+                if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+                if (e != cudaSuccess || state[2]) break;
+            }
+        }
+        if (rc == 0 && e != cudaSuccess) { vxc_set_error("vxc_greedy_generate: %s", cudaGetErrorString(e)); rc = -3; }
+    }
+    if (rc == 0) {
+        e = cudaMemcpyAsync(state, d_i + o_st, sizeof state, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e == cudaSuccess && state[0] > 0)
+            e = cudaMemcpy(h_out, d_i + o_out, (size_t)state[0] * sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) { vxc_set_error("vxc_greedy_generate: %s", cudaGetErrorString(e)); rc = -3; }
+    }
+    if (rc == 0) rc = vxc_check_device_error(NULL);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
+    if (st) {
+        cudaStreamSynchronize(st);
+        cudaStreamDestroy(st);
+    }
+    if (d_i) cudaFree(d_i);
+    if (d_l) cudaFree(d_l);
+    if (rc == 0) {
+        if (n_out) *n_out = state[0];
+        if (pos_out) *pos_out = state[1];
+    }
     return rc;
 }

@@ -287,6 +287,29 @@ vx_error vx_model_forward(vx_model *model, const int *tokens, int n_tokens, floa
     return VX_OK;
 }
 
+int vx_model_generate_greedy(vx_model *model, const int *prompt, int n_prompt, int *out, int max_tokens,
+                             int eos_id) {
+    if (!model || !prompt || n_prompt <= 0 || !out || max_tokens <= 0) return VX_ERR_PARAM;
+    if (g_level != VX_COMPUTE_EXACT) return VX_ERR_UNSUPPORTED;
+    vxb_model *m = vxb_of(model);
+    int keep = model->cache_len;
+    vx_error e = ensure_seqs(m);
+    if (e) return e;
+    model->cache_len = keep < 0 ? 0 : keep;
+    if ((long long)model->cache_len + n_prompt + max_tokens > m->seqs_ctx) return VX_ERR_PARAM;
+    if (vxc_device_current() != m->device) vxc_device_init(m->device);
+    int n = 0, pos = 0;
+    double t0 = g_timing ? now_us() : 0.0;
+    int rc = vxc_greedy_generate(m->seqs, 0, model->cache_len, prompt, n_prompt, out, max_tokens, eos_id, &n, &pos);
+    if (g_timing) { g_fwd_us += now_us() - t0; g_fwd_calls++; g_fwd_tokens += n_prompt + n; }
+    if (rc) {
+        fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
+        return rc == -4 ? VX_ERR_PARAM : VX_ERR_MEMORY;
+    }
+    model->cache_len = pos;
+    return n;
+}
+
 void vx_model_kv_truncate(vx_model *model, int length) {   /* src/model.c:384-389 */
     if (!model) return;
     if (length < 0) length = 0;

@@ -55,6 +55,9 @@ PROTOTYPES = {
     "vx_model_create_tp": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, _vp, ctypes.POINTER(_vp)]),
     "vx_model_destroy": (None, [_vp]),
     "vx_model_forward": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    "vx_model_generate_greedy": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_int]),
+    "vxc_greedy_generate": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, ctypes.c_int,
+                                           ctypes.c_int, _c_int_p, _c_int_p]),
     "vx_model_kv_truncate": (None, [_vp, ctypes.c_int]),
     "vx_set_compute_level": (None, [ctypes.c_int]),
     "vx_enable_metalearn": (None, [ctypes.c_bool]),
@@ -244,6 +247,16 @@ class Model:
         if rc != 0:
             raise VxError(f"vx_model_forward = {rc}: {lib().vxc_error_string()}")
         return out
+
+    def generate_greedy(self, prompt, max_tokens, eos_id=-1):
+        """vx_model_generate_greedy: the emitted tokens (int32 array)."""
+        import numpy as np
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(max_tokens, np.int32)
+        n = lib().vx_model_generate_greedy(self.h, p.ctypes.data, p.size, out.ctypes.data, max_tokens, eos_id)
+        if n < 0:
+            raise VxError(f"vx_model_generate_greedy = {n}: {lib().vxc_error_string()}")
+        return out[:n]
 
     def close(self):
         if self.h:
