@@ -35,6 +35,17 @@ void     vxo_dequant_q8_0(const void *blocks, float *y, int n);
 void     vxo_qgemv(int type, const void *w, const float *x, float *y,
                    int M, int rows, int cols);
 
+/* ---- K-quant weights (vxo_kquant.c; type ids 10..15 = Q2_K..Q8_K) ---- */
+size_t vxo_kquant_block_bytes(int type);
+/* The reference's vx_dequantize_row_* for the type; n % 256 == 0. */
+int vxo_dequant_kquant(int type, const void *blocks, float *y, int n);
+/* y[r] = dequant(W)[r] . x, one sequential fp32 sum per row (the
+ * reference's blockwise GEMV); cols % 256 == 0. */
+int vxo_gemv_kquant(int type, const void *w, const float *x, float *y, int rows, int cols);
+/* The reference's GEMV as shipped: Q2_K/Q3_K/Q4_K through Q8_K-quantised
+ * activations and integer dots, other types as vxo_gemv_kquant. */
+int vxo_gemv_kquant_shipped(int type, const void *w, const float *x, float *y, int rows, int cols);
+
 /* ---- elementwise ops (reference src/tensor.c scalar branches) ---- */
 void vxo_rms_norm(float *o, const float *x, const float *w, int n);
 void vxo_softmax(float *x, int n);
