@@ -62,8 +62,16 @@ typedef struct vxc_qmat vxc_qmat;
  * per 128-row tile and 32-column block, records of a tile contiguous along
  * K).  type: 2 = Q4_0 (18-byte blocks), 8 = Q8_0 (34-byte blocks).
  * Replaces the reference's tensor load + whole-matrix dequant buffer
- * (src/gguf.c:236-287, src/model.c:74-87). */
+ * (src/gguf.c:236-287, src/model.c:74-87).
+ * K-quant types 10..15 (Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, Q8_K; cols % 256 == 0,
+ * blocks of 84/110/144/176/210/292 bytes) are kept as GGUF super-blocks:
+ * vxc_qgemv then decodes each weight as the reference does and sums in fp32
+ * (the reference's blockwise GEMV, src/quantize.c:486-505; it needs no
+ * workspace).  Models with K-quant matrices are not loaded yet. */
 int vxc_qmat_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out);
+/* Decoded weights of a K-quant matrix, fp32 [rows][cols] in device memory,
+ * bit for bit the reference's vx_dequantize_row_* for the type. */
+int vxc_kquant_dequant(const vxc_qmat *w, float *y, void *stream);
 void vxc_qmat_destroy(vxc_qmat *w);
 int vxc_qmat_shape(const vxc_qmat *w, int *type, int *rows, int *cols);
 

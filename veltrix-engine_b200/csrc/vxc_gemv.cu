@@ -148,6 +148,10 @@ int vxc_qmat_from_device(int type, const uint8_t *dev_blocks, int rows, int cols
 }
 
 extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out) {
+    if (vxc_is_kquant(type)) {
+        int rc = vxc_require_device();
+        return rc ? rc : vxc_kquant_create(type, host_blocks, rows, cols, out);
+    }
     if (!out || !host_blocks || rows <= 0 || cols <= 0 || (cols % 32) != 0 || (type != 2 && type != 8)) {
         vxc_set_error("vxc_qmat_create: bad arguments (type %d, %d x %d)", type, rows, cols);
         return -4;
@@ -331,6 +335,7 @@ static void simt_split(const vxc_qmat *w, int *ks, int *bps) {
 }
 
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M) {
+    if (vxc_is_kquant(w->type)) return 0;
     int ks, bps;
     simt_split(w, &ks, &bps);
     return ks > 1 ? (size_t)ks * M * w->rows * sizeof(float) : 0;
@@ -339,6 +344,7 @@ size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M) {
 extern "C" int vxc_qgemv_simt(const vxc_qmat *w, const float *x, int M, float *y, void *workspace,
                               size_t workspace_bytes, void *stream) {
     if (!w || !x || !y || M <= 0) { vxc_set_error("vxc_qgemv_simt: bad arguments"); return -4; }
+    if (vxc_is_kquant(w->type)) { vxc_set_error("vxc_qgemv_simt: Q4_0 / Q8_0 only"); return -7; }
     int ks, bps;
     simt_split(w, &ks, &bps);
     size_t need = ks > 1 ? (size_t)ks * M * w->rows * sizeof(float) : 0;

@@ -581,7 +581,7 @@ static size_t chunk_ws_bytes(const vxc_qmat *w, int M) {
 }
 
 extern "C" size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M) {
-    if (!w || M <= 0) return 0;
+    if (!w || M <= 0 || vxc_is_kquant(w->type)) return 0;
     const int mc = M < 64 ? M : 64;
     size_t b = chunk_ws_bytes(w, mc);
     if (M > 64 && M % 64) {
@@ -599,6 +599,7 @@ extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, voi
     if (((uintptr_t)x & 15) != 0) { vxc_set_error("vxc_qgemv: x must be 16-byte aligned"); return -4; }
     if (((uintptr_t)workspace & 15) != 0) { vxc_set_error("vxc_qgemv: workspace must be 16-byte aligned"); return -4; }
     cudaStream_t st = (cudaStream_t)stream;
+    if (vxc_is_kquant(w->type)) return vxc_kquant_gemv(w, x, M, y, st);   // no workspace
     for (int m0 = 0; m0 < M; m0 += 64) {
         const int mc = M - m0 < 64 ? M - m0 : 64;
         VxcGemvPlan p;

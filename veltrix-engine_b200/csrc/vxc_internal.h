@@ -24,6 +24,12 @@ int vxc_qmat_from_device(int type, const uint8_t *dev_blocks, int rows, int cols
 int vxc_synth_blocks(int type, uint64_t seed, uint32_t ti, long long row0, int nrows, int nblk_full, int blk0,
                      int nblk, uint8_t *dev_out);
 
+// K-quant matrices (vxc_kquant.cu): GGUF super-blocks kept as they are;
+// nblk = super-blocks per row, rec = bytes per super-block.
+bool vxc_is_kquant(int type);
+int vxc_kquant_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out);
+int vxc_kquant_gemv(const vxc_qmat *w, const float *x, int M, float *y, cudaStream_t st);
+
 // Tensor-core GEMV plan for M <= 64 activation rows (vxc_gemv_tc.cu).
 struct VxcGemvPlan {
     int nt;       // N / 16 (N = padded rows of the image)

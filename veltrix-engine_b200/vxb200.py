@@ -30,6 +30,7 @@ PROTOTYPES = {
     "vxc_qgemv": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]),
     "vxc_qgemv_simt": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_size_t, _vp]),
     "vxc_qgemv_noalloc": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp, _vp]),
+    "vxc_kquant_dequant": (ctypes.c_int, [_vp, _vp, _vp]),
     "vxc_device_current": (ctypes.c_int, []),
     "vxc_launch_count": (ctypes.c_longlong, []),
     "vxc_profile_enable": (None, [ctypes.c_int]),
