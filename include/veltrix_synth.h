@@ -23,7 +23,11 @@ extern "C" {
 typedef struct {
     int n_embd, n_layers, n_heads, n_kv_heads, n_ff, n_vocab;
     float rope_theta;
-    int wtype;   /* 2 = Q4_0, 8 = Q8_0 for every 2-D tensor */
+    int wtype;   /* 2 = Q4_0, 8 = Q8_0 for every 2-D tensor; or a K-quant type
+                  * 10..15 (Q2_K..Q8_K; n_embd, n_ff % 256 == 0), whose
+                  * super-blocks hold Philox bytes with fixed scale fields
+                  * (decoded weights of the order of 0.02), not quantised
+                  * normals */
 } vx_synth_config;
 
 /* Writes `path`; returns 0 or a vx_error code. */

@@ -160,12 +160,21 @@ void vxo_dequant_q8_0(const void *vx, float *y, int n) {
 static size_t row_bytes(int type, int cols) {
     if (type == T_Q4_0) return (size_t)(cols / 32) * Q4_BYTES;
     if (type == T_Q8_0) return (size_t)(cols / 32) * Q8_BYTES;
+    if (vxo_kquant_block_bytes(type)) return (size_t)(cols / 256) * vxo_kquant_block_bytes(type);
     return (size_t)cols * 4;
 }
 
+/* K-quant rows (types 10..15) decode as the reference's vx_dequantize does;
+ * their GEMV is then the f32 GEMV of every other type.  The reference's own
+ * apply_gemv runs Q2_K/Q3_K/Q4_K through int8-rounded activations
+ * (src/quantize.c:439-561, with the Q4_K dot dropping half of every
+ * super-block) and sums Q5_K/Q6_K/Q8_K in another order (:486-505); its
+ * sparse-row up projection and its embedding lookup decode as here
+ * (src/model.c:191-198, :462-496).  See oracle/vxo_kquant.c. */
 static void dequant_row(int type, const uint8_t *src, float *dst, int cols) {
     if (type == T_Q4_0) vxo_dequant_q4_0(src, dst, cols);
     else if (type == T_Q8_0) vxo_dequant_q8_0(src, dst, cols);
+    else if (vxo_kquant_block_bytes(type)) vxo_dequant_kquant(type, src, dst, cols);
     else memcpy(dst, src, (size_t)cols * 4);
 }
 

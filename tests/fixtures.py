@@ -12,6 +12,13 @@ CONFIGS = {
     # config 1: tiny Llama target / draft, all Q8_0
     "tiny_target": (256, 4, 8, 8, 768, 4096, 8, 1, 10000.0),
     "tiny_draft": (128, 2, 4, 4, 384, 4096, 8, 2, 10000.0),
+    # K-quant models at the tiny target's shape (every 2-D tensor of one type; widths % 256 == 0)
+    "tiny_q2k": (256, 2, 8, 8, 768, 4096, 10, 40, 10000.0),
+    "tiny_q3k": (256, 2, 8, 8, 768, 4096, 11, 41, 10000.0),
+    "tiny_q4k": (256, 2, 8, 8, 768, 4096, 12, 42, 10000.0),
+    "tiny_q5k": (256, 2, 8, 8, 768, 4096, 13, 43, 10000.0),
+    "tiny_q6k": (256, 2, 8, 8, 768, 4096, 14, 44, 10000.0),
+    "tiny_q8k": (256, 2, 8, 8, 768, 4096, 15, 45, 10000.0),
     # config 4 shapes, fewer layers (parity at 7B width)
     "l7b_2layer": (4096, 2, 32, 32, 11008, 32000, 2, 3, 10000.0),
     "d11b_2layer": (2048, 2, 32, 4, 5632, 32000, 8, 4, 10000.0),

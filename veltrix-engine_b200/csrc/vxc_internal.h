@@ -29,6 +29,12 @@ int vxc_synth_blocks(int type, uint64_t seed, uint32_t ti, long long row0, int n
 bool vxc_is_kquant(int type);
 int vxc_kquant_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out);
 int vxc_kquant_gemv(const vxc_qmat *w, const float *x, int M, float *y, cudaStream_t st);
+// The forward's K-quant GEMV: activations from one chunk's GEMV image (N
+// image rows, prescales xs), out[M][R]; programmatic dependent launch.
+int vxc_kquant_gemv_image(const vxc_qmat *w, const uint8_t *img, int N, const float *xs, int M, float *out,
+                          cudaStream_t st);
+// A K-quant matrix from super-blocks already in device memory (copied).
+int vxc_kquant_from_device(int type, const uint8_t *dev_blocks, int rows, int cols, vxc_qmat **out);
 
 // Tensor-core GEMV plan for M <= 64 activation rows (vxc_gemv_tc.cu).
 struct VxcGemvPlan {

@@ -19,6 +19,7 @@
 #include <climits>
 #include "vxc_common.cuh"
 #include "vxc_image.cuh"
+#include "vxc_kquant.cuh"
 #include "vxc_ptx.cuh"
 #include "vxc_qmat.cuh"
 #include "vxc_internal.h"
@@ -103,6 +104,12 @@ __global__ void k_embed(const uint8_t *__restrict__ embd, int type, size_t row_b
     if (type == 0) {
         const float *f = reinterpret_cast<const float *>(row);
         for (int i = threadIdx.x; i < E; i += blockDim.x) xr[i] = f[i];
+        return;
+    }
+    if (type >= 10 && type <= 15) {   // K-quant rows of E / 256 super-blocks (src/model.c:462-496)
+        const int bb = vxc_kq_block_bytes(type);
+        for (int i = threadIdx.x; i < E; i += blockDim.x)
+            xr[i] = vxc_kq_decode_any(type, row + (size_t)(i / VXC_QK_K) * bb, i % VXC_QK_K);
         return;
     }
     // one thread per element: block b = i/32 (src/quantize.c:578-591, :642-651)
@@ -665,6 +672,7 @@ __global__ void k_part_out(Part p, int n_rows, float *__restrict__ out) {
 static size_t row_bytes_of(int type, int cols) {
     if (type == 2) return (size_t)(cols / 32) * 18;
     if (type == 8) return (size_t)(cols / 32) * 34;
+    if (vxc_is_kquant(type)) return (size_t)(cols / VXC_QK_K) * vxc_kq_block_bytes(type);
     return (size_t)cols * 4;
 }
 
@@ -697,6 +705,10 @@ struct NetSource {
 
 static size_t block_bytes(int type) { return type == 2 ? 18 : 34; }
 
+// Columns per quantisation block: 32 (Q4_0, Q8_0) or 256 (K-quant super-blocks).
+static int block_cols(int type) { return vxc_is_kquant(type) ? VXC_QK_K : 32; }
+static size_t unit_bytes(int type) { return vxc_is_kquant(type) ? (size_t)vxc_kq_block_bytes(type) : block_bytes(type); }
+
 // Weights in host memory (GGUF views, e.g. an mmap'd file).
 struct HostSource : NetSource {
     const vxc_tensor_view *tok, *onorm, *output;
@@ -718,7 +730,11 @@ struct HostSource : NetSource {
     }
     int blocks(int ti, int r0, int nr, int b0, int nb, uint8_t *dev) const override {
         const vxc_tensor_view *t = view(ti);
-        const size_t bb = block_bytes(t->type), nbf = (size_t)t->cols / 32, rb = nbf * bb;
+        // b0, nb count 32-column blocks; a K-quant tensor moves whole super-blocks of 8 of them
+        const int per = block_cols(t->type) / 32;
+        b0 /= per;
+        nb /= per;
+        const size_t bb = unit_bytes(t->type), nbf = (size_t)t->cols / block_cols(t->type), rb = nbf * bb;
         const uint8_t *src = (const uint8_t *)t->data;
         cudaError_t e;
         if (b0 == 0 && (size_t)nb == nbf) {
@@ -796,8 +812,12 @@ static int upload_pieces(const NetSource &src, const Piece *p, int n, vxc_qmat *
         int t, r, c;
         src.shape(p[i].ti, &t, &r, &c);
         if (t < 0) { vxc_set_error("fused matrix parts differ in type/shape or are missing"); return -7; }
-        if (t != 2 && t != 8) {
-            vxc_set_error("weight type %d not supported on the device (Q4_0 / Q8_0 only)", t);
+        if (t != 2 && t != 8 && !vxc_is_kquant(t)) {
+            vxc_set_error("weight type %d not supported on the device (Q4_0, Q8_0, Q2_K..Q8_K)", t);
+            return -7;
+        }
+        if (vxc_is_kquant(t) && (p[i].b0 % 8 || p[i].nb % 8)) {
+            vxc_set_error("K-quant matrix slices must be whole 256-column super-blocks");
             return -7;
         }
         if ((i > 0 && (t != type || p[i].nb != p[0].nb)) || p[i].r0 + p[i].nr > r || p[i].b0 + p[i].nb > c / 32) {
@@ -807,9 +827,9 @@ static int upload_pieces(const NetSource &src, const Piece *p, int n, vxc_qmat *
         type = t;
         rows += p[i].nr;
     }
-    const size_t bb = block_bytes(type);
+    const size_t per = (size_t)block_cols(type) / 32, bb = unit_bytes(type);   // per staging unit
     uint8_t *staging = NULL;
-    if (cudaMalloc((void **)&staging, (size_t)rows * p[0].nb * bb) != cudaSuccess) {
+    if (cudaMalloc((void **)&staging, (size_t)rows * (p[0].nb / per) * bb) != cudaSuccess) {
         vxc_set_error("vxc_net_create: out of device memory");
         return -3;
     }
@@ -817,9 +837,11 @@ static int upload_pieces(const NetSource &src, const Piece *p, int n, vxc_qmat *
     size_t off = 0;
     for (int i = 0; i < n && rc == 0; i++) {
         rc = src.blocks(p[i].ti, p[i].r0, p[i].nr, p[i].b0, p[i].nb, staging + off);
-        off += (size_t)p[i].nr * p[i].nb * bb;
+        off += (size_t)p[i].nr * (p[i].nb / per) * bb;
     }
-    if (rc == 0) rc = vxc_qmat_from_device(type, staging, rows, p[0].nb * 32, out);
+    if (rc == 0)
+        rc = vxc_is_kquant(type) ? vxc_kquant_from_device(type, staging, rows, p[0].nb * 32, out)
+                                 : vxc_qmat_from_device(type, staging, rows, p[0].nb * 32, out);
     cudaFree(staging);
     return rc;
 }
@@ -869,6 +891,10 @@ static int net_build(const vxc_net_config *cfg, const NetSource &src, const vxc_
     if (et < 0 || ec != E || er <= 0) {
         vxc_set_error("vxc_net_create: token embedding missing or not %d wide", E);
         return -4;
+    }
+    if (et != 0 && et != 2 && et != 8 && !(vxc_is_kquant(et) && E % VXC_QK_K == 0)) {
+        vxc_set_error("vxc_net_create: token embedding type %d (width %d) not supported", et, E);
+        return -7;
     }
     vxc_net *n = (vxc_net *)calloc(1, sizeof(vxc_net));
     n->cfg = *cfg;
@@ -1122,6 +1148,10 @@ static cudaError_t launch_pdl_cluster(void (*k)(KArgs...), dim3 grid, dim3 block
 static size_t part_slot_floats(const vxc_net *n) {
     size_t best = 0;
     auto consider = [&](const vxc_qmat *w) {
+        if (vxc_is_kquant(w->type)) {   // one slice [64][R]
+            if ((size_t)64 * w->rows > best) best = (size_t)64 * w->rows;
+            return;
+        }
         for (int m = 1; m <= 64; m++) {
             VxcGemvPlan p;
             if (vxc_gemv_plan(w, m, &p)) {
@@ -1279,6 +1309,16 @@ static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStrea
     p.R = w->rows;
     p.M = M;
     p.ks_full = p.ks_last = 1;
+    if (vxc_is_kquant(w->type)) {   // CUDA-core K-quant GEMV on the same image, one slice
+        for (int c = 0; c * 64 < M; c++) {
+            const int Mc = M - c * 64 < 64 ? M - c * 64 : 64;
+            int rc = vxc_kquant_gemv_image(w, s->img + c * s->img_chunk, vxc_img_rows(Mc), s->xs + c * 64, Mc,
+                                           s->part + c * s->part_slot, st);
+            if (rc) return rc;
+        }
+        *out = p;
+        return 0;
+    }
     for (int c = 0; c * 64 < M; c++) {
         const int Mc = M - c * 64 < 64 ? M - c * 64 : 64;
         VxcGemvPlan pl;

@@ -78,6 +78,39 @@ static void quant_block(int type, const float *x, uint8_t *b) {
     }
 }
 
+/* K-quant super-blocks (256 weights; types 10..15 = Q2_K..Q8_K, layouts of
+ * the reference's include/quantize.h:47-93).  Their quantised bytes are
+ * Philox words keyed by (seed, tensor, super-block); the scale fields are
+ * fixed per type so that the decoded weights are of the order of 0.02
+ * (a valid block of any content decodes to finite weights). */
+static int kq_bytes(int type) {
+    return type == 10 ? 84 : type == 11 ? 110 : type == 12 ? 144 : type == 13 ? 176 : type == 14 ? 210
+         : type == 15 ? 292 : 0;
+}
+
+static void put_h(uint8_t *b, float v) {
+    uint16_t h = f2h_trunc(v);
+    b[0] = (uint8_t)h;
+    b[1] = (uint8_t)(h >> 8);
+}
+
+static void kq_block(int type, uint64_t seed, uint32_t ti, uint64_t blk, uint8_t *b) {
+    const int n = kq_bytes(type);
+    for (int w = 0; w * 16 < n; w++) {
+        uint32_t r[4];
+        philox((uint32_t)blk, (uint32_t)(blk >> 32), ti, 0xB10C0000u + (uint32_t)w, seed, r);
+        for (int k = 0; k < 16 && w * 16 + k < n; k++) b[w * 16 + k] = (uint8_t)(r[k / 4] >> (8 * (k % 4)));
+    }
+    switch (type) {
+    case 10: put_h(b + 80, 0.004f); put_h(b + 82, 0.004f); break;      /* d, dmin */
+    case 11: put_h(b + 108, 0.0006f); break;                          /* d */
+    case 12: put_h(b, 1.3e-4f); put_h(b + 2, 9.75e-4f); break;         /* d, dmin */
+    case 13: put_h(b, 7e-5f); put_h(b + 2, 1.085e-3f); break;          /* d, dmin */
+    case 14: put_h(b + 208, 6.2e-5f); break;                          /* d (smallest normal fp16 is 6.1e-5) */
+    default: { const float d = 3e-4f; memcpy(b, &d, 4); } break;     /* Q8_K: float d */
+    }
+}
+
 typedef struct { char name[64]; int nd; uint64_t ne0, ne1; int type; uint64_t off, bytes; } tinfo;
 
 static void wr(FILE *f, const void *p, size_t n) { fwrite(p, 1, n, f); }
@@ -91,8 +124,9 @@ static void pad32(FILE *f) {
 }
 
 int vx_synth_write_gguf(const char *path, const vx_synth_config *c, uint64_t seed) {
+    const int kq = kq_bytes(c ? c->wtype : 0) > 0;
     if (!path || !c || c->n_embd % 32 || c->n_ff % 32 || c->n_heads <= 0 || c->n_kv_heads <= 0 ||
-        (c->wtype != 2 && c->wtype != 8))
+        (c->wtype != 2 && c->wtype != 8 && !kq) || (kq && (c->n_embd % 256 || c->n_ff % 256)))
         return VX_ERR_PARAM;
     const int hd = c->n_embd / c->n_heads, kvd = c->n_kv_heads * hd;
     const int nt = 9 * c->n_layers + 3;
@@ -118,7 +152,9 @@ int vx_synth_write_gguf(const char *path, const vx_synth_config *c, uint64_t see
     uint64_t off = 0;
     for (int i = 0; i < nt; i++) {
         uint64_t n = t[i].ne0 * t[i].ne1;
-        t[i].bytes = t[i].type == 0 ? n * 4 : (n / 32) * (t[i].type == 8 ? 34 : 18);
+        t[i].bytes = t[i].type == 0 ? n * 4
+                   : kq_bytes(t[i].type) ? (n / 256) * (uint64_t)kq_bytes(t[i].type)
+                   : (n / 32) * (t[i].type == 8 ? 34 : 18);
         t[i].off = off;
         off += (t[i].bytes + 31) & ~31ull;
     }
@@ -153,6 +189,11 @@ int vx_synth_write_gguf(const char *path, const vx_synth_config *c, uint64_t see
         if (t[i].type == 0) {
             float *fb = (float *)buf;
             for (uint64_t j = 0; j < t[i].ne0 * t[i].ne1; j++) fb[j] = 1.0f;
+        } else if (kq_bytes(t[i].type)) {
+            const int64_t nsb = (int64_t)(t[i].ne0 * t[i].ne1 / 256);
+            const int bb = kq_bytes(t[i].type);
+#pragma omp parallel for schedule(static) num_threads(omp_get_num_procs())
+            for (int64_t b = 0; b < nsb; b++) kq_block(t[i].type, seed, (uint32_t)i, (uint64_t)b, buf + (size_t)b * bb);
         } else {
             const int64_t nblk = (int64_t)(t[i].ne0 * t[i].ne1 / 32);
             const size_t bb = t[i].type == 8 ? 34 : 18;
