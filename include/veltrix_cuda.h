@@ -67,7 +67,9 @@ typedef struct vxc_qmat vxc_qmat;
  * blocks of 84/110/144/176/210/292 bytes) are kept as GGUF super-blocks:
  * vxc_qgemv then decodes each weight as the reference does and sums in fp32
  * (the reference's blockwise GEMV, src/quantize.c:486-505; it needs no
- * workspace).  Models with K-quant matrices are not loaded yet. */
+ * workspace).  Nets may hold K-quant matrices and a K-quant token
+ * embedding when every split is whole super-blocks and the parts fused into
+ * one matrix (Q/K/V, gate/up) share one type. */
 int vxc_qmat_create(int type, const void *host_blocks, int rows, int cols, vxc_qmat **out);
 /* Decoded weights of a K-quant matrix, fp32 [rows][cols] in device memory,
  * bit for bit the reference's vx_dequantize_row_* for the type. */
