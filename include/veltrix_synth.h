@@ -27,8 +27,11 @@ typedef struct {
                   * 10..15 (Q2_K..Q8_K; n_embd, n_ff % 256 == 0), whose
                   * super-blocks hold Philox bytes with fixed scale fields
                   * (decoded weights of the order of 0.02), not quantised
-                  * normals */
+                  * normals; or VX_SYNTH_KQ_MIX: Q4_K, with Q6_K for
+                  * attn_v, ffn_down and the LM head */
 } vx_synth_config;
+
+#define VX_SYNTH_KQ_MIX 100
 
 /* Writes `path`; returns 0 or a vx_error code. */
 int vx_synth_write_gguf(const char *path, const vx_synth_config *cfg, uint64_t seed);

@@ -19,6 +19,8 @@ CONFIGS = {
     "tiny_q5k": (256, 2, 8, 8, 768, 4096, 13, 43, 10000.0),
     "tiny_q6k": (256, 2, 8, 8, 768, 4096, 14, 44, 10000.0),
     "tiny_q8k": (256, 2, 8, 8, 768, 4096, 15, 45, 10000.0),
+    # Q4_K with Q6_K value, down and LM-head tensors (VX_SYNTH_KQ_MIX)
+    "tiny_kqmix": (256, 2, 8, 8, 768, 4096, 100, 46, 10000.0),
     # config 4 shapes, fewer layers (parity at 7B width)
     "l7b_2layer": (4096, 2, 32, 32, 11008, 32000, 2, 3, 10000.0),
     "d11b_2layer": (2048, 2, 32, 4, 5632, 32000, 8, 4, 10000.0),

@@ -53,3 +53,9 @@ def test_q3k_reference_rounds_activations():
 @pytest.mark.parametrize("name", ["tiny_q2k", "tiny_q4k"])
 def test_q2k_q4k_reference_gemv_disagrees_with_its_dequant(name):
     assert both(name) > 0.5
+
+
+def test_mixed_q4k_q6k_model_loads_in_the_oracle():
+    """The Q4_K/Q6_K mix (value, down and LM head in Q6_K) decodes to finite
+    logits; the reference's Q4_K GEMV (KQ2) makes its own differ."""
+    assert both("tiny_kqmix") > 0.1

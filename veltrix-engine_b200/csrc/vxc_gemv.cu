@@ -174,6 +174,8 @@ extern "C" int vxc_qmat_create(int type, const void *host_blocks, int rows, int 
 
 extern "C" void vxc_qmat_destroy(vxc_qmat *w) {
     if (!w) return;
+    if (w->type == VXC_QMAT_STACK)
+        for (int i = 0; i < w->nparts; i++) vxc_qmat_destroy(w->parts[i]);
     if (w->qs) cudaFree(w->qs);
     free(w);
 }

@@ -35,6 +35,9 @@ int vxc_kquant_gemv_image(const vxc_qmat *w, const uint8_t *img, int N, const fl
                           cudaStream_t st);
 // A K-quant matrix from super-blocks already in device memory (copied).
 int vxc_kquant_from_device(int type, const uint8_t *dev_blocks, int rows, int cols, vxc_qmat **out);
+// K-quant matrices of different types stacked by rows (type VXC_QMAT_STACK;
+// takes ownership of the parts).  The forward runs it like a K-quant matrix.
+int vxc_kquant_stack(vxc_qmat **parts, int n, vxc_qmat **out);
 
 // Tensor-core GEMV plan for M <= 64 activation rows (vxc_gemv_tc.cu).
 struct VxcGemvPlan {

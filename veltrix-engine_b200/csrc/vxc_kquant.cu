@@ -68,11 +68,12 @@ __global__ void __launch_bounds__(256) k_gemv_kq(const uint8_t *__restrict__ w, 
 // Forward-pass variant: the activations are the GEMV image of one chunk of
 // up to 64 rows (layout in vxc_qmat.cuh): element k of row m is
 // (hi + lo) / xs[m], where hi + lo is exact in fp32 and xs[m] a power of two.
-// out[m][r] for m < M, one slice (no split-K).
+// out[m * ldo + r] for m < M, one slice (no split-K).
 template <int T>
 __global__ void __launch_bounds__(256) k_gemv_kq_img(const uint8_t *__restrict__ w, int R, int nb,
                                                      const uint8_t *__restrict__ img, int N,
-                                                     const float *__restrict__ xs, int M, float *__restrict__ out) {
+                                                     const float *__restrict__ xs, int M, float *__restrict__ out,
+                                                     int ldo) {
     pdl_trigger();
     pdl_wait();
     constexpr int BB = vxc_kq_block_bytes(T);
@@ -105,13 +106,13 @@ __global__ void __launch_bounds__(256) k_gemv_kq_img(const uint8_t *__restrict__
         for (int mm = 0; mm < 8; mm++) {
             float v = acc[mm];
             for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && mm < mc) out[(size_t)(m0 + mm) * R + r] = v / xs[m0 + mm];
+            if (lane == 0 && mm < mc) out[(size_t)(m0 + mm) * ldo + r] = v / xs[m0 + mm];
         }
     }
 }
 
 template <int T>
-cudaError_t launch_img(const vxc_qmat *w, const uint8_t *img, int N, const float *xs, int M, float *out,
+cudaError_t launch_img(const vxc_qmat *w, const uint8_t *img, int N, const float *xs, int M, float *out, int ldo,
                        cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((size_t)w->rows * 32 + 255) / 256));
@@ -123,27 +124,54 @@ cudaError_t launch_img(const vxc_qmat *w, const uint8_t *img, int N, const float
     cfg.attrs = at;
     cfg.numAttrs = 1;
     const uint8_t *q = w->qs;
-    return cudaLaunchKernelEx(&cfg, k_gemv_kq_img<T>, q, w->rows, w->nblk, img, N, xs, M, out);
+    return cudaLaunchKernelEx(&cfg, k_gemv_kq_img<T>, q, w->rows, w->nblk, img, N, xs, M, out, ldo);
 }
 
 }  // namespace
 
-int vxc_kquant_gemv_image(const vxc_qmat *w, const uint8_t *img, int N, const float *xs, int M, float *out,
+static int gemv_image_one(const vxc_qmat *w, const uint8_t *img, int N, const float *xs, int M, float *out, int ldo,
                           cudaStream_t st) {
     cudaError_t e;
     switch (w->type) {
-    case 10: e = launch_img<10>(w, img, N, xs, M, out, st); break;
-    case 11: e = launch_img<11>(w, img, N, xs, M, out, st); break;
-    case 12: e = launch_img<12>(w, img, N, xs, M, out, st); break;
-    case 13: e = launch_img<13>(w, img, N, xs, M, out, st); break;
-    case 14: e = launch_img<14>(w, img, N, xs, M, out, st); break;
-    default: e = launch_img<15>(w, img, N, xs, M, out, st); break;
+    case 10: e = launch_img<10>(w, img, N, xs, M, out, ldo, st); break;
+    case 11: e = launch_img<11>(w, img, N, xs, M, out, ldo, st); break;
+    case 12: e = launch_img<12>(w, img, N, xs, M, out, ldo, st); break;
+    case 13: e = launch_img<13>(w, img, N, xs, M, out, ldo, st); break;
+    case 14: e = launch_img<14>(w, img, N, xs, M, out, ldo, st); break;
+    default: e = launch_img<15>(w, img, N, xs, M, out, ldo, st); break;
     }
     vxc_count_launches(1);
     if (e != cudaSuccess) {
         vxc_set_error("vxc_forward: K-quant GEMV: %s", cudaGetErrorString(e));
         return -3;
     }
+    return 0;
+}
+
+int vxc_kquant_gemv_image(const vxc_qmat *w, const uint8_t *img, int N, const float *xs, int M, float *out,
+                          cudaStream_t st) {
+    if (w->type != VXC_QMAT_STACK) return gemv_image_one(w, img, N, xs, M, out, w->rows, st);
+    for (int i = 0; i < w->nparts; i++) {
+        int rc = gemv_image_one(w->parts[i], img, N, xs, M, out + w->part_row0[i], w->rows, st);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+int vxc_kquant_stack(vxc_qmat **parts, int n, vxc_qmat **out) {
+    if (n < 1 || n > 3) { vxc_set_error("vxc_net_create: 1 to 3 stacked parts"); return -4; }
+    vxc_qmat *w = (vxc_qmat *)calloc(1, sizeof(vxc_qmat));
+    if (!w) { vxc_set_error("vxc_net_create: out of host memory"); return -3; }
+    w->type = VXC_QMAT_STACK;
+    w->cols = parts[0]->cols;
+    w->nparts = n;
+    for (int i = 0; i < n; i++) {
+        w->parts[i] = parts[i];
+        w->part_row0[i] = w->rows;
+        w->rows += parts[i]->rows;
+        w->qs_bytes += parts[i]->qs_bytes;
+    }
+    *out = w;
     return 0;
 }
 

@@ -820,9 +820,24 @@ static int upload_pieces(const NetSource &src, const Piece *p, int n, vxc_qmat *
             vxc_set_error("K-quant matrix slices must be whole 256-column super-blocks");
             return -7;
         }
-        if ((i > 0 && (t != type || p[i].nb != p[0].nb)) || p[i].r0 + p[i].nr > r || p[i].b0 + p[i].nb > c / 32) {
-            vxc_set_error("fused matrix parts differ in type/shape or are missing");
+        if ((i > 0 && p[i].nb != p[0].nb) || p[i].r0 + p[i].nr > r || p[i].b0 + p[i].nb > c / 32) {
+            vxc_set_error("fused matrix parts differ in shape or are missing");
             return -7;
+        }
+        if (i > 0 && t != type) {
+            // parts of different K-quant types (e.g. Q4_K query/key with Q6_K value rows) stay
+            // separate matrices, stacked by rows
+            if (!vxc_is_kquant(t) || !vxc_is_kquant(type)) {
+                vxc_set_error("fused matrix parts differ in type (%d, %d)", type, t);
+                return -7;
+            }
+            vxc_qmat *parts[3] = {NULL, NULL, NULL};
+            int rc = n > 3 ? -4 : 0;
+            for (int k = 0; k < n && rc == 0; k++) rc = upload_pieces(src, &p[k], 1, &parts[k]);
+            if (rc == 0) rc = vxc_kquant_stack(parts, n, out);
+            if (rc)
+                for (int k = 0; k < n; k++) vxc_qmat_destroy(parts[k]);
+            return rc;
         }
         type = t;
         rows += p[i].nr;
@@ -1148,7 +1163,7 @@ static cudaError_t launch_pdl_cluster(void (*k)(KArgs...), dim3 grid, dim3 block
 static size_t part_slot_floats(const vxc_net *n) {
     size_t best = 0;
     auto consider = [&](const vxc_qmat *w) {
-        if (vxc_is_kquant(w->type)) {   // one slice [64][R]
+        if (vxc_is_kquant(w->type) || w->type == VXC_QMAT_STACK) {   // one slice [64][R]
             if ((size_t)64 * w->rows > best) best = (size_t)64 * w->rows;
             return;
         }
@@ -1309,7 +1324,7 @@ static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStrea
     p.R = w->rows;
     p.M = M;
     p.ks_full = p.ks_last = 1;
-    if (vxc_is_kquant(w->type)) {   // CUDA-core K-quant GEMV on the same image, one slice
+    if (vxc_is_kquant(w->type) || w->type == VXC_QMAT_STACK) {   // CUDA-core K-quant GEMV, one slice
         for (int c = 0; c * 64 < M; c++) {
             const int Mc = M - c * 64 < 64 ? M - c * 64 : 64;
             int rc = vxc_kquant_gemv_image(w, s->img + c * s->img_chunk, vxc_img_rows(Mc), s->xs + c * 64, Mc,

@@ -40,7 +40,7 @@
 #define VXC_TILE_ROWS 128
 
 struct vxc_qmat {
-    int type;           // 2 = Q4_0, 8 = Q8_0
+    int type;           // 2 = Q4_0, 8 = Q8_0; 10..15 K-quant; VXC_QMAT_STACK: parts below
     int rows, cols;     // R, K (K % 32 == 0)
     int nblk;           // K / 32
     int ntile;          // ceil(R / 128)
@@ -50,7 +50,14 @@ struct vxc_qmat {
     float wscale;       // 2^-wshift
     uint8_t *qs;        // device records
     size_t qs_bytes;
+    // VXC_QMAT_STACK: K-quant matrices of different types stacked by rows
+    // (e.g. Q4_K query/key and Q6_K value rows); part i fills output rows
+    // [part_row0[i], part_row0[i] + parts[i]->rows)
+    int nparts;
+    vxc_qmat *parts[3];
+    int part_row0[3];
 };
+#define VXC_QMAT_STACK 100
 
 // Image bytes of one 32-column block for N padded rows.
 __host__ __device__ static inline size_t vxc_img_block_bytes(int N) { return (size_t)N * 128; }

@@ -124,9 +124,13 @@ static void pad32(FILE *f) {
 }
 
 int vx_synth_write_gguf(const char *path, const vx_synth_config *c, uint64_t seed) {
-    const int kq = kq_bytes(c ? c->wtype : 0) > 0;
+    /* wtype VX_SYNTH_KQ_MIX: Q4_K everywhere except Q6_K for attn_v, ffn_down
+     * and the LM head, the split of common Q4_K_M GGUF files */
+    const int mix = c && c->wtype == VX_SYNTH_KQ_MIX;
+    const int wt = mix ? 12 : c ? c->wtype : 0, wt6 = mix ? 14 : wt;
+    const int kq = kq_bytes(wt) > 0;
     if (!path || !c || c->n_embd % 32 || c->n_ff % 32 || c->n_heads <= 0 || c->n_kv_heads <= 0 ||
-        (c->wtype != 2 && c->wtype != 8 && !kq) || (kq && (c->n_embd % 256 || c->n_ff % 256)))
+        (wt != 2 && wt != 8 && !kq) || (kq && (c->n_embd % 256 || c->n_ff % 256)))
         return VX_ERR_PARAM;
     const int hd = c->n_embd / c->n_heads, kvd = c->n_kv_heads * hd;
     const int nt = 9 * c->n_layers + 3;
@@ -136,18 +140,18 @@ int vx_synth_write_gguf(const char *path, const vx_synth_config *c, uint64_t see
     char nm[64];
     for (int l = 0; l < c->n_layers; l++) {
         snprintf(nm, 64, "blk.%d.attn_norm.weight", l); ADD(nm, 1, c->n_embd, 1, 0);
-        snprintf(nm, 64, "blk.%d.attn_q.weight", l); ADD(nm, 2, c->n_embd, c->n_embd, c->wtype);
-        snprintf(nm, 64, "blk.%d.attn_k.weight", l); ADD(nm, 2, c->n_embd, kvd, c->wtype);
-        snprintf(nm, 64, "blk.%d.attn_v.weight", l); ADD(nm, 2, c->n_embd, kvd, c->wtype);
-        snprintf(nm, 64, "blk.%d.attn_output.weight", l); ADD(nm, 2, c->n_embd, c->n_embd, c->wtype);
+        snprintf(nm, 64, "blk.%d.attn_q.weight", l); ADD(nm, 2, c->n_embd, c->n_embd, wt);
+        snprintf(nm, 64, "blk.%d.attn_k.weight", l); ADD(nm, 2, c->n_embd, kvd, wt);
+        snprintf(nm, 64, "blk.%d.attn_v.weight", l); ADD(nm, 2, c->n_embd, kvd, wt6);
+        snprintf(nm, 64, "blk.%d.attn_output.weight", l); ADD(nm, 2, c->n_embd, c->n_embd, wt);
         snprintf(nm, 64, "blk.%d.ffn_norm.weight", l); ADD(nm, 1, c->n_embd, 1, 0);
-        snprintf(nm, 64, "blk.%d.ffn_gate.weight", l); ADD(nm, 2, c->n_embd, c->n_ff, c->wtype);
-        snprintf(nm, 64, "blk.%d.ffn_up.weight", l); ADD(nm, 2, c->n_embd, c->n_ff, c->wtype);
-        snprintf(nm, 64, "blk.%d.ffn_down.weight", l); ADD(nm, 2, c->n_ff, c->n_embd, c->wtype);
+        snprintf(nm, 64, "blk.%d.ffn_gate.weight", l); ADD(nm, 2, c->n_embd, c->n_ff, wt);
+        snprintf(nm, 64, "blk.%d.ffn_up.weight", l); ADD(nm, 2, c->n_embd, c->n_ff, wt);
+        snprintf(nm, 64, "blk.%d.ffn_down.weight", l); ADD(nm, 2, c->n_ff, c->n_embd, wt6);
     }
-    ADD("token_embd.weight", 2, c->n_embd, c->n_vocab, c->wtype);
+    ADD("token_embd.weight", 2, c->n_embd, c->n_vocab, wt);
     ADD("output_norm.weight", 1, c->n_embd, 1, 0);
-    ADD("output.weight", 2, c->n_embd, c->n_vocab, c->wtype);
+    ADD("output.weight", 2, c->n_embd, c->n_vocab, wt6);
 #undef ADD
     uint64_t off = 0;
     for (int i = 0; i < nt; i++) {
