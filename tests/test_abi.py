@@ -69,3 +69,25 @@ def test_no_device_fails_loudly():
     assert b"no CUDA device" in L.vxc_error_string()
     h = ctypes.c_void_p()
     assert L.vx_model_create(b"/nonexistent.gguf", ctypes.byref(h)) != 0
+    # the additive entry points fail the same way
+    cfg = vxb200.SynthConfig(256, 2, 8, 8, 768, 4096, 10000.0, 2)
+    assert L.vx_model_create_synth(ctypes.byref(cfg), 1, 0, 1, None, ctypes.byref(h)) != 0
+    assert L.vx_model_create_tp(b"/nonexistent.gguf", 0, 2, b"\0" * 128, ctypes.byref(h)) != 0
+
+
+def test_additive_entry_points_check_arguments():
+    """Argument errors are reported before any device work (vx_error codes)."""
+    import vxb200
+    L = vxb200.lib()
+    h = ctypes.c_void_p()
+    VX_ERR_PARAM = -4
+    cfg = vxb200.SynthConfig(256, 2, 8, 8, 768, 4096, 10000.0, 2)
+    assert L.vx_model_create_tp(None, 0, 2, b"\0" * 128, ctypes.byref(h)) == VX_ERR_PARAM
+    assert L.vx_model_create_tp(b"x.gguf", 2, 2, b"\0" * 128, ctypes.byref(h)) == VX_ERR_PARAM   # rank >= world
+    assert L.vx_model_create_tp(b"x.gguf", 0, 2, None, ctypes.byref(h)) == VX_ERR_PARAM
+    assert L.vx_model_create_synth(ctypes.byref(cfg), 1, 0, 2, None, ctypes.byref(h)) == VX_ERR_PARAM  # no id
+    assert L.vx_model_create_synth(None, 1, 0, 1, None, ctypes.byref(h)) == VX_ERR_PARAM
+    assert L.vx_model_generate_greedy(None, None, 0, None, 1, -1) == VX_ERR_PARAM
+    # the writer rejects K-quant widths that are not whole super-blocks
+    bad = vxb200.SynthConfig(128, 1, 4, 4, 384, 256, 10000.0, 12)
+    assert L.vx_synth_write_gguf(b"/tmp/never_written.gguf", ctypes.byref(bad), 1) == VX_ERR_PARAM
