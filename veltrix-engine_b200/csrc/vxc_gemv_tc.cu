@@ -8,12 +8,11 @@
 // significant bits, so it is exactly w_hi + w_lo with w_hi = RN_fp16(w) and
 // w_lo = w - w_hi (computed by one fused fp16 multiply-add).  The activation
 // row is prescaled by a power of two and split into fp16 hi + lo (22
-// significant bits; the image layout is in vxc_qmat.cuh).  Three kind::f16
-// MMAs per K step, w_hi*x_hi + w_hi*x_lo + w_lo*x_hi, accumulate in fp32
-// TMEM over the whole K-slice; the dropped w_lo*x_lo term is below 2^-22 of
-// each product, i.e. fp32 rounding level.  A single fp16 weight or activation
-// would move the logits by ~1e-3 relative through the FFN's |silu| < 0.01
-// row mask (reference src/model.c:583-585).
+// significant bits; the image layout is in vxc_qmat.cuh).  The products are
+// accumulated in fp32 TMEM over the whole K-slice (MMA shape below), so the
+// result equals the fp32 reference up to summation order.  A single fp16
+// weight or activation would move the logits by ~1e-3 relative through the
+// FFN's |silu| < 0.01 row mask (reference src/model.c:583-585).
 //
 // Work split.  Items are (128-row tile, K-slice of nbs blocks).  CTA c owns
 // slice c % ks and the tiles c / ks, c / ks + cps, ...  (cps = CTAs per
@@ -30,17 +29,21 @@
 // epilogue adds column m and N + m.
 //
 // Warp roles (448 threads, one CTA per SM):
-//   warp 0      producer: cp.async.bulk of KB weight records per stage into a
-//               ring of RS stages (weights first: they do not depend on the
-//               preceding kernel), then the image slice after griddepcontrol.wait
+//   warp 0      producer: cp.async.bulk of KB weight records per stage into
+//               the two groups' halves of a ring of RS stages (weights first:
+//               they do not depend on the preceding kernel), then the image
+//               slice after griddepcontrol.wait
 //   warp 1      TMEM owner
 //   warps 2-9   two converter groups (even / odd stages): thread = weight row;
 //               raw quants -> w_hi, w_lo fp16 -> tcgen05.st into the group's
-//               TMEM A buffer (A operand read from TMEM by the MMA)
-//   warps 10-13 lane 0 of the first NI: MMA issuers, issuer i taking blocks
-//               i, i+NI, ... of the slice into its own accumulator; then all
-//               four warps run the epilogue (tcgen05.ld, sum, scale, store)
-// TMEM: A buffers 2 x KB*32 columns, NI accumulators x 2N columns.  No TMA
+//               TMEM A buffer (A operand read from TMEM by the MMA).  Lane 0
+//               of the group's first IG warps then issues the MMAs of the
+//               stage, issuer i taking blocks i, i+IG, ... into its own
+//               accumulator
+//   warps 10-13 epilogue: zero the accumulators for the next item, then
+//               tcgen05.ld, sum the 2*IG accumulators in a fixed order, scale,
+//               store
+// TMEM: A buffers 2 x KB*32 columns, 2*IG accumulators x 2N columns.  No TMA
 // multicast anywhere.
 //
 // Every mbarrier wait is bounded (VXC_WAIT_NS); on expiry the CTA records an
