@@ -15,7 +15,14 @@
 // RoPE uses a host-built (cos, sin) table computed exactly as the reference
 // does (freq = 1/powf(theta, 2i/hd), val = pos*freq, cosf/sinf), and the
 // rotation is written with explicitly rounded ops, so it matches the
-// reference bit-for-bit.  The KV cache is fp32 ([layer][slot][pos][kv_dim]).
+// reference bit-for-bit.  The KV cache is fp32, head-major
+// ([layer][slot][kv head][pos][hd]).
+//
+// Weights are Q4_0/Q8_0 (tensor-core GEMV, vxc_gemv_tc.cu) or K-quant
+// (CUDA-core GEMV on the same activation image, vxc_kquant.cu).  Under tensor
+// parallelism (vxc_tp.cu) a net holds this GPU's heads, FFN columns and
+// vocabulary rows; the forward then all-reduces the output and down
+// projections and gathers the logits, so every GPU ends with the same rows.
 #include <climits>
 #include "vxc_common.cuh"
 #include "vxc_image.cuh"
