@@ -180,7 +180,7 @@ int vxc_net_config_get(const vxc_net *net, vxc_net_config *cfg);
 size_t vxc_net_weight_bytes(const vxc_net *net);
 
 /* KV cache for n_slots independent sequences of up to max_ctx positions
- * (fp32, [layer][slot][pos][kv_dim] — reference src/model.c:404-411 keeps
+ * (fp32, [layer][slot][kv head][pos][head_dim] — reference src/model.c:404-411 keeps
  * one [layer][n_ctx][kv_dim] cache per model) plus work buffers for up to
  * max_rows rows per forward call. */
 int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int max_rows, vxc_seqs **out);
