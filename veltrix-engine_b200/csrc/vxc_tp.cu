@@ -17,28 +17,23 @@ static_assert(sizeof(ncclUniqueId) == VXC_TP_ID_BYTES, "NCCL unique id size");
 namespace {
 struct Nccl {
     bool ok = false;
-    ncclResult_t (*get_unique_id)(ncclUniqueId *);
-    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
-    ncclResult_t (*comm_destroy)(ncclComm_t);
-    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
-    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
-    const char *(*error_string)(ncclResult_t);
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
 };
 
-const Nccl *nccl() {
-    static Nccl n;
-    static bool tried = false;
-    if (tried) return n.ok ? &n : NULL;
-    tried = true;
+Nccl load_nccl() {
+    Nccl n;
     // connect every channel at communicator creation, not lazily at a first
     // collective that may sit inside a CUDA-graph capture (kept if the caller set it)
     setenv("NCCL_RUNTIME_CONNECT", "0", 0);
     void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
     if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
-    if (!h) {
-        vxc_set_error("tensor parallelism needs libnccl.so.2: %s", dlerror());
-        return NULL;
-    }
+    if (!h) return n;
     n.get_unique_id = (decltype(n.get_unique_id))dlsym(h, "ncclGetUniqueId");
     n.comm_init_rank = (decltype(n.comm_init_rank))dlsym(h, "ncclCommInitRank");
     n.comm_destroy = (decltype(n.comm_destroy))dlsym(h, "ncclCommDestroy");
@@ -46,7 +41,14 @@ const Nccl *nccl() {
     n.all_gather = (decltype(n.all_gather))dlsym(h, "ncclAllGather");
     n.error_string = (decltype(n.error_string))dlsym(h, "ncclGetErrorString");
     n.ok = n.get_unique_id && n.comm_init_rank && n.comm_destroy && n.all_reduce && n.all_gather && n.error_string;
-    if (!n.ok) vxc_set_error("libnccl.so.2 lacks a symbol the tensor-parallel path needs");
+    return n;
+}
+
+// The library, opened once (thread-safe static initialisation); NULL with the
+// error set when it is missing or incomplete.
+const Nccl *nccl() {
+    static const Nccl n = load_nccl();
+    if (!n.ok) vxc_set_error("tensor parallelism needs libnccl.so.2 with the collectives it uses");
     return n.ok ? &n : NULL;
 }
 }  // namespace
