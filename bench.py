@@ -2,7 +2,7 @@
 """Benchmark of the Veltrix B200 speculative-decoding hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spec7b|spec2l|spec70b|q4matvec]
+                    [--workload spec7b|spec2l|spec70b|spec_tiny|q4matvec|accept]
 
 Prints ONE JSON line on rank 0.  For N > 1 launch it with
 torch.distributed.run (one rank per GPU, NCCL for the barrier and the
@@ -34,6 +34,16 @@ Workload `q4matvec` (benchmark configuration 2): Q4_0 verify matmuls 4096x4096 a
 accumulation.  One step = one GEMV over every rotated weight copy for each of
 the 8 (shape, M) cases; the copies of each shape exceed 2x the 126 MB L2, so
 every step streams its weights from HBM.
+
+Workload `spec_tiny` (benchmark configuration 1): the tiny Q8_0 target and
+draft of the parity tests, batch 1, k = 4, greedy, 32-id prompt, 128 new
+tokens (launch-bound: reported, not judged).  Its CPU baseline is the
+oracle's corrected speculative loop over the whole workload.
+
+Workload `accept` (benchmark configuration 3): the fused acceptance kernel
+for 64 sequences, k = 5, V = 32000, T = 0.8 (target logits N(0, 2^2), draft
+logits = target + N(0, 0.5^2)); 90.1 MB of logits per launch, rotated over
+copies larger than 2x L2.  Its CPU baseline is the oracle's acceptance.
 
 --impl reference times the reference's own CPU implementation (oracle/_ref,
 compiled from the reference sources with its shipped flags) on this host's
@@ -306,6 +316,11 @@ SPEC70_DRAFT = (2048, 16, 32, 8, 8192, 128256, 8, 22)
 SPEC70 = {"seqs_per_gpu": 32, "k": 6, "prompt": 4096, "new": 128, "temp": 0.8, "seed": 1}
 ROPE_THETA = {False: 10000.0, True: 500000.0}
 TP = False   # set by --workload spec70b
+# configuration 1: tiny Llama target / draft, Q8_0, batch 1, k=4, greedy, 32-id prompt, 128 new tokens
+SPEC_TINY_TARGET = (256, 4, 8, 8, 768, 4096, 8, 1)
+SPEC_TINY_DRAFT = (128, 2, 4, 4, 384, 4096, 8, 2)
+SPEC_TINY = {"seqs_per_gpu": 1, "k": 4, "prompt": 32, "new": 128, "temp": 0.0, "seed": 1}
+TINY = False   # set by --workload spec_tiny
 SPEC_TARGET_2L = (4096, 2, 32, 32, 11008, 32000, 2, 13)
 SPEC_DRAFT_2L = (2048, 2, 32, 4, 5632, 32000, 8, 14)
 
@@ -343,6 +358,8 @@ def spec_fixtures(write):
     paths = []
     if TP:
         names = ("target70b_q4_0", "draft1b70_q8_0")
+    elif TINY:
+        names = ("tiny_target_q8_0", "tiny_draft_q8_0")
     elif SPEC_TARGET[1] == 32:
         names = ("target7b_q4_0", "draft1b_q8_0")
     else:
@@ -616,6 +633,13 @@ def spec_config(ws):
                 "l2": "no flush: >= 20 GB of weights and KV per GPU per verify step, far above L2",
                 "parallelism": f"tp{ws}: heads, FFN columns and vocabulary split over {ws} GPU(s), "
                                "NCCL all-reduce after the output and down projections, all-gather of the logits"}
+    if TINY:
+        return {"workload": "spec_tiny: tiny Llama Q8_0 target (dim 256, 4 layers) + draft (dim 128, 2 layers), "
+                            f"k={SPEC['k']}, greedy, {SPEC['prompt']}-id prompt, {SPEC['new']} new tokens, batch 1",
+                "seqs_per_gpu": SPEC["seqs_per_gpu"], "global_seqs": SPEC["seqs_per_gpu"] * ws, "k": SPEC["k"],
+                "prompt": SPEC["prompt"], "new_tokens": SPEC["new"], "temp": SPEC["temp"],
+                "l2": "none needed: launch-bound (4.7 MB of weights, L2-resident); reported, not judged",
+                "parallelism": f"replicas x{ws}"}
     layers = "" if SPEC_TARGET[1] == 32 else f" ({SPEC_TARGET[1]}+{SPEC_DRAFT[1]} layers: profiling case)"
     return {"workload": "spec7b: Llama-2-7B-shape Q4_0 target + 1.1B-shape Q8_0 draft, k=4, greedy, "
                         f"512-id prompts, {SPEC['new']} new tokens" + layers,
@@ -631,9 +655,10 @@ def main_spec7b(args, ws, rank, threads):
                           "of weights per token; only the configuration 4 sample is timed"}))
         return
     if args.impl == "reference":
-        toks, kind, sample, det = cpu_spec7b_reference(threads)
+        toks, kind, sample, det = cpu_spec_tiny_port(threads) if TINY else cpu_spec7b_reference(threads)
         toks *= 1.0
-        print(json.dumps({"impl": "reference", "metric": SPEC_METRIC, "value": round(toks, 4), "unit": "tok/s",
+        print(json.dumps({"impl": "reference", "metric": SPEC_TINY_METRIC if TINY else SPEC_METRIC,
+                          "value": round(toks, 4), "unit": "tok/s",
                           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                           "higher_is_better": True, "scaling": "weak", "dtype": "f32", "data": "synthetic",
                           "config": spec_config(ws),
@@ -656,19 +681,20 @@ def main_spec7b(args, ws, rank, threads):
     round_ms = r["dec_ms"] / args.steps / rounds_per_step
     round_bytes = v_bytes + SPEC["k"] * (dw + r["d_kv"])
     cpu = None
-    if TP:
-        traffic, traffic_note = None, "not captured for the 70B workload"
+    if TP or TINY:
+        traffic, traffic_note = None, "not captured for this workload"
     else:
         traffic = int(SPEC_TARGET[1] * TRAFFIC_LAYER_NONATTN + TRAFFIC_ATTN_PER_KV_BYTE * r["v_kv"] + TRAFFIC_HEAD)
         traffic_note = "ncu DRAM bytes of the 2-layer case's verify, scaled per layer"
     if ws == 1 and not args.no_cpu and not TP:
         try:
-            toks, kind, sample, _ = cpu_spec7b_reference(threads)
+            toks, kind, sample, _ = cpu_spec_tiny_port(threads) if TINY else cpu_spec7b_reference(threads)
             cpu = {"value": round(toks, 4), "unit": "tok/s", "cores": threads, "kind": kind, "sample": sample}
         except Exception as ex:   # the reference build is absent: say so, never substitute
             cpu = {"value": None, "unit": "tok/s", "cores": threads, "kind": "reference",
                    "sample": f"not run: {ex}"}
-    out = {"metric": SPEC70_METRIC if TP else SPEC_METRIC, "value": round(value, 2), "unit": "tok/s",
+    out = {"metric": SPEC70_METRIC if TP else SPEC_TINY_METRIC if TINY else SPEC_METRIC,
+           "value": round(value, 2), "unit": "tok/s",
            "n_gpus": ws, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round((r["dec_ms"] + r["pre_ms"]) / args.steps, 3),
            "higher_is_better": True, "scaling": "strong" if TP else "weak", "vs_baseline": None, "dtype": "f32",
@@ -697,13 +723,238 @@ def main_spec7b(args, ws, rank, threads):
     print(json.dumps(out))
 
 
+SPEC_TINY_METRIC = "accepted tok/s (tiny spec decode, configuration 1)"
+
+
+def cpu_spec_tiny_port(threads):
+    """Configuration 1 on the host, timed in full: the oracle's corrected
+    speculative loop (oracle/vxo_spec.c: the reference's scalar forward with
+    standard rejection sampling; the reference's own loop corrupts its heap
+    and samples other distributions) on the same two GGUFs and prompt.
+    Returns (tok/s, kind, sample, detail)."""
+    import ctypes as C
+    from _paths import oracle
+    O = oracle()
+    tpath, dpath = spec_fixtures(write=True)
+    ot = O.vxo_model_load(tpath.encode(), 0)
+    od = O.vxo_model_load(dpath.encode(), 0)
+    prompt = spec_prompts(0, 1)[0]
+    n = SPEC["new"]
+    out = np.zeros(n, np.int32)
+    rounds = C.c_int()
+    t0 = time.perf_counter()
+    got = O.vxo_spec_generate(ot, od, prompt.ctypes.data, len(prompt), SPEC["k"], SPEC["temp"], SPEC["seed"], 0,
+                              out.ctypes.data, n, C.byref(rounds))
+    dt = time.perf_counter() - t0
+    O.vxo_model_free(ot)
+    O.vxo_model_free(od)
+    got = got if got > 0 else n
+    sample = (f"oracle speculative loop (scalar reference forward, OpenMP over rows, {threads} threads): "
+              f"the whole workload, {got} tokens in {dt:.2f} s, {rounds.value} rounds")
+    return got / dt, "port", sample, {"seconds": dt, "rounds": rounds.value}
+
+
+# ---------------------------------------------------------------------------
+# accept: configuration 3, the fused acceptance kernel
+# ---------------------------------------------------------------------------
+ACC = {"seqs": 64, "k": 5, "V": 32000, "temp": 0.8, "seed": 77}
+ACC_METRIC = "acceptance kernel HBM GB/s (configuration 3)"
+DRAFT_PURPOSE = 1
+
+
+def accept_inputs():
+    """Target logits [S][k+1][V] ~ N(0, 2^2) (the last row for the bonus
+    token), draft logits = target rows + N(0, 0.5^2), positions and ids."""
+    S, k, V = ACC["seqs"], ACC["k"], ACC["V"]
+    rng = np.random.default_rng(1)
+    P = (rng.standard_normal((S, k + 1, V)) * 2.0).astype(np.float32)
+    Q = (P[:, :k] + rng.standard_normal((S, k, V)) * 0.5).astype(np.float32)
+    pos0 = (100 + np.arange(S)).astype(np.int32)
+    ids = np.arange(S, dtype=np.int32)
+    return P, Q, pos0, ids
+
+
+def accept_bytes():
+    """Algorithmic bytes of one launch: every logit of P and Q read once."""
+    S, k, V = ACC["seqs"], ACC["k"], ACC["V"]
+    return S * (2 * k + 1) * V * 4
+
+
+def run_accept_gpu(args, ws, rank, local):
+    import torch
+    import vxb200
+    torch.cuda.set_device(local)
+    L = vxb200.lib()
+    vxb200.check(L.vxc_device_init(local), "vxc_device_init")
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    S, k, V, T, seed = ACC["seqs"], ACC["k"], ACC["V"], ACC["temp"], ACC["seed"]
+    P, Q, pos0, ids = accept_inputs()
+    nb = accept_bytes()
+    ncopy = max(2, (2 * L2_BYTES + nb - 1) // nb)       # rotated copies: more than 2x L2 in total
+    Pd = [torch.from_numpy(P).cuda() for _ in range(ncopy)]
+    Qd = [torch.from_numpy(Q).cuda() for _ in range(ncopy)]
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    # draft tokens drawn from q by the library's own sampler (Philox purpose DRAFT), as the engine does
+    rpos = torch.from_numpy((pos0[:, None] + np.arange(k)[None, :]).astype(np.int32).ravel()).cuda()
+    rseq = torch.from_numpy(np.repeat(ids, k).astype(np.int32)).cuda()
+    d = torch.zeros(S * k, dtype=torch.int32, device="cuda")
+    vxb200.check(L.vxc_sample_rows(Qd[0].data_ptr(), S * k, V, T, seed, rpos.data_ptr(), rseq.data_ptr(),
+                                   DRAFT_PURPOSE, d.data_ptr(), ctypes.c_void_p(sp)), "vxc_sample_rows")
+    posd, idd = torch.from_numpy(pos0).cuda(), torch.from_numpy(ids).cuda()
+    na = torch.zeros(S, dtype=torch.int32, device="cuda")
+    nx = torch.zeros(S, dtype=torch.int32, device="cuda")
+    wsb = L.vxc_accept_workspace_bytes(S, k)
+    wsp = torch.zeros(wsb // 4 + 1, dtype=torch.int32, device="cuda")
+
+    def launch(i):
+        vxb200.check(L.vxc_accept(Pd[i].data_ptr(), (k + 1) * V, V, Qd[i].data_ptr(), k * V, V, d.data_ptr(), S, k,
+                                  V, T, seed, idd.data_ptr(), posd.data_ptr(), na.data_ptr(), nx.data_ptr(),
+                                  wsp.data_ptr(), wsb, ctypes.c_void_p(sp)), "vxc_accept")
+
+    for _ in range(max(args.warmup, 3)):
+        for i in range(ncopy):
+            launch(i)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps * ncopy)]
+    clk = ClockSampler(local)
+    clk.start()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = L.vxc_launch_count()
+    t0.record(stream)
+    for j in range(args.steps * ncopy):
+        evs[j][0].record(stream)
+        launch(j % ncopy)
+        evs[j][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    launches = L.vxc_launch_count() - l0
+    clocks = clk.stop()
+    ms_total = t0.elapsed_time(t1)
+    kern = [a.elapsed_time(b) for a, b in evs]
+    # e2e: logits from pinned host memory each step, accepted lengths and tokens back
+    hP, hQ = torch.from_numpy(P).pin_memory(), torch.from_numpy(Q).pin_memory()
+    hna, hnx = torch.zeros(S, dtype=torch.int32).pin_memory(), torch.zeros(S, dtype=torch.int32).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        Pd[0].copy_(hP, non_blocking=True)
+        Qd[0].copy_(hQ, non_blocking=True)
+        launch(0)
+        hna.copy_(na, non_blocking=True)
+        hnx.copy_(nx, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    code = ctypes.c_uint(0)
+    vxb200.check(L.vxc_check_device_error(ctypes.byref(code)), "device error check")
+    t = torch.tensor([ms_total, e2e_ms, max(kern)], device="cuda", dtype=torch.float64)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total, e2e_ms, _ = t.tolist()
+    res = dict(ms_total=ms_total, e2e_ms=e2e_ms, kern_ms=sum(kern) / len(kern), n=len(kern), ncopy=ncopy,
+               clocks=clocks, launches=launches, d=d.cpu().numpy(), na=na.cpu().numpy(),
+               h2d=P.nbytes + Q.nbytes, d2h=2 * S * 4)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
+def cpu_accept_port(threads, d=None, budget_s=10.0):
+    """The acceptance of all 64 sequences on the host: the oracle's restatement
+    (oracle/vxo_spec.c vxo_accept: standard rejection sampling with Philox
+    uniforms; the reference's verify_draft, src/speculative.c:178-236, is a
+    static part of its broken loop and samples other distributions), one
+    thread, repeated for about budget_s.  d = the draft tokens (drawn with
+    the oracle's sampler when not given).  Returns (GB/s, kind, sample)."""
+    import ctypes as C
+    from _paths import oracle
+    O = oracle()
+    S, k, V, T, seed = ACC["seqs"], ACC["k"], ACC["V"], ACC["temp"], ACC["seed"]
+    P, Q, pos0, ids = accept_inputs()
+    if d is None:
+        d = np.zeros(S * k, np.int32)
+        for s in range(S):
+            for i in range(k):
+                d[s * k + i] = O.vxo_sample(Q[s, i].ctypes.data, V, T,
+                                            O.vxo_philox_u32(seed, int(pos0[s]) + i, int(ids[s]), DRAFT_PURPOSE))
+    d = np.ascontiguousarray(d, np.int32).reshape(S, k)
+    nxt = C.c_int()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or n == 0:
+        for s in range(S):
+            O.vxo_accept(P[s].ctypes.data, Q[s].ctypes.data, d[s].ctypes.data, k, V, T, seed, int(ids[s]),
+                         int(pos0[s]), C.byref(nxt))
+        n += 1
+    dt = time.perf_counter() - t0
+    return accept_bytes() * n / dt / 1e9, "port", f"oracle acceptance, 1 thread, all {S} sequences x {n} repetitions"
+
+
+def main_accept(args, ws, rank, threads):
+    config = {"workload": f"accept: fused acceptance of {ACC['seqs']} sequences, k={ACC['k']}, V={ACC['V']}, "
+                          f"T={ACC['temp']}; target logits N(0,2^2), draft = target + N(0,0.5^2)",
+              "l2": "inputs rotated over copies > 2x L2 (no flush needed)", "parallelism": f"replicas x{ws}"}
+    if args.impl == "reference":
+        gbs, kind, sample = cpu_accept_port(threads, budget_s=max(1, args.steps) * 2.0)
+        print(json.dumps({"impl": "reference", "metric": ACC_METRIC, "value": round(gbs, 4), "unit": "GB/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "dtype": "f32", "data": "synthetic", "config": config,
+                          "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind,
+                                           "sample": sample},
+                          "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
+    r = run_accept_gpu(args, ws, rank, int(os.environ.get("LOCAL_RANK", "0")))
+    if rank != 0:
+        return
+    nb = accept_bytes()
+    value = ws * nb * r["n"] / (r["ms_total"] * 1e-3) / 1e9
+    e2e = ws * nb * args.steps / (r["e2e_ms"] * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    achieved = nb / (r["kern_ms"] * 1e-3) / 1e9
+    cpu = None
+    if ws == 1 and not args.no_cpu:
+        gbs, kind, sample = cpu_accept_port(threads, d=r["d"])
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": kind, "sample": sample}
+    out = {"metric": ACC_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(r["ms_total"] / args.steps, 4), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+           "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(achieved / peak, 4), "traffic": None,
+                        "traffic_note": "not captured for this workload",
+                        "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                        "kernel": "vxc_accept, per-launch CUDA events", "algorithmic_bytes": nb,
+                        "kernel_us": round(r["kern_ms"] * 1e3, 2)},
+           "accepted_mean": round(float(np.mean(r["na"])), 3),
+           "cpu_baseline": cpu,
+           "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": r["h2d"],
+                   "d2h_bytes_per_step": r["d2h"]},
+           "gpu_launches": r["launches"], "clocks": r["clocks"]}
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="spec7b", choices=["spec7b", "spec2l", "spec70b", "q4matvec"],
+    ap.add_argument("--workload", default="spec7b",
+                    choices=["spec7b", "spec2l", "spec70b", "spec_tiny", "q4matvec", "accept"],
                     help="spec2l: spec7b with 2-layer models, the small case for profilers; "
                          "spec70b: configuration 5, the 70B-shape target tensor-parallel over --gpus")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
@@ -713,7 +964,11 @@ def main():
                     help="spec70b: target layers (fewer than 80 = a small functional/profiling case)")
     ap.add_argument("--prompt", type=int, default=None, help="spec70b: prompt ids per sequence")
     args = ap.parse_args()
-    global SPEC_TARGET, SPEC_DRAFT, TP
+    global SPEC_TARGET, SPEC_DRAFT, TP, TINY
+    if args.workload == "spec_tiny":
+        TINY = True
+        SPEC_TARGET, SPEC_DRAFT = SPEC_TINY_TARGET, SPEC_TINY_DRAFT
+        SPEC.update(SPEC_TINY)
     if args.workload == "spec70b":
         TP = True
         SPEC_TARGET, SPEC_DRAFT = SPEC70_TARGET, SPEC70_DRAFT
@@ -730,8 +985,10 @@ def main():
         return   # the CPU reference runs on rank 0 only
     if args.workload == "spec2l":
         SPEC_TARGET, SPEC_DRAFT = SPEC_TARGET_2L, SPEC_DRAFT_2L
-    if args.workload in ("spec7b", "spec2l", "spec70b"):
+    if args.workload in ("spec7b", "spec2l", "spec70b", "spec_tiny"):
         main_spec7b(args, ws, rank, threads)
+    elif args.workload == "accept":
+        main_accept(args, ws, rank, threads)
     else:
         main_q4matvec(args, ws, rank, threads)
 
