@@ -37,3 +37,17 @@ def test_spec70b_reference_arm_is_unavailable():
     assert r.returncode == 0, r.stderr[-2000:]
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and "unavailable" in line
+
+
+def _reference_line(workload):
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload",
+                        workload, "--steps", "1"], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
+def test_accept_and_tiny_reference_arms_print_their_lines():
+    for workload, unit in (("accept", "GB/s"), ("spec_tiny", "tok/s")):
+        line = _reference_line(workload)
+        assert line["impl"] == "reference" and line["unit"] == unit and line["value"] > 0
+        assert line["cpu_baseline"]["kind"] == "port" and line["e2e"]["value"] == line["value"]
