@@ -79,6 +79,10 @@
 #ifndef GM_RING_BLOCKS
 #define GM_RING_BLOCKS 24   // Q4_0 blocks in flight per CTA (Q8_0: two thirds)
 #endif
+#ifndef GM_LO_HALF_N
+#define GM_LO_HALF_N 0      // 1: the w_lo MMA over the x_hi rows only (drops w_lo*x_lo, <= 2^-22 of a
+                            // product): 3N instead of 4N accumulator columns of tensor work per K step
+#endif
 template <int QT, int NT>
 struct GmCfg {
     static constexpr int QB = QT == 2 ? 16 : 32;
@@ -261,6 +265,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
         const uint32_t tlane = tmem_base + ((uint32_t)(quarter * 32) << 16);
         const bool issuer = kw < IG && lane == 0;
         const uint32_t idesc = (1u << 4) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+        // the w_lo MMA: all 2N rows of B, or (GM_LO_HALF_N) the first N, the x_hi parts
+        const uint32_t idesc_lo =
+            GM_LO_HALF_N ? (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24) : idesc;
         const uint32_t bbase = smem_u32(Bs);
         const uint32_t dcol = tmem_base + 2 * ACOL + (group * IG + kw) * NP;
         const int per_item = (nst - group + 1) / 2;   // this group's stages per item
@@ -343,7 +350,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
                                 const uint64_t bd =
                                     sdesc(bbase + (uint32_t)((bl * 4 + 2 * kk) * NP * 16), NP * 16, 128);
                                 mma_f16_ts(dcol, ahi, bd, idesc, 1u);
-                                mma_f16_ts(dcol, ahi + 16, bd, idesc, 1u);
+                                mma_f16_ts(dcol, ahi + 16, bd, idesc_lo, 1u);
                             }
                         }
                     }
