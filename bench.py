@@ -466,6 +466,12 @@ def run_spec7b_gpu(args, ws, rank, local):
         first, S = shard(rank, ws, SPEC["seqs_per_gpu"])
     progress("models loaded")
     k = SPEC["k"]
+    # generation stops at the target's n_ctx (the reference's rule); configuration 5's
+    # 4096-id prompts need a context above the loader's default of 4096
+    need = SPEC["prompt"] + SPEC["new"] + k + 8
+    for m in (target, draft):
+        if m.head.config.n_ctx < need:
+            m.head.config.n_ctx = need
     sp = vxb200.Speculative(draft, target, k, temp=SPEC["temp"], seed=SPEC["seed"], seq_id_base=first)
     prompts = spec_prompts(first, S)
     new = SPEC["new"]

@@ -4,7 +4,7 @@
  *
  * Arithmetic order follows the reference's non-AVX2 build exactly so that the
  * result is bit-identical to the reference compiled with -O2 -march=x86-64
- * (tests/test_oracle_vs_ref.py).  The one semantic change is the reference's
+ * (tests/test_oracle_pin.py).  The one semantic change is the reference's
  * in-place attn_o GEMV (src/model.c:543-544), which races under OpenMP; here
  * it is out of place, which is what the reference computes at one thread
  * with a private copy of its input.

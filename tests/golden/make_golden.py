@@ -5,7 +5,8 @@ oracle/Makefile into oracle/_ref/libvxref.so: scalar build, out-of-place
 attn_o) on the tiny configuration-1 checkpoints that the library's
 deterministic GGUF writer produces, and stores:
   - logits of every position of a 24-token prompt (fp32),
-  - the target-only greedy continuation of a 32-token prompt (64 tokens) and
+  - the target-only greedy continuation of a 32-token prompt (128 tokens, the
+    configuration-1 workload) and
     the top-2 logit margin at each step.
 Run from the repository root:  python tests/golden/make_golden.py
 """
@@ -51,7 +52,7 @@ def main():
     rng = np.random.default_rng(12345)
     prompt = rng.integers(0, 4096, 32).astype(np.int32)
     for name in ("tiny_target", "tiny_draft"):
-        logits, gen, marg = ref_run(name, prompt, 64)
+        logits, gen, marg = ref_run(name, prompt, 128)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), prompt=prompt, logits=logits[:8], greedy=gen,
                             margins=marg)
         print(name, "greedy head", gen[:8], "min margin", marg.min())

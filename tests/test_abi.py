@@ -91,3 +91,29 @@ def test_additive_entry_points_check_arguments():
     # the writer rejects K-quant widths that are not whole super-blocks
     bad = vxb200.SynthConfig(128, 1, 4, 4, 384, 256, 10000.0, 12)
     assert L.vx_synth_write_gguf(b"/tmp/never_written.gguf", ctypes.byref(bad), 1) == VX_ERR_PARAM
+
+
+REF_INCLUDE = "/root/reference/include"
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_INCLUDE), reason="reference headers not present on this machine")
+def test_vx_model_layout_matches_reference_header(tmp_path):
+    """The same C program compiled against the reference's include/veltrix.h
+    and against this repository's prints identical offsets for every field a
+    caller of the reference API can read or poke, and identical error codes."""
+    src = tmp_path / "lay.c"
+    fields = ["config", "config.n_layers", "config.n_vocab", "config.n_ctx", "config.rope_theta",
+              "config.has_ffn_bias", "tensors", "n_tensors", "tok_embd", "attn_q", "output_w",
+              "k_cache", "v_cache", "cache_len"]
+    body = "".join(f'printf("%zu\\n", offsetof(vx_model, {f}));' for f in fields)
+    codes = "".join(f'printf("%d\\n", (int){c});' for c in
+                    ("VX_OK", "VX_ERR_FILE", "VX_ERR_FORMAT", "VX_ERR_MEMORY", "VX_ERR_PARAM", "VX_ERR_GGUF",
+                     "VX_ERR_NOMODEL", "VX_ERR_UNSUPPORTED"))
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "model.h"\n#include "speculative.h"\n'
+                   'int main(){' + body + codes + 'printf("%zu\\n", sizeof(vx_model_config));return 0;}\n')
+    outs = []
+    for inc in (REF_INCLUDE, os.path.join(ROOT, "include")):
+        exe = tmp_path / ("lay_" + str(len(outs)))
+        subprocess.run(["gcc", "-I", inc, str(src), "-o", str(exe)], check=True)
+        outs.append(subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split())
+    assert outs[0] == outs[1]

@@ -2,11 +2,9 @@
 tiny_kqmix fixtures) against the oracle within 2e-3 x max|logit|, over a
 prompt of two chunks, then two decode steps.
 
-Not collected under this name: the K-quant forward path (embedding decode,
-k_gemv_kq_img, stacked matrices) has not run on a GPU yet, and a failure
-there must not take the process that runs the other GPU tests with it.
-Rename to test_kquant_model_gpu.py once it has passed on its own:
-    python -m pytest tests/pending_kquant_model_gpu.py -m gpu
+Covers the K-quant forward path: K-quant embedding rows, k_gemv_kq_img on
+the forward's activation image, and row-stacked matrices of mixed K-quant
+types (reference dispatch src/model.c:222-233).
 """
 import ctypes
 import numpy as np

@@ -38,16 +38,18 @@ def test_greedy_equals_reference_greedy(models):
     import vxb200
     t, d = models
     g = np.load(os.path.join(GOLD, "tiny_target.npz"))
+    n = len(g["greedy"])                  # the whole configuration-1 workload: 128 new tokens
+    assert n == 128
     sp = vxb200.Speculative(d, t, 4, temp=0.0)
-    out = sp.generate(g["prompt"], 64)
-    assert len(out) == 64
+    out = sp.generate(g["prompt"], n)
+    assert len(out) == n
     ref = g["greedy"]
-    for i in range(64):
+    for i in range(n):
         if out[i] != ref[i]:
             assert g["margins"][i] <= 1e-3, (i, out[i], ref[i])
             break
     st = sp.stats()
-    assert st.emitted == 64 and st.rounds >= 1 and st.accepted <= st.drafted
+    assert st.emitted == n and st.rounds >= 1 and st.accepted <= st.drafted
     sp.close()
 
 
@@ -132,3 +134,31 @@ def test_eager_rounds_equal_graph_rounds(models):
         assert r.returncode == 0, r.stderr[-2000:]
         outs.append(r.stdout.strip().splitlines()[-1])
     assert outs[0] == outs[1] and len(outs[0].split()) == 48
+
+
+def test_generation_stops_at_n_ctx(models):
+    """The reference loop stops when prompt + generated tokens reach the
+    target's n_ctx (src/speculative.c:254, :293): a sequence emits at most
+    n_ctx - prompt_len tokens, the same ones an unbounded run starts with, and
+    nothing when its prompt already fills the context."""
+    import vxb200
+    t, d = models
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, 4096, n).astype(np.int32) for n in (40, 20, 64)]
+    sp = vxb200.Speculative(d, t, 4, temp=0.8, seed=5)
+    free_run = sp.generate_batch(prompts, 30)
+    assert [len(o) for o in free_run] == [30, 30, 30]
+    saved = t.head.config.n_ctx
+    try:
+        t.head.config.n_ctx = 48
+        capped = sp.generate_batch(prompts, 30)
+        assert [len(o) for o in capped] == [8, 28, 0]
+        for a, b in zip(capped, free_run):
+            assert np.array_equal(a, b[:len(a)])
+        one = vxb200.Speculative(d, t, 4, temp=0.8, seed=5, seq_id_base=1)
+        one_out = one.generate(prompts[1], 100)
+        assert len(one_out) == 28 and np.array_equal(one_out, free_run[1][:28])
+        one.close()
+    finally:
+        t.head.config.n_ctx = saved
+    sp.close()

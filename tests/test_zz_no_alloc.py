@@ -4,8 +4,10 @@ that cannot afford cudaMalloc's device synchronisation).  Its scratch is a
 static device array inside the library.
 
 Checked through the C-ABI: two calls in a row give the same result as
-vxc_qgemv with a caller-provided workspace (tolerance 2e-5 x max|y|, as in
-test_gemv_gpu.py), no device memory is taken between the two calls, and a
+vxc_qgemv with a caller-provided workspace, and both agree with the CPU
+oracle's GEMV (oracle/vxo_fwd.c vxo_qgemv, the reference's scalar
+src/quantize.c:728-750 arithmetic) within 2e-5 x max|y| as in
+test_gemv_gpu.py; no device memory is taken between the two calls, and a
 shape whose scratch exceeds the static limit is rejected with an error.
 This file is named so that pytest collects it last.
 """
@@ -14,6 +16,7 @@ import ctypes
 import numpy as np
 import pytest
 
+from _paths import oracle
 from qgen import q4_0_blocks, q8_0_blocks
 
 pytestmark = pytest.mark.gpu
@@ -39,6 +42,11 @@ def test_noalloc_matches_qgemv_twice(cuda, qt, rows, cols, M):
     torch.cuda.synchronize()
     ref = y_ref.cpu().numpy()
     mx = float(np.max(np.abs(ref)))
+    # the existing entry point against the oracle
+    xh = x.cpu().numpy()
+    yo = np.zeros((M, rows), np.float32)
+    oracle().vxo_qgemv(qt, blk.ctypes.data, xh.ctypes.data, yo.ctypes.data, M, rows, cols)
+    assert float(np.max(np.abs(ref - yo))) <= TOL * float(np.max(np.abs(yo)))
     free_after = []
     for _ in range(2):
         y = torch.full((M, rows), float("nan"), device="cuda")
@@ -50,8 +58,10 @@ def test_noalloc_matches_qgemv_twice(cuda, qt, rows, cols, M):
         code = ctypes.c_uint(0)
         assert L.vxc_check_device_error(ctypes.byref(code)) == 0, code.value
         free_after.append(torch.cuda.mem_get_info()[0])
-        err = float(np.max(np.abs(y.cpu().numpy() - ref)))
+        got = y.cpu().numpy()
+        err = float(np.max(np.abs(got - ref)))
         assert err <= TOL * mx, (err, mx)
+        assert float(np.max(np.abs(got - yo))) <= TOL * float(np.max(np.abs(yo)))
     # the second call allocates nothing on the device
     assert free_after[1] == free_after[0]
     W.close()

@@ -21,9 +21,10 @@
 // its tiles.  Each item writes fp32 partial sums part[slice][m][row]; the
 // consumer of the GEMV output adds the ks slices in slice order.
 //
-// MMA shape.  A tcgen05.mma of N <= 64 costs ~50 cycles of its issuing
-// thread whatever N is, so one issuer cannot keep up with HBM at these
-// sizes; several threads issuing into separate accumulators can.  The image
+// MMA shape.  One thread issues one tcgen05.mma per ~200 SM cycles whatever
+// N is (16..256, A from TMEM or shared memory; measured on B200), while MMAs
+// of different threads overlap, so one issuer cannot keep up with HBM at
+// these sizes; several threads issuing into separate accumulators can.  The image
 // stacks [x_hi; x_lo] as 2N rows of B, so per K step two MMAs (A = w_hi, then
 // A = w_lo) give all four hi/lo products in one 2N-column accumulator; the
 // epilogue adds column m and N + m.
@@ -55,6 +56,7 @@
 #include "vxc_qmat.cuh"
 #include "vxc_internal.h"
 
+#include <atomic>
 #include <stdio.h>
 
 #define GM_THREADS 448
@@ -507,12 +509,16 @@ bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p) {
 
 template <int QT, int NT>
 static cudaError_t launch_mma(const GmArgs &ga, const VxcGemvPlan &p, cudaStream_t st) {
-    static bool attr_set = false;   // one flag per template instance
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(k_qgemv_mma<QT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             GM_SMEM_DYN);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
+    // the attribute is per device: a process that drives several GPUs sets it on each
+    static std::atomic<uint64_t> attr_set{0};   // bit d: set on device d
+    int dev = 0;
+    cudaError_t ea = cudaGetDevice(&dev);
+    if (ea != cudaSuccess) return ea;
+    const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t)1 << dev : 0;
+    if (!bit || !(attr_set.load(std::memory_order_acquire) & bit)) {
+        ea = cudaFuncSetAttribute(k_qgemv_mma<QT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM_DYN);
+        if (ea != cudaSuccess) return ea;
+        if (bit) attr_set.fetch_or(bit, std::memory_order_acq_rel);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
@@ -648,10 +654,18 @@ extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, voi
 // start at zero: every byte a call reads was written earlier by the same
 // call.  All calls on a device share the array, so calls whose GPU work
 // overlaps (different streams without ordering between them) race on it.
+// The array's device address is looked up on the first call on each device
+// (with that device current) and cached with the context it belongs to; a
+// device reset that recreates the primary context makes the next call look
+// it up again.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) uint8_t g_qgemv_scratch[VXC_QGEMV_NOALLOC_BYTES];
 
-static void *g_qgemv_scratch_ptr[64];   // device address of g_qgemv_scratch, per device
+struct NoallocSlot {
+    std::atomic<void *> ptr{nullptr};   // device address of g_qgemv_scratch
+    std::atomic<void *> ctx{nullptr};   // the context it belongs to
+};
+static NoallocSlot g_qgemv_scratch_slot[64];
 
 extern "C" int vxc_qgemv_noalloc(const vxc_qmat *w, const float *x, int M, float *y, void *stream) {
     if (!w || !x || !y || M <= 0) {
@@ -670,16 +684,22 @@ extern "C" int vxc_qgemv_noalloc(const vxc_qmat *w, const float *x, int M, float
                       w->rows, w->cols, M, need, (size_t)VXC_QGEMV_NOALLOC_BYTES);
         return -4;
     }
-    if (!g_qgemv_scratch_ptr[dev]) {
-        // set-up, once per device, with that device current: the host-side
-        // name of the array is not a device address
-        void *p = NULL;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_qgemv_scratch);
+    NoallocSlot &slot = g_qgemv_scratch_slot[dev];
+    void *ctx = vxc_current_context();
+    void *p = slot.ptr.load(std::memory_order_acquire);
+    if (!p || slot.ctx.load(std::memory_order_acquire) != ctx) {
+        // set-up, once per device (and context), with that device current: the
+        // host-side name of the array is not a device address.  Two threads that
+        // get here together store the same address.
+        p = NULL;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_qgemv_scratch);
         if (e != cudaSuccess || !p) {
+            cudaGetLastError();   // do not leave the error for a later call to report
             vxc_set_error("vxc_qgemv_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
             return -3;
         }
-        g_qgemv_scratch_ptr[dev] = p;
+        slot.ctx.store(ctx, std::memory_order_release);
+        slot.ptr.store(p, std::memory_order_release);
     }
-    return vxc_qgemv(w, x, M, y, g_qgemv_scratch_ptr[dev], VXC_QGEMV_NOALLOC_BYTES, stream);
+    return vxc_qgemv(w, x, M, y, p, VXC_QGEMV_NOALLOC_BYTES, stream);
 }

@@ -55,6 +55,8 @@ bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p);
 int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, float *part,
                  const VxcGemvPlan &p, cudaStream_t st, const float *x = NULL);
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
+// The calling thread's current CUDA context (driver handle), or NULL.
+void *vxc_current_context(void);
 // Library-wide count of kernel launches (a CUDA-graph replay adds its kernels).
 void vxc_count_launches(long long n);
 

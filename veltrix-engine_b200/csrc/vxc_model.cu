@@ -1254,9 +1254,16 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_swiglu_image, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_combine_image, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     }
-    for (int qc = 8; qc <= 16 && e == cudaSuccess; qc += 8)
-        e = cudaFuncSetAttribute(attn_kernel(hd, qc), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)attn_smem(hd, SL, qc));
+    // The attribute is per kernel (and device), shared by every sequence set of
+    // the process, so it is only ever raised: a set with a shorter context
+    // must not shrink it under one with a longer context.
+    for (int qc = 8; qc <= 16 && e == cudaSuccess; qc += 8) {
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, attn_kernel(hd, qc));
+        if (e == cudaSuccess && fa.maxDynamicSharedSizeBytes < (int)attn_smem(hd, SL, qc))
+            e = cudaFuncSetAttribute(attn_kernel(hd, qc), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)attn_smem(hd, SL, qc));
+    }
     if (e != cudaSuccess) {
         vxc_set_error("vxc_seqs_create: %s", cudaGetErrorString(e));
         vxc_seqs_destroy(s);

@@ -31,6 +31,24 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps until the phase completes or the hint (ns) elapses, instead of
+// spinning and taking issue slots from the warps that do the work.
+#ifndef VXC_SUSPEND_NS
+#define VXC_SUSPEND_NS 0x100000u
+#endif
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "n"(VXC_SUSPEND_NS)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on phase `parity`.  Returns false when the CTA is aborting:
 // this wait ran past VXC_WAIT_NS (the error word gets `code`), or another
 // role of the CTA already gave up (*abort_flag set).
@@ -38,8 +56,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           unsigned int code) {
     uint64_t t0 = 0;
     for (uint32_t it = 0;; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if ((it & 63u) == 63u) {
+        if (mbar_try_sleep(bar, parity)) return true;
+        if ((it & 3u) == 3u) {
             if (*abort_flag) return false;
             const uint64_t now = vxc_globaltimer();
             if (t0 == 0) {
@@ -151,3 +169,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// After tcgen05.wait::ld: makes each loaded register a value defined after
+// the wait, so the compiler cannot move a use of it above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_pin(uint32_t *r) {
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
+}
+
+// One 32-bit column per lane.
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+    uint32_t r;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+    return r;
+}

@@ -92,3 +92,25 @@ extern "C" int vxc_device_current(void) {
     if (vxc_device_count() <= 0 || cudaGetDevice(&d) != cudaSuccess) { cudaGetLastError(); return -1; }
     return d;
 }
+
+// The driver's current-context handle, reached through the runtime's entry
+// point table (the library links only the static runtime, not libcuda).
+typedef int (*cu_ctx_get_current_t)(void **);
+
+void *vxc_current_context(void) {
+    static std::atomic<cu_ctx_get_current_t> fn{nullptr};
+    cu_ctx_get_current_t f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        void *p = NULL;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !p) {
+            cudaGetLastError();
+            return NULL;
+        }
+        f = (cu_ctx_get_current_t)p;
+        fn.store(f, std::memory_order_release);
+    }
+    void *ctx = NULL;
+    return f(&ctx) == 0 ? ctx : NULL;
+}

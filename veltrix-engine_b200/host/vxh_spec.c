@@ -89,38 +89,63 @@ static int ensure_engine(vx_speculative_state *s, int n_seq, int ctx) {
 int vx_speculative_generate_batch(vx_speculative_state *s, const int *const *prompts, const int *prompt_lens,
                                   int n_seq, int **outputs, int max_tokens, int *counts) {
     if (!s || !prompts || !prompt_lens || !outputs || n_seq < 1 || max_tokens < 1) return 0;
-    int maxp = 0;
-    size_t total = 0;
     for (int i = 0; i < n_seq; i++) {
         if (!prompts[i] || prompt_lens[i] < 1 || !outputs[i]) return 0;
+        if (counts) counts[i] = 0;
+    }
+    /* The reference loop stops once prompt + generated tokens reach the
+     * target's n_ctx (src/speculative.c:254, :258-262, :293), so a sequence
+     * emits at most n_ctx - prompt_len tokens, and none when its prompt already
+     * fills the context.  Sequences with room run together; each keeps its own
+     * Philox sequence id (seq_id_base + its index in the call). */
+    const int n_ctx = s->target->config.n_ctx;
+    int *sel = (int *)malloc((size_t)n_seq * sizeof(int));
+    if (!sel) return 0;
+    int nsel = 0, maxp = 0, eff = 0;
+    size_t total = 0;
+    for (int i = 0; i < n_seq; i++) {
+        const int cap = n_ctx > 0 ? n_ctx - prompt_lens[i] : max_tokens;
+        if (cap <= 0) continue;
+        sel[nsel++] = i;
         if (prompt_lens[i] > maxp) maxp = prompt_lens[i];
+        const int want = cap < max_tokens ? cap : max_tokens;
+        if (want > eff) eff = want;
         total += (size_t)prompt_lens[i];
     }
-    if (ensure_engine(s, n_seq, maxp + max_tokens + s->k + 2)) return 0;
+    if (nsel == 0 || ensure_engine(s, nsel, maxp + eff + s->k + 2)) {
+        free(sel);
+        return 0;
+    }
     int *cat = (int *)malloc(total * sizeof(int));
-    int *ids = (int *)malloc((size_t)n_seq * sizeof(int));
-    int *out = (int *)malloc((size_t)n_seq * max_tokens * sizeof(int));
-    int *cnt = (int *)calloc((size_t)n_seq, sizeof(int));
-    if (!cat || !ids || !out || !cnt) {
-        free(cat); free(ids); free(out); free(cnt);
+    int *lens = (int *)malloc((size_t)nsel * sizeof(int));
+    int *ids = (int *)malloc((size_t)nsel * sizeof(int));
+    int *out = (int *)malloc((size_t)nsel * eff * sizeof(int));
+    int *cnt = (int *)calloc((size_t)nsel, sizeof(int));
+    if (!cat || !lens || !ids || !out || !cnt) {
+        free(sel); free(cat); free(lens); free(ids); free(out); free(cnt);
         return 0;
     }
     size_t off = 0;
-    for (int i = 0; i < n_seq; i++) {
+    for (int j = 0; j < nsel; j++) {
+        const int i = sel[j];
         memcpy(cat + off, prompts[i], (size_t)prompt_lens[i] * sizeof(int));
         off += (size_t)prompt_lens[i];
-        ids[i] = s->seq_base + i;
+        lens[j] = prompt_lens[i];
+        ids[j] = s->seq_base + i;
     }
     vxc_spec_stats st;
     memset(&st, 0, sizeof st);
-    int rc = vxc_spec_generate(s->eng, cat, prompt_lens, ids, n_seq, max_tokens, s->temperature, s->seed, out, cnt,
-                               &st);
+    int rc = vxc_spec_generate(s->eng, cat, lens, ids, nsel, eff, s->temperature, s->seed, out, cnt, &st);
     int total_gen = 0;
     if (rc == 0) {
-        for (int i = 0; i < n_seq; i++) {
-            memcpy(outputs[i], out + (size_t)i * max_tokens, (size_t)cnt[i] * sizeof(int));
-            if (counts) counts[i] = cnt[i];
-            total_gen += cnt[i];
+        for (int j = 0; j < nsel; j++) {
+            const int i = sel[j];
+            int c = cnt[j];
+            if (n_ctx > 0 && c > n_ctx - prompt_lens[i]) c = n_ctx - prompt_lens[i];
+            if (c > max_tokens) c = max_tokens;
+            memcpy(outputs[i], out + (size_t)j * eff, (size_t)c * sizeof(int));
+            if (counts) counts[i] = c;
+            total_gen += c;
         }
         s->last.rounds = st.rounds;
         s->last.drafted = st.drafted;
@@ -131,7 +156,7 @@ int vx_speculative_generate_batch(vx_speculative_state *s, const int *const *pro
     } else {
         fprintf(stderr, "veltrix-b200: %s\n", vxc_error_string());
     }
-    free(cat); free(ids); free(out); free(cnt);
+    free(sel); free(cat); free(lens); free(ids); free(out); free(cnt);
     return total_gen;
 }
 
