@@ -30,7 +30,7 @@ typedef unsigned __int128 u128;
 #define SMP_THREADS 1024
 
 // ---------------------------------------------------------------------------
-// block-wide helpers (blockDim.x == SMP_THREADS)
+// block-wide helpers (blockDim.x a multiple of 32, at most 1024)
 // ---------------------------------------------------------------------------
 struct MaxIdx {
     float v;
@@ -43,9 +43,44 @@ __device__ __forceinline__ MaxIdx better(MaxIdx a, MaxIdx b) {
     return a;
 }
 
+// f(v, x) for every element v of a row, x = row[v].  Rows of 16-byte aligned
+// start and V % 4 == 0 are read as float4 with RP_UNROLL loads in flight per
+// thread (one memory latency per RP_UNROLL * 4 * blockDim.x elements, not one
+// per element); other rows element by element.  Visiting order differs per
+// thread, so f must be order-independent (integer sums, first-max argmax).
+#define RP_UNROLL 8
+template <class F>
+__device__ __forceinline__ void row_pass(const float *__restrict__ row, int V, F f) {
+    const int nt = blockDim.x;
+    if ((((uintptr_t)row) & 15) == 0 && (V & 3) == 0) {
+        const int V4 = V >> 2;
+        const float4 *r4 = reinterpret_cast<const float4 *>(row);
+        for (int base = 0; base < V4; base += nt * RP_UNROLL) {
+            float4 x[RP_UNROLL];
+#pragma unroll
+            for (int u = 0; u < RP_UNROLL; u++) {
+                const int j = base + u * nt + (int)threadIdx.x;
+                x[u] = j < V4 ? __ldg(r4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < RP_UNROLL; u++) {
+                const int j = base + u * nt + (int)threadIdx.x;
+                if (j < V4) {
+                    f(4 * j, x[u].x);
+                    f(4 * j + 1, x[u].y);
+                    f(4 * j + 2, x[u].z);
+                    f(4 * j + 3, x[u].w);
+                }
+            }
+        }
+    } else {
+        for (int v = threadIdx.x; v < V; v += nt) f(v, row[v]);
+    }
+}
+
 __device__ MaxIdx block_argmax(const float *__restrict__ row, int V, MaxIdx *red) {
     MaxIdx m = {-INFINITY, 0x7fffffff};
-    for (int v = threadIdx.x; v < V; v += blockDim.x) m = better(m, MaxIdx{row[v], v});
+    row_pass(row, V, [&](int v, float x) { m = better(m, MaxIdx{x, v}); });
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         MaxIdx t;
@@ -142,7 +177,7 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample_rows(const float *__rest
     const float invT = 1.0f / temp;
     auto wt = [&](int v) -> u64 { return vxc_weight(row[v], mx.v, invT); };
     u64 s = 0;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) s += wt(v);
+    row_pass(row, V, [&](int, float x) { s += vxc_weight(x, mx.v, invT); });
     u64 S = block_sum_u64(s, red_u);
     uint32_t word = vxc_philox_u32(seed, (uint32_t)pos[r], (uint32_t)seq[r], purpose);
     int t = block_draw(V, draw_threshold(S, word), wt, red_u, &res);
@@ -171,7 +206,9 @@ struct AccStat {
     u64 Sp, Sq, Wpd, Wqd;
 };
 
-__global__ void __launch_bounds__(SMP_THREADS) k_accept(const float *__restrict__ P, long long p_seq, long long p_pos,
+#define ACC_THREADS 256   // 64 x 6 CTAs of 256 threads (<= 64 registers): one wave at 4 CTAs per SM
+
+__global__ void __launch_bounds__(ACC_THREADS, 4) k_accept(const float *__restrict__ P, long long p_seq, long long p_pos,
                                                         const float *__restrict__ Q, long long q_seq, long long q_pos,
                                                         const int *__restrict__ d, int k, int V, float temp, u64 seed,
                                                         const int *__restrict__ seq_id, const int *__restrict__ pos0,
@@ -195,14 +232,14 @@ __global__ void __launch_bounds__(SMP_THREADS) k_accept(const float *__restrict_
         a.Sp = a.Sq = a.Wpd = a.Wqd = 0;
         if (!greedy) {
             u64 sp = 0;
-            for (int v = threadIdx.x; v < V; v += blockDim.x) sp += vxc_weight(pr[v], mp.v, invT);
+            row_pass(pr, V, [&](int, float x) { sp += vxc_weight(x, mp.v, invT); });
             a.Sp = block_sum_u64(sp, red_u);
             if (i < k) {
                 const float *qr = Q + s * q_seq + i * q_pos;
                 MaxIdx mq = block_argmax(qr, V, red_m);
                 a.maxq = mq.v;
                 u64 sq = 0;
-                for (int v = threadIdx.x; v < V; v += blockDim.x) sq += vxc_weight(qr[v], mq.v, invT);
+                row_pass(qr, V, [&](int, float x) { sq += vxc_weight(x, mq.v, invT); });
                 a.Sq = block_sum_u64(sq, red_u);
                 int t = d[s * k + i];
                 if (t >= 0 && t < V) {
@@ -287,7 +324,7 @@ static int launch_accept(const float *P, long long p_seq, long long p_pos, const
                          long long q_pos, const int *d, int n_seq, int k, int V, float temp, uint64_t seed,
                          const int *seq_id, const int *pos0, int *n_acc, int *next, void *ws, cudaStream_t st) {
     size_t a = ((size_t)n_seq * (k + 1) * sizeof(AccStat) + 255) & ~(size_t)255;
-    (k_accept<<<dim3(n_seq, k + 1), SMP_THREADS, 0, st>>>(P, p_seq, p_pos, Q, q_seq, q_pos, d, k, V, temp, seed,
+    (k_accept<<<dim3(n_seq, k + 1), ACC_THREADS, 0, st>>>(P, p_seq, p_pos, Q, q_seq, q_pos, d, k, V, temp, seed,
                                                          seq_id, pos0, n_acc, next, (AccStat *)ws,
                                                          (unsigned int *)((char *)ws + a)), vxc_count_launches(1));
     cudaError_t e = cudaGetLastError();
