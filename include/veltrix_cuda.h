@@ -226,13 +226,16 @@ int vxc_greedy_generate(vxc_seqs *seqs, int slot, int pos0, const int *h_prompt,
  */
 
 /* One token per row of logits[n_rows][V] (device) into tokens[n_rows]
- * (device), row r using Philox counter (pos[r], seq[r], purpose).
+ * (device), row r using Philox counter (pos[r], seq[r], purpose);
+ * n_rows <= 65535.
  * Replaces sample_top_p / sample_greedy (src/speculative.c:35-98) with
  * top_p = 1. */
 int vxc_sample_rows(const float *logits, int n_rows, int V, float temp, uint64_t seed, const int *d_pos,
                     const int *d_seq, unsigned int purpose, int *d_tokens, void *stream);
 
-/* Scratch bytes vxc_accept needs for n_seq sequences of k draft tokens. */
+/* Scratch bytes vxc_accept needs for n_seq sequences of k draft tokens
+ * (0 with the current kernel, which keeps its state on chip; callers pass
+ * what this returns, and workspace may then be NULL). */
 size_t vxc_accept_workspace_bytes(int n_seq, int k);
 
 /* Fused acceptance for n_seq sequences (reference verify_draft,
@@ -243,7 +246,8 @@ size_t vxc_accept_workspace_bytes(int n_seq, int k);
  * pos0[s] + i and uses Philox counters (pos0[s]+i, seq_id[s], ACCEPT /
  * RESAMPLE).  Outputs n_acc[s] in 0..k and next[s] (the correction token,
  * or the bonus token drawn from row k when all k are accepted).  One kernel
- * launch; all pointers are device memory. */
+ * launch (one thread-block cluster per sequence); all pointers are device
+ * memory; k <= 64 and n_seq <= 65535. */
 int vxc_accept(const float *P, long long p_seq, long long p_pos, const float *Q, long long q_seq,
                long long q_pos, const int *d, int n_seq, int k, int V, float temp, uint64_t seed,
                const int *seq_id, const int *pos0, int *n_acc, int *next, void *workspace,

@@ -43,7 +43,7 @@ def run_gpu_accept(torch, P, Q, d, pos0, ids, T, seed):
     nx = torch.zeros(S, dtype=torch.int32, device="cuda")
     wsb = L.vxc_accept_workspace_bytes(S, k)
     ws = torch.zeros(wsb // 4 + 1, dtype=torch.int32, device="cuda")
-    for _ in range(2):   # the second launch checks that the kernel re-arms its counters
+    for _ in range(2):   # a repeated launch gives the same result (no state kept between launches)
         vxb200.check(L.vxc_accept(Pd.data_ptr(), k1 * V, V, Qd.data_ptr(), k * V, V, dd.data_ptr(), S, k, V, T, seed,
                                   idd.data_ptr(), pd_.data_ptr(), na.data_ptr(), nx.data_ptr(), ws.data_ptr(), wsb, None),
                      "vxc_accept")
@@ -89,13 +89,39 @@ def test_accept_edge_cases(cuda):
         assert (a, nxt.value) == (na[s], nx[s])
 
 
-@pytest.mark.parametrize("T", [0.8, 1.5, 0.0])
-def test_sample_rows_bit_exact(cuda, T):
+def test_accept_large_vocab(cuda):
+    """Configuration 5's vocabulary (128256): 2048-element draw sub-blocks."""
+    P, Q, d, pos0, ids = config3(seed=4, S=6, k=6, V=128256)
+    S, k1, V = P.shape
+    k = k1 - 1
+    na, nx = run_gpu_accept(cuda, P, Q, d, pos0, ids, 0.8, 77)
+    O = oracle()
+    for s in range(S):
+        nxt = ctypes.c_int()
+        a = O.vxo_accept(f32p(P[s]), f32p(Q[s]), f32p(d[s]), k, V, 0.8, 77, int(ids[s]), int(pos0[s]), ctypes.byref(nxt))
+        assert (a, nxt.value) == (na[s], nx[s]), s
+
+
+def test_accept_rejects_long_drafts(cuda):
+    import vxb200
+    L = vxb200.lib()
+    torch = cuda
+    buf = torch.zeros(4 * 65 * 100, device="cuda")
+    ib = torch.zeros(130, dtype=torch.int32, device="cuda")
+    rc = L.vxc_accept(buf.data_ptr(), 65 * 100, 100, buf.data_ptr(), 65 * 100, 100, ib.data_ptr(), 1, 65, 100, 0.8,
+                      1, ib.data_ptr(), ib.data_ptr(), ib.data_ptr(), ib.data_ptr(), None, 0, None)
+    assert rc != 0 and b"at most 64" in L.vxc_error_string()
+
+
+@pytest.mark.parametrize("T,V", [(0.8, 32000), (1.5, 32000), (0.0, 32000), (0.8, 1001), (0.0, 1001), (0.7, 100)])
+def test_sample_rows_bit_exact(cuda, T, V):
+    """V = 1001: rows not 16-byte aligned (element loads); V = 100: one
+    CTA of the cluster holds the whole row, the other seven nothing."""
     import vxb200
     torch = cuda
     O = oracle()
     rng = np.random.default_rng(3)
-    R, V = 96, 32000
+    R = 96
     l = (rng.standard_normal((R, V)) * 3).astype(np.float32)
     l[5, 10] = l[5, 20] = l[5].max() + 1       # tie: first maximum wins
     pos = rng.integers(0, 5000, R).astype(np.int32)

@@ -74,10 +74,16 @@ __host__ __device__ __forceinline__ uint32_t vxc_philox_u32(uint64_t seed, uint3
 // Waite 1980) and the degree-7 Taylor polynomial of e^r by Horner with FMA,
 // scaled by 2^k through the exponent field.  Written with explicitly rounded
 // operations so no contraction changes it; bit-identical to the CPU oracle.
+// Branch-free: arguments at or below -80 (and NaN) are clamped, evaluated and
+// then replaced by 0; positive arguments are clamped to 0.
 __device__ __forceinline__ float vxc_expf_canon(float x) {
-    if (!(x > -80.0f)) return 0.0f;
-    if (x > 0.0f) x = 0.0f;
-    float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
+    const bool zero = !(x > -80.0f);
+    x = fminf(fmaxf(x, -80.0f), 0.0f);
+    // k = nearest integer (ties to even) to x log2(e), |x log2(e)| < 116:
+    // adding 1.5 * 2^23 leaves k in the low significand bits, and removing it
+    // again gives k as a float (the classic round-by-magic-constant method).
+    const float big = __fadd_rn(__fmul_rn(x, 1.44269504088896341f), 12582912.0f);
+    const float kf = __fsub_rn(big, 12582912.0f);
     float r = __fmaf_rn(kf, -0.693145751953125f, x);
     r = __fmaf_rn(kf, -1.42860682030941723212e-6f, r);
     float p = 1.98412698412698413e-4f;
@@ -88,15 +94,17 @@ __device__ __forceinline__ float vxc_expf_canon(float x) {
     p = __fmaf_rn(p, r, 0.5f);
     p = __fmaf_rn(p, r, 1.0f);
     p = __fmaf_rn(p, r, 1.0f);
-    int k = (int)kf;
-    return __fmul_rn(p, __uint_as_float((uint32_t)(k + 127) << 23));
+    // 2^k: the bits of big are those of 1.5 * 2^23 + k
+    const uint32_t k127 = __float_as_uint(big) - 0x4B400000u + 127u;
+    const float e = __fmul_rn(p, __uint_as_float(k127 << 23));
+    return zero ? 0.0f : e;
 }
 
 // Integer sampling weight of one logit: trunc(exp((l - max) / T) * 2^32).
+// The scaling by 2^32 is exact; the conversion truncates.
 __device__ __forceinline__ uint64_t vxc_weight(float l, float mx, float invT) {
-    float z = __fmul_rn(__fsub_rn(l, mx), invT);
-    float e = vxc_expf_canon(z);
-    return (uint64_t)__fmul_rn(e, 4294967296.0f);
+    const float z = __fmul_rn(__fsub_rn(l, mx), invT);
+    return (uint64_t)__fmul_rn(vxc_expf_canon(z), 4294967296.0f);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

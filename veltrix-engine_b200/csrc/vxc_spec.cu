@@ -9,7 +9,7 @@
 //     d_{i+1}        sampled from q_i with Philox (pos L+i, DRAFT)
 //     verify         rows (c[L-1], d_1..d_k) at positions L-1..L+k-1 -> p_0..p_k
 //     accept         first rejection i: sample max(0, p_i - q_i); all accepted:
-//                    bonus from p_k                (fused kernel k_accept)
+//                    bonus from p_k         (fused kernel k_accept, one cluster)
 //     commit         c += d_1..d_a, next ; L += a + 1
 // KV invariants: target holds 0..L-2 at round start (the verify rewrites
 // L-1..); draft holds 0..L-3 (step 0 rewrites L-2, L-1).  Positions past a
@@ -19,19 +19,34 @@
 #include "vxc_common.cuh"
 #include "vxc_internal.h"
 
+#include <cooperative_groups.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 #include <vector>
 
+namespace cg = cooperative_groups;
+
 typedef unsigned long long u64;
 typedef unsigned __int128 u128;
 
-#define SMP_THREADS 1024
+// ---------------------------------------------------------------------------
+// cluster row helpers
+//
+// A row of V logits is handled by one thread-block cluster of CL CTAs.  CTA c
+// owns the slice [c*sw, (c+1)*sw) of the row (sw a multiple of 128 elements,
+// so slices of a 16-byte aligned row start 16-byte aligned) and cuts it into
+// at most CL_WARPS draw sub-blocks, one per warp.  Partial results (maxima,
+// weight sums, sub-block sums) are exchanged through distributed shared
+// memory between cluster barriers; every CTA of a cluster passes the same
+// sequence of barriers.
+// ---------------------------------------------------------------------------
+#define CL 8
+#define CL_THREADS 256
+#define CL_WARPS (CL_THREADS / 32)
+#define CL_SUBS (CL * CL_WARPS)   // draw sub-blocks of a row, in element order
+static_assert(CL_SUBS <= CL_THREADS, "one sub-block entry per thread of the leader");
 
-// ---------------------------------------------------------------------------
-// block-wide helpers (blockDim.x a multiple of 32, at most 1024)
-// ---------------------------------------------------------------------------
 struct MaxIdx {
     float v;
     int i;
@@ -43,44 +58,75 @@ __device__ __forceinline__ MaxIdx better(MaxIdx a, MaxIdx b) {
     return a;
 }
 
-// f(v, x) for every element v of a row, x = row[v].  Rows of 16-byte aligned
-// start and V % 4 == 0 are read as float4 with RP_UNROLL loads in flight per
-// thread (one memory latency per RP_UNROLL * 4 * blockDim.x elements, not one
-// per element); other rows element by element.  Visiting order differs per
+struct Slice {
+    int a, b;   // elements [a, b) of the row
+    int sb;     // draw sub-block length, a multiple of 128
+    int nsb;    // sub-blocks in [a, b), at most CL_WARPS
+};
+
+__device__ __forceinline__ Slice cl_slice(int V, int c) {
+    const int sw = ((V + CL - 1) / CL + 127) & ~127;
+    Slice s;
+    s.a = min(V, c * sw);
+    s.b = min(V, s.a + sw);
+    s.sb = ((sw / 128 + CL_WARPS - 1) / CL_WARPS) * 128;
+    s.nsb = (s.b - s.a + s.sb - 1) / s.sb;
+    return s;
+}
+
+// Elements v..v+3 of a row (v % 4 == 0); positions at or past `end` read as
+// -inf (sampling weight 0).  One 16-byte load when the row is 16-byte aligned.
+__device__ __forceinline__ float4 ld_quad(const float *__restrict__ row, int v, int end, bool vec) {
+    if (vec && v + 4 <= end) return __ldg(reinterpret_cast<const float4 *>(row + v));
+    float4 r;
+    r.x = v < end ? __ldg(row + v) : -INFINITY;
+    r.y = v + 1 < end ? __ldg(row + v + 1) : -INFINITY;
+    r.z = v + 2 < end ? __ldg(row + v + 2) : -INFINITY;
+    r.w = v + 3 < end ? __ldg(row + v + 3) : -INFINITY;
+    return r;
+}
+
+// f(v, x) for every element v of [a, b) (a % 4 == 0), a quad per thread per
+// step with up to four quads in flight.  The visiting order differs per
 // thread, so f must be order-independent (integer sums, first-max argmax).
-#define RP_UNROLL 8
 template <class F>
-__device__ __forceinline__ void row_pass(const float *__restrict__ row, int V, F f) {
-    const int nt = blockDim.x;
-    if ((((uintptr_t)row) & 15) == 0 && (V & 3) == 0) {
-        const int V4 = V >> 2;
-        const float4 *r4 = reinterpret_cast<const float4 *>(row);
-        for (int base = 0; base < V4; base += nt * RP_UNROLL) {
-            float4 x[RP_UNROLL];
-#pragma unroll
-            for (int u = 0; u < RP_UNROLL; u++) {
-                const int j = base + u * nt + (int)threadIdx.x;
-                x[u] = j < V4 ? __ldg(r4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < RP_UNROLL; u++) {
-                const int j = base + u * nt + (int)threadIdx.x;
-                if (j < V4) {
-                    f(4 * j, x[u].x);
-                    f(4 * j + 1, x[u].y);
-                    f(4 * j + 2, x[u].z);
-                    f(4 * j + 3, x[u].w);
-                }
-            }
-        }
-    } else {
-        for (int v = threadIdx.x; v < V; v += nt) f(v, row[v]);
+__device__ __forceinline__ void slice_pass(const float *__restrict__ row, int a, int b, bool vec, F f) {
+#pragma unroll 4
+    for (int v = a + 4 * (int)threadIdx.x; v < b; v += 4 * CL_THREADS) {
+        const float4 x = ld_quad(row, v, b, vec);
+        f(v, x.x);
+        if (v + 1 < b) f(v + 1, x.y);
+        if (v + 2 < b) f(v + 2, x.z);
+        if (v + 3 < b) f(v + 3, x.w);
     }
 }
 
-__device__ MaxIdx block_argmax(const float *__restrict__ row, int V, MaxIdx *red) {
-    MaxIdx m = {-INFINITY, 0x7fffffff};
-    row_pass(row, V, [&](int v, float x) { m = better(m, MaxIdx{x, v}); });
+// The same over two rows at once (twice the loads in flight): fa(v, ra[v])
+// and fb(v, rb[v]).
+template <class F, class G>
+__device__ __forceinline__ void slice_pass2(const float *__restrict__ ra, const float *__restrict__ rb, int a, int b,
+                                            bool vec, F fa, G fb) {
+#pragma unroll 2
+    for (int v = a + 4 * (int)threadIdx.x; v < b; v += 4 * CL_THREADS) {
+        const float4 x = ld_quad(ra, v, b, vec), y = ld_quad(rb, v, b, vec);
+        fa(v, x.x);
+        fb(v, y.x);
+        if (v + 1 < b) {
+            fa(v + 1, x.y);
+            fb(v + 1, y.y);
+        }
+        if (v + 2 < b) {
+            fa(v + 2, x.z);
+            fb(v + 2, y.z);
+        }
+        if (v + 3 < b) {
+            fa(v + 3, x.w);
+            fb(v + 3, y.w);
+        }
+    }
+}
+
+__device__ __forceinline__ MaxIdx warp_best(MaxIdx m) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         MaxIdx t;
@@ -88,19 +134,26 @@ __device__ MaxIdx block_argmax(const float *__restrict__ row, int V, MaxIdx *red
         t.i = __shfl_xor_sync(0xffffffffu, m.i, o);
         m = better(m, t);
     }
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    __syncthreads();
-    if (l == 0) red[w] = m;
-    __syncthreads();
-    MaxIdx r = red[0];
-    for (int i = 1; i < (int)(blockDim.x >> 5); i++) r = better(r, red[i]);
-    __syncthreads();
-    return r;
+    return m;
+}
+
+__device__ __forceinline__ u64 warp_sum_u64(u64 v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ u64 warp_incl_scan_u64(u64 v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const u64 t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
 }
 
 __device__ u64 block_sum_u64(u64 v, u64 *red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    v = warp_sum_u64(v);
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     __syncthreads();
     if (l == 0) red[w] = v;
@@ -114,12 +167,7 @@ __device__ u64 block_sum_u64(u64 v, u64 *red) {
 // Exclusive prefix of per-thread values in thread order.
 __device__ u64 block_excl_scan_u64(u64 v, u64 *red) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    u64 inc = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        u64 t = __shfl_up_sync(0xffffffffu, inc, o);
-        if (l >= o) inc += t;
-    }
+    const u64 inc = warp_incl_scan_u64(v, l);
     __syncthreads();
     if (l == 31) red[w] = inc;
     __syncthreads();
@@ -129,28 +177,90 @@ __device__ u64 block_excl_scan_u64(u64 v, u64 *red) {
     return base + inc - v;
 }
 
-// Chunked search: thread t owns elements [t*C, (t+1)*C).  Returns the first
-// v with inclusive prefix sum of wt(v) > thr (or V-1 if none).
-template <class WF>
-__device__ int block_draw(int V, u64 thr, WF wt, u64 *red, int *res) {
-    const int C = (V + blockDim.x - 1) / blockDim.x;
-    const int a = threadIdx.x * C, b = min(V, a + C);
-    u64 s = 0;
-    for (int v = a; v < b; v++) s += wt(v);
-    u64 ex = block_excl_scan_u64(s, red);
-    if (threadIdx.x == 0) *res = V - 1;
+// Sum of w4's weights over each draw sub-block of this CTA's slice: warp j
+// takes sub-block j, lane l the quads at s0 + 128 q + 4 l.  w4(v, end, w)
+// writes the weights of elements v..v+3 (0 at or past end).
+template <class W4>
+__device__ __forceinline__ void slice_sub_sums(const Slice &sl, W4 w4, u64 *sub) {
+    const int j = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (j < sl.nsb) {
+        const int s0 = sl.a + j * sl.sb, s1 = min(sl.b, s0 + sl.sb);
+        u64 acc = 0;
+#pragma unroll 4
+        for (int q = s0 + 4 * lane; q < s1; q += 128) {
+            u64 w[4];
+            w4(q, s1, w);
+            acc += w[0] + w[1] + w[2] + w[3];
+        }
+        acc = warp_sum_u64(acc);
+        if (lane == 0) sub[j] = acc;
+    }
+}
+
+// The cluster leader's entry of the row's sub-block table: thread t <
+// CL_SUBS reads sub-block t % CL_WARPS of CTA t / CL_WARPS (0 where that
+// slice has fewer sub-blocks), so threads 0..CL_SUBS-1 hold the table in
+// element order.  Call between two cluster barriers.
+__device__ __forceinline__ u64 cl_table_entry(cg::cluster_group &cl, int V, u64 *sub) {
+    u64 e = 0;
+    if (threadIdx.x < CL_SUBS) {
+        const int c = threadIdx.x / CL_WARPS, j = threadIdx.x % CL_WARPS;
+        if (j < cl_slice(V, c).nsb) e = *cl.map_shared_rank(sub + j, c);
+    }
+    return e;
+}
+
+// First element whose inclusive prefix weight exceeds thr (V - 1 if none, as
+// the oracle's draw), given each thread's table entry e: a block scan finds
+// the sub-block holding thr, then warp 0 rescans it quad by quad with w4.
+// The result is valid in warp 0.
+template <class W4>
+__device__ int cl_draw(int V, u64 e, u64 thr, W4 w4, u64 *red, int *s_sub, u64 *s_base) {
+    const u64 ex = block_excl_scan_u64(e, red);
+    if (threadIdx.x == 0) *s_sub = -1;
     __syncthreads();
-    if (a < b && ex <= thr && thr < ex + s) {
-        u64 acc = ex;
-        for (int v = a; v < b; v++) {
-            acc += wt(v);
-            if (acc > thr) { *res = v; break; }
+    if (e != 0 && ex <= thr && thr < ex + e) {
+        *s_sub = threadIdx.x;
+        *s_base = ex;
+    }
+    __syncthreads();
+    const int f = *s_sub;
+    int res = V - 1;
+    if (f >= 0 && threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const Slice sl = cl_slice(V, f / CL_WARPS);
+        const int s0 = sl.a + (f % CL_WARPS) * sl.sb, s1 = min(sl.b, s0 + sl.sb);
+        u64 base = *s_base;
+        for (int q = s0; q < s1; q += 128) {
+            const int v = q + 4 * lane;
+            u64 w[4];
+            w4(v, s1, w);
+            const u64 lt = w[0] + w[1] + w[2] + w[3];
+            const u64 inc = warp_incl_scan_u64(lt, lane);
+            const u64 lex = base + inc - lt;
+            const unsigned hit = __ballot_sync(0xffffffffu, lt != 0 && lex <= thr && thr < lex + lt);
+            if (hit) {
+                const int hl = __ffs(hit) - 1;
+                int t = V - 1;
+                if (lane == hl) {
+                    u64 a = lex;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        a += w[i];
+                        if (a > thr) {
+                            t = v + i;
+                            break;
+                        }
+                    }
+                }
+                res = __shfl_sync(0xffffffffu, t, hl);
+                break;
+            }
+            base += __shfl_sync(0xffffffffu, inc, 31);
         }
     }
     __syncthreads();
-    int r = *res;
-    __syncthreads();
-    return r;
+    return res;
 }
 
 __device__ __forceinline__ u64 draw_threshold(u64 S, uint32_t word) {
@@ -158,30 +268,80 @@ __device__ __forceinline__ u64 draw_threshold(u64 S, uint32_t word) {
 }
 
 // ---------------------------------------------------------------------------
-// per-row sampler
+// per-row sampler: one cluster per row (grid CL x n_rows)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(SMP_THREADS) k_sample_rows(const float *__restrict__ logits, int V, float temp,
-                                                             u64 seed, const int *__restrict__ pos,
-                                                             const int *__restrict__ seq, unsigned purpose,
-                                                             int *__restrict__ out) {
-    __shared__ MaxIdx red_m[32];
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(CL_THREADS)
+    k_sample_rows(const float *__restrict__ logits, int V, float temp, u64 seed, const int *__restrict__ pos,
+                  const int *__restrict__ seq, unsigned purpose, int *__restrict__ out, int vec) {
+    cg::cluster_group cl = cg::this_cluster();
+    __shared__ MaxIdx red_m[CL_WARPS];
+    __shared__ MaxIdx part_m, g_m;
     __shared__ u64 red_u[32];
-    __shared__ int res;
-    const int r = blockIdx.x;
+    __shared__ u64 sub[CL_WARPS];
+    __shared__ int s_sub;
+    __shared__ u64 s_base;
+    const int c = blockIdx.x, r = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float *row = logits + (size_t)r * V;
-    MaxIdx mx = block_argmax(row, V, red_m);
+    const Slice sl = cl_slice(V, c);
+    // first maximum of the row
+    MaxIdx m = {-INFINITY, 0x7fffffff};
+    slice_pass(row, sl.a, sl.b, vec, [&](int v, float x) { m = better(m, MaxIdx{x, v}); });
+    m = warp_best(m);
+    if (lane == 0) red_m[w] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        MaxIdx b = red_m[0];
+        for (int i = 1; i < CL_WARPS; i++) b = better(b, red_m[i]);
+        part_m = b;
+    }
+    cl.sync();
+    if (threadIdx.x == 0) {
+        MaxIdx b = *cl.map_shared_rank(&part_m, 0);
+        for (int i = 1; i < CL; i++) b = better(b, *cl.map_shared_rank(&part_m, i));
+        g_m = b;
+    }
+    __syncthreads();
+    const MaxIdx g = g_m;
     if (!(temp > 0.0f)) {
-        if (threadIdx.x == 0) out[r] = mx.i;
+        cl.sync();   // every remote read is done before any CTA of the cluster exits
+        if (c == 0 && threadIdx.x == 0) out[r] = g.i;
         return;
     }
+    // integer weights W_v = vxc_weight(l_v, max, 1/T): sub-block sums, then the draw
     const float invT = 1.0f / temp;
-    auto wt = [&](int v) -> u64 { return vxc_weight(row[v], mx.v, invT); };
-    u64 s = 0;
-    row_pass(row, V, [&](int, float x) { s += vxc_weight(x, mx.v, invT); });
-    u64 S = block_sum_u64(s, red_u);
-    uint32_t word = vxc_philox_u32(seed, (uint32_t)pos[r], (uint32_t)seq[r], purpose);
-    int t = block_draw(V, draw_threshold(S, word), wt, red_u, &res);
+    auto w4 = [&](int v, int end, u64 *wt) {
+        const float4 x = ld_quad(row, v, end, vec);
+        wt[0] = vxc_weight(x.x, g.v, invT);
+        wt[1] = vxc_weight(x.y, g.v, invT);
+        wt[2] = vxc_weight(x.z, g.v, invT);
+        wt[3] = vxc_weight(x.w, g.v, invT);
+    };
+    slice_sub_sums(sl, w4, sub);
+    cl.sync();
+    const u64 e = c == 0 ? cl_table_entry(cl, V, sub) : 0;
+    cl.sync();
+    if (c != 0) return;
+    const u64 S = block_sum_u64(e, red_u);
+    const uint32_t word = vxc_philox_u32(seed, (uint32_t)pos[r], (uint32_t)seq[r], purpose);
+    const int t = cl_draw(V, e, draw_threshold(S, word), w4, red_u, &s_sub, &s_base);
     if (threadIdx.x == 0) out[r] = t;
+}
+
+static int launch_sample_rows(const float *logits, int n_rows, int V, float temp, uint64_t seed, const int *pos,
+                              const int *seq, unsigned purpose, int *out, cudaStream_t st) {
+    if (n_rows > 65535) {
+        vxc_set_error("vxc_sample_rows: %d rows, at most 65535 per launch", n_rows);
+        return -4;
+    }
+    const int vec = (((uintptr_t)logits) & 15) == 0 && (V & 3) == 0;
+    (k_sample_rows<<<dim3(CL, n_rows), CL_THREADS, 0, st>>>(logits, V, temp, seed, pos, seq, purpose, out, vec),
+     vxc_count_launches(1));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        vxc_set_error("vxc_sample_rows: %s", cudaGetErrorString(e));
+        return -3;
+    }
+    return 0;
 }
 
 extern "C" int vxc_sample_rows(const float *logits, int n_rows, int V, float temp, uint64_t seed, const int *d_pos,
@@ -190,119 +350,175 @@ extern "C" int vxc_sample_rows(const float *logits, int n_rows, int V, float tem
         vxc_set_error("vxc_sample_rows: bad arguments");
         return -4;
     }
-    (k_sample_rows<<<n_rows, SMP_THREADS, 0, (cudaStream_t)stream>>>(logits, V, temp, seed, d_pos, d_seq, purpose,
-                                                                    d_tokens), vxc_count_launches(1));
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) { vxc_set_error("vxc_sample_rows: %s", cudaGetErrorString(e)); return -3; }
-    return 0;
+    return launch_sample_rows(logits, n_rows, V, temp, seed, d_pos, d_seq, purpose, d_tokens, (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------
-// fused acceptance
+// fused acceptance: one cluster per sequence (grid CL x n_seq)
+//
+// Rows r = 0..k are the target rows P_0..P_k, rows k+1..2k the draft rows
+// Q_0..Q_{k-1}; every CTA covers its slice of all of them.
+//   1. max and first argmax of every row                      (exchange)
+//   2. integer weight sums S_r of P_j and Q_j, j < k           (exchange)
+//   3. first rejection j: u24 * Wq(d_j) * Sp_j >= 2^24 * Wp(d_j) * Sq_j
+//   4. sub-block sums of the residual (Wp Sq - Wq Sp)^+ >> 36 of row j, or
+//      of the bonus row P_k's weights when all k are accepted (exchange)
+//   5. the cluster leader draws from the sub-block table.
+// Greedy (temp <= 0) stops after 1: the first j with d_j != argmax P_j.
 // ---------------------------------------------------------------------------
-struct AccStat {
-    float maxp, maxq;
-    int argp, pad;
-    u64 Sp, Sq, Wpd, Wqd;
-};
+#define ACC_MAX_K 64
+#define ACC_MAX_ROWS (2 * ACC_MAX_K + 1)
 
-#define ACC_THREADS 256   // 64 x 6 CTAs of 256 threads (<= 64 registers): one wave at 4 CTAs per SM
-
-__global__ void __launch_bounds__(ACC_THREADS, 4) k_accept(const float *__restrict__ P, long long p_seq, long long p_pos,
-                                                        const float *__restrict__ Q, long long q_seq, long long q_pos,
-                                                        const int *__restrict__ d, int k, int V, float temp, u64 seed,
-                                                        const int *__restrict__ seq_id, const int *__restrict__ pos0,
-                                                        int *__restrict__ n_acc, int *__restrict__ next,
-                                                        AccStat *st, unsigned int *__restrict__ cnt) {
-    __shared__ MaxIdx red_m[32];
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(CL_THREADS, 4)
+    k_accept(const float *__restrict__ P, long long p_seq, long long p_pos, const float *__restrict__ Q,
+             long long q_seq, long long q_pos, const int *__restrict__ d, int k, int V, float temp, u64 seed,
+             const int *__restrict__ seq_id, const int *__restrict__ pos0, int *__restrict__ n_acc,
+             int *__restrict__ next, int vec) {
+    cg::cluster_group cl = cg::this_cluster();
+    __shared__ MaxIdx red_m[ACC_MAX_ROWS][CL_WARPS];
+    __shared__ u64 red_s[ACC_MAX_ROWS][CL_WARPS];
+    __shared__ MaxIdx part_m[ACC_MAX_ROWS], g_m[ACC_MAX_ROWS];
+    __shared__ u64 part_s[ACC_MAX_ROWS], g_s[ACC_MAX_ROWS];
+    __shared__ u64 sub[CL_WARPS];
     __shared__ u64 red_u[32];
-    __shared__ int res;
-    __shared__ int is_last;
-    const int s = blockIdx.x, i = blockIdx.y;
+    __shared__ int first_rej, s_sub;
+    __shared__ u64 s_base;
+    const int c = blockIdx.x, s = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool greedy = !(temp > 0.0f);
-    const float invT = greedy ? 0.0f : 1.0f / temp;
-    // ---- phase 1: statistics of row i ----
-    {
-        const float *pr = P + s * p_seq + i * p_pos;
-        MaxIdx mp = block_argmax(pr, V, red_m);
-        AccStat a;
-        a.maxp = mp.v;
-        a.argp = mp.i;
-        a.maxq = 0.0f;
-        a.Sp = a.Sq = a.Wpd = a.Wqd = 0;
-        if (!greedy) {
-            u64 sp = 0;
-            row_pass(pr, V, [&](int, float x) { sp += vxc_weight(x, mp.v, invT); });
-            a.Sp = block_sum_u64(sp, red_u);
-            if (i < k) {
-                const float *qr = Q + s * q_seq + i * q_pos;
-                MaxIdx mq = block_argmax(qr, V, red_m);
-                a.maxq = mq.v;
-                u64 sq = 0;
-                row_pass(qr, V, [&](int, float x) { sq += vxc_weight(x, mq.v, invT); });
-                a.Sq = block_sum_u64(sq, red_u);
-                int t = d[s * k + i];
-                if (t >= 0 && t < V) {
-                    a.Wpd = vxc_weight(pr[t], mp.v, invT);
-                    a.Wqd = vxc_weight(qr[t], mq.v, invT);
-                }
-            }
+    const int R = greedy ? k + 1 : 2 * k + 1;
+    const Slice sl = cl_slice(V, c);
+    auto rowp = [&](int r) -> const float * {
+        return r <= k ? P + s * p_seq + r * p_pos : Q + s * q_seq + (r - k - 1) * q_pos;
+    };
+    if (threadIdx.x == 0) first_rej = k;
+    // 1. maxima: P_j with Q_j (sampled), then the rest of the P rows alone
+    const int npair = greedy ? 0 : k;
+    for (int j = 0; j < npair; j++) {
+        MaxIdx mp = {-INFINITY, 0x7fffffff}, mq = mp;
+        slice_pass2(rowp(j), rowp(k + 1 + j), sl.a, sl.b, vec, [&](int v, float x) { mp = better(mp, MaxIdx{x, v}); },
+                    [&](int v, float x) { mq = better(mq, MaxIdx{x, v}); });
+        mp = warp_best(mp);
+        mq = warp_best(mq);
+        if (lane == 0) {
+            red_m[j][w] = mp;
+            red_m[k + 1 + j][w] = mq;
         }
-        if (threadIdx.x == 0) {
-            st[s * (k + 1) + i] = a;
-            __threadfence();
-            unsigned prev = atomicAdd(&cnt[s], 1u);
-            is_last = (prev == (unsigned)k);
-        }
-        __syncthreads();
-        if (!is_last) return;
     }
-    // ---- phase 2 (last CTA of sequence s): decision and resample ----
-    __threadfence();
-    if (threadIdx.x == 0) cnt[s] = 0;   // re-arm for the next launch
-    // other CTAs wrote these; read them through L2, not a stale L1 line
-    const AccStat *S_ = st + s * (k + 1);
+    for (int r = npair; r <= k; r++) {
+        MaxIdx m = {-INFINITY, 0x7fffffff};
+        slice_pass(rowp(r), sl.a, sl.b, vec, [&](int v, float x) { m = better(m, MaxIdx{x, v}); });
+        m = warp_best(m);
+        if (lane == 0) red_m[r][w] = m;
+    }
     __syncthreads();
-    const int p0 = pos0[s], sid = seq_id[s];
-    int acc = k, nxt = -1, rej = -1;
-    for (int j = 0; j < k; j++) {
-        AccStat a = S_[j];
-        int t = d[s * k + j];
-        bool ok;
-        if (greedy) {
-            ok = (t == a.argp);
-        } else {
-            u64 u = vxc_philox_u32(seed, (uint32_t)(p0 + j), (uint32_t)sid, VXC_PURPOSE_ACCEPT) >> 8;
-            ok = (t >= 0 && t < V) && ((u128)u * a.Wqd * a.Sp < (((u128)a.Wpd * a.Sq) << 24));
-        }
-        if (!ok) { acc = j; rej = j; break; }
+    for (int r = threadIdx.x; r < R; r += CL_THREADS) {
+        MaxIdx b = red_m[r][0];
+        for (int i = 1; i < CL_WARPS; i++) b = better(b, red_m[r][i]);
+        part_m[r] = b;
     }
+    cl.sync();
+    for (int r = threadIdx.x; r < R; r += CL_THREADS) {
+        MaxIdx b = cl.map_shared_rank(part_m, 0)[r];
+        for (int i = 1; i < CL; i++) b = better(b, cl.map_shared_rank(part_m, i)[r]);
+        g_m[r] = b;
+    }
+    __syncthreads();
     if (greedy) {
-        nxt = S_[acc].argp;
-    } else if (rej >= 0) {
-        const AccStat a = S_[rej];
-        const float *pr = P + s * p_seq + rej * p_pos;
-        const float *qr = Q + s * q_seq + rej * q_pos;
-        auto rw = [&](int v) -> u64 {
-            u128 x = (u128)vxc_weight(pr[v], a.maxp, invT) * a.Sq;
-            u128 y = (u128)vxc_weight(qr[v], a.maxq, invT) * a.Sp;
-            return x > y ? (u64)((x - y) >> 36) : 0ull;
-        };
-        u64 sr = 0;
-        for (int v = threadIdx.x; v < V; v += blockDim.x) sr += rw(v);
-        u64 SR = block_sum_u64(sr, red_u);
-        if (SR == 0) {
-            nxt = a.argp;
-        } else {
-            uint32_t w = vxc_philox_u32(seed, (uint32_t)(p0 + rej), (uint32_t)sid, VXC_PURPOSE_RESAMPLE);
-            nxt = block_draw(V, draw_threshold(SR, w), rw, red_u, &res);
+        cl.sync();   // every remote read is done before any CTA of the cluster exits
+        if (c == 0 && threadIdx.x == 0) {
+            int acc = k;
+            for (int j = 0; j < k; j++)
+                if (d[s * k + j] != g_m[j].i) {
+                    acc = j;
+                    break;
+                }
+            n_acc[s] = acc;
+            next[s] = g_m[acc].i;
         }
+        return;
+    }
+    const float invT = 1.0f / temp;
+    // 2. weight sums of P_j and Q_j, j < k (the bonus row's total comes out
+    //    of its sub-block table in 4)
+    for (int j = 0; j < k; j++) {
+        const float mp = g_m[j].v, mq = g_m[k + 1 + j].v;
+        u64 ap = 0, aq = 0;
+        slice_pass2(rowp(j), rowp(k + 1 + j), sl.a, sl.b, vec, [&](int, float x) { ap += vxc_weight(x, mp, invT); },
+                    [&](int, float x) { aq += vxc_weight(x, mq, invT); });
+        ap = warp_sum_u64(ap);
+        aq = warp_sum_u64(aq);
+        if (lane == 0) {
+            red_s[j][w] = ap;
+            red_s[k + 1 + j][w] = aq;
+        }
+    }
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += CL_THREADS) {
+        if (r == k) continue;
+        u64 a = 0;
+        for (int i = 0; i < CL_WARPS; i++) a += red_s[r][i];
+        part_s[r] = a;
+    }
+    cl.sync();
+    for (int r = threadIdx.x; r < R; r += CL_THREADS) {
+        if (r == k) continue;
+        u64 a = 0;
+        for (int i = 0; i < CL; i++) a += cl.map_shared_rank(part_s, i)[r];
+        g_s[r] = a;
+    }
+    __syncthreads();
+    // 3. acceptance tests; the first failing draft position wins
+    const int p0 = pos0[s], sid = seq_id[s];
+    for (int j = threadIdx.x; j < k; j += CL_THREADS) {
+        const int t = d[s * k + j];
+        bool ok = false;
+        if (t >= 0 && t < V) {
+            const u64 wp = vxc_weight(rowp(j)[t], g_m[j].v, invT);
+            const u64 wq = vxc_weight(rowp(k + 1 + j)[t], g_m[k + 1 + j].v, invT);
+            const u64 u = vxc_philox_u32(seed, (uint32_t)(p0 + j), (uint32_t)sid, VXC_PURPOSE_ACCEPT) >> 8;
+            ok = (u128)u * wq * g_s[j] < (((u128)wp * g_s[k + 1 + j]) << 24);
+        }
+        if (!ok) atomicMin(&first_rej, j);
+    }
+    __syncthreads();
+    const int acc = first_rej;
+    const bool resid = acc < k;
+    // 4. the distribution to draw from: residual of row acc, or the bonus row
+    const float *pr = rowp(acc);
+    const float *qr = resid ? rowp(k + 1 + acc) : pr;
+    const float mp = g_m[acc].v, mq = resid ? g_m[k + 1 + acc].v : 0.0f;
+    const u64 Sp = resid ? g_s[acc] : 0, Sq = resid ? g_s[k + 1 + acc] : 0;
+    auto w4 = [&](int v, int end, u64 *wt) {
+        const float4 x = ld_quad(pr, v, end, vec);
+        if (resid) {
+            const float4 y = ld_quad(qr, v, end, vec);
+            const float xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const u128 a = (u128)vxc_weight(xs[i], mp, invT) * Sq;
+                const u128 b = (u128)vxc_weight(ys[i], mq, invT) * Sp;
+                wt[i] = a > b ? (u64)((a - b) >> 36) : 0ull;
+            }
+        } else {
+            wt[0] = vxc_weight(x.x, mp, invT);
+            wt[1] = vxc_weight(x.y, mp, invT);
+            wt[2] = vxc_weight(x.z, mp, invT);
+            wt[3] = vxc_weight(x.w, mp, invT);
+        }
+    };
+    slice_sub_sums(sl, w4, sub);
+    cl.sync();
+    const u64 e = c == 0 ? cl_table_entry(cl, V, sub) : 0;
+    cl.sync();
+    if (c != 0) return;
+    // 5. draw
+    const u64 SR = block_sum_u64(e, red_u);
+    int nxt;
+    if (resid && SR == 0) {
+        nxt = g_m[acc].i;   // p <= q everywhere after rounding: the target's first maximum
     } else {
-        const AccStat a = S_[k];
-        const float *pr = P + s * p_seq + k * p_pos;
-        auto pw = [&](int v) -> u64 { return vxc_weight(pr[v], a.maxp, invT); };
-        uint32_t w = vxc_philox_u32(seed, (uint32_t)(p0 + k), (uint32_t)sid, VXC_PURPOSE_RESAMPLE);
-        nxt = block_draw(V, draw_threshold(a.Sp, w), pw, red_u, &res);
+        const uint32_t word = vxc_philox_u32(seed, (uint32_t)(p0 + acc), (uint32_t)sid, VXC_PURPOSE_RESAMPLE);
+        nxt = cl_draw(V, e, draw_threshold(SR, word), w4, red_u, &s_sub, &s_base);
     }
     if (threadIdx.x == 0) {
         n_acc[s] = acc;
@@ -310,25 +526,28 @@ __global__ void __launch_bounds__(ACC_THREADS, 4) k_accept(const float *__restri
     }
 }
 
-static size_t accept_ws(int n_seq, int k) {
-    size_t a = (size_t)n_seq * (k + 1) * sizeof(AccStat);
-    a = (a + 255) & ~(size_t)255;
-    return a + (size_t)n_seq * sizeof(unsigned int);
-}
+// The kernel keeps all of its state in shared memory; no scratch is needed.
+static size_t accept_ws(int, int) { return 0; }
 
 extern "C" size_t vxc_accept_workspace_bytes(int n_seq, int k) { return accept_ws(n_seq, k); }
 
-// The counters at the end of the workspace must be zero on the first launch;
-// the kernel re-arms them itself.
 static int launch_accept(const float *P, long long p_seq, long long p_pos, const float *Q, long long q_seq,
                          long long q_pos, const int *d, int n_seq, int k, int V, float temp, uint64_t seed,
-                         const int *seq_id, const int *pos0, int *n_acc, int *next, void *ws, cudaStream_t st) {
-    size_t a = ((size_t)n_seq * (k + 1) * sizeof(AccStat) + 255) & ~(size_t)255;
-    (k_accept<<<dim3(n_seq, k + 1), ACC_THREADS, 0, st>>>(P, p_seq, p_pos, Q, q_seq, q_pos, d, k, V, temp, seed,
-                                                         seq_id, pos0, n_acc, next, (AccStat *)ws,
-                                                         (unsigned int *)((char *)ws + a)), vxc_count_launches(1));
+                         const int *seq_id, const int *pos0, int *n_acc, int *next, cudaStream_t st) {
+    if (k > ACC_MAX_K || n_seq > 65535) {
+        vxc_set_error("vxc_accept: k = %d, n_seq = %d (at most %d and 65535)", k, n_seq, ACC_MAX_K);
+        return -4;
+    }
+    const int vec = (((uintptr_t)P) & 15) == 0 && (((uintptr_t)Q) & 15) == 0 && (p_seq & 3) == 0 &&
+                    (p_pos & 3) == 0 && (q_seq & 3) == 0 && (q_pos & 3) == 0;
+    (k_accept<<<dim3(CL, n_seq), CL_THREADS, 0, st>>>(P, p_seq, p_pos, Q, q_seq, q_pos, d, k, V, temp, seed, seq_id,
+                                                     pos0, n_acc, next, vec),
+     vxc_count_launches(1));
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) { vxc_set_error("vxc_accept: %s", cudaGetErrorString(e)); return -3; }
+    if (e != cudaSuccess) {
+        vxc_set_error("vxc_accept: %s", cudaGetErrorString(e));
+        return -3;
+    }
     return 0;
 }
 
@@ -340,12 +559,12 @@ extern "C" int vxc_accept(const float *P, long long p_seq, long long p_pos, cons
         vxc_set_error("vxc_accept: bad arguments");
         return -4;
     }
-    if (!workspace || workspace_bytes < accept_ws(n_seq, k)) {
+    if (workspace_bytes < accept_ws(n_seq, k) || (accept_ws(n_seq, k) && !workspace)) {
         vxc_set_error("vxc_accept: workspace of %zu bytes needed", accept_ws(n_seq, k));
         return -4;
     }
     return launch_accept(P, p_seq, p_pos, Q, q_seq, q_pos, d, n_seq, k, V, temp, seed, seq_id, pos0, n_acc, next,
-                         workspace, (cudaStream_t)stream);
+                         (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -444,7 +663,6 @@ struct vxc_spec {
     SpecDev D;
     float *dlog;       // [k][S][V]
     float *vlog;       // [S][k+1][V]
-    void *acc_ws;
     int *prefill_meta; // per prompt chunk: sequence slot, first position
     int prefill_cap;   // ints in prefill_meta
     cudaStream_t st;
@@ -466,6 +684,10 @@ extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int 
     }
     if (tc.n_vocab != dc.n_vocab) {
         vxc_set_error("vxc_spec_create: draft vocab %d != target vocab %d", dc.n_vocab, tc.n_vocab);
+        return -4;
+    }
+    if (k > ACC_MAX_K || n_seq > 65535) {
+        vxc_set_error("vxc_spec_create: k = %d, n_seq = %d (at most %d and 65535)", k, n_seq, ACC_MAX_K);
         return -4;
     }
     vxc_spec *e = (vxc_spec *)calloc(1, sizeof(vxc_spec));
@@ -513,10 +735,8 @@ extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int 
     DALLOC(D.n_done, sizeof(int));
     DALLOC(e->dlog, (size_t)k * S * e->V * sizeof(float));
     DALLOC(e->vlog, (size_t)S * (k + 1) * e->V * sizeof(float));
-    DALLOC(e->acc_ws, accept_ws(S, k));
     DALLOC(e->prefill_meta, (size_t)e->prefill_cap * sizeof(int));
 #undef DALLOC
-    if (err == cudaSuccess) err = cudaMemset(e->acc_ws, 0, accept_ws(S, k));
     if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
     if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->st2, cudaStreamNonBlocking);
     if (err == cudaSuccess) err = cudaMallocHost((void **)&e->h_ndone, 4 * sizeof(int));
@@ -543,7 +763,7 @@ extern "C" void vxc_spec_destroy(vxc_spec *e) {
     SpecDev &D = e->D;
     void *ptrs[] = {D.c, D.L, D.gen, D.done, D.seq_id, D.slot, D.out, D.tok0, D.pos0, D.lrow0, D.dpos, D.dtok,
                     D.vtok, D.vpos, D.vrows, D.dseq, D.apos, D.n_acc, D.next, D.ctr, D.n_done, e->dlog, e->vlog,
-                    e->acc_ws, e->prefill_meta};
+                    e->prefill_meta};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (e->h_ndone) cudaFreeHost(e->h_ndone);
@@ -562,20 +782,22 @@ static int enqueue_round(vxc_spec *e, float temp, uint64_t seed) {
     (k_round_prep<<<gb, tb, 0, st>>>(D), vxc_count_launches(1));
     // draft step 0: 2 rows per sequence
     if ((rc = vxc_forward(e->ds, D.tok0, D.slot, D.pos0, S, 2, D.lrow0, S, e->dlog, st))) return rc;
-    (k_sample_rows<<<S, SMP_THREADS, 0, st>>>(e->dlog, V, temp, seed, D.dpos, D.seq_id, VXC_PURPOSE_DRAFT, D.dtok), vxc_count_launches(1));
+    if ((rc = launch_sample_rows(e->dlog, S, V, temp, seed, D.dpos, D.seq_id, VXC_PURPOSE_DRAFT, D.dtok, st)))
+        return rc;
     for (int i = 1; i < k; i++) {
         float *q = e->dlog + (size_t)i * S * V;
         // rows: d_i at position L+i-1 == dpos[i-1]; logits of all S rows
         if ((rc = vxc_forward(e->ds, D.dtok + (size_t)(i - 1) * S, D.slot, D.dpos + (size_t)(i - 1) * S, S, 1,
                               D.slot, S, q, st)))
             return rc;
-        (k_sample_rows<<<S, SMP_THREADS, 0, st>>>(q, V, temp, seed, D.dpos + (size_t)i * S, D.seq_id,
-                                                 VXC_PURPOSE_DRAFT, D.dtok + (size_t)i * S), vxc_count_launches(1));
+        if ((rc = launch_sample_rows(q, S, V, temp, seed, D.dpos + (size_t)i * S, D.seq_id, VXC_PURPOSE_DRAFT,
+                                     D.dtok + (size_t)i * S, st)))
+            return rc;
     }
     (k_gather_verify<<<gb, tb, 0, st>>>(D), vxc_count_launches(1));
     if ((rc = vxc_forward(e->ts, D.vtok, D.slot, D.vpos, S, k + 1, D.vrows, S * (k + 1), e->vlog, st))) return rc;
     if ((rc = launch_accept(e->vlog, (long long)(k + 1) * V, V, e->dlog, V, (long long)S * V, D.dseq, S, k, V, temp,
-                            seed, D.seq_id, D.apos, D.n_acc, D.next, e->acc_ws, st)))
+                            seed, D.seq_id, D.apos, D.n_acc, D.next, st)))
         return rc;
     (k_commit<<<gb, tb, 0, st>>>(D), vxc_count_launches(1));
     cudaError_t er = cudaGetLastError();
@@ -816,7 +1038,7 @@ extern "C" int vxc_spec_probe(vxc_spec *e, int which, int reps, double *ms, doub
             rc = vxc_forward(e->ds, D.dtok, D.slot, D.dpos, S, 1, D.slot, S, e->dlog, st);
         else
             rc = launch_accept(e->vlog, (long long)(k + 1) * V, V, e->dlog, V, (long long)S * V, D.dseq, S, k, V,
-                               0.8f, 1, D.seq_id, D.apos, D.n_acc, D.next, e->acc_ws, st);
+                               0.8f, 1, D.seq_id, D.apos, D.n_acc, D.next, st);
     }
     cudaEventRecord(b, st);
     err = cudaStreamSynchronize(st);
