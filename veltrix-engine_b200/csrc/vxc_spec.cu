@@ -36,7 +36,8 @@ typedef unsigned __int128 u128;
 // A row of V logits is handled by one thread-block cluster of CL CTAs.  CTA c
 // owns the slice [c*sw, (c+1)*sw) of the row (sw a multiple of 128 elements,
 // so slices of a 16-byte aligned row start 16-byte aligned) and cuts it into
-// at most CL_WARPS draw sub-blocks, one per warp.  Partial results (maxima,
+// at most CL_SPB draw sub-blocks (CL_SPW per warp), so that the row's
+// sub-block table has one entry per thread of a CTA.  Partial results (maxima,
 // weight sums, sub-block sums) are exchanged through distributed shared
 // memory between cluster barriers; every CTA of a cluster passes the same
 // sequence of barriers.
@@ -44,7 +45,9 @@ typedef unsigned __int128 u128;
 #define CL 8
 #define CL_THREADS 256
 #define CL_WARPS (CL_THREADS / 32)
-#define CL_SUBS (CL * CL_WARPS)   // draw sub-blocks of a row, in element order
+#define CL_SPW 4                   // draw sub-blocks per warp
+#define CL_SPB (CL_WARPS * CL_SPW)  // draw sub-blocks per CTA
+#define CL_SUBS (CL * CL_SPB)       // draw sub-blocks of a row, in element order
 static_assert(CL_SUBS <= CL_THREADS, "one sub-block entry per thread of the leader");
 
 struct MaxIdx {
@@ -61,7 +64,7 @@ __device__ __forceinline__ MaxIdx better(MaxIdx a, MaxIdx b) {
 struct Slice {
     int a, b;   // elements [a, b) of the row
     int sb;     // draw sub-block length, a multiple of 128
-    int nsb;    // sub-blocks in [a, b), at most CL_WARPS
+    int nsb;    // sub-blocks in [a, b), at most CL_SPB
 };
 
 __device__ __forceinline__ Slice cl_slice(int V, int c) {
@@ -69,7 +72,7 @@ __device__ __forceinline__ Slice cl_slice(int V, int c) {
     Slice s;
     s.a = min(V, c * sw);
     s.b = min(V, s.a + sw);
-    s.sb = ((sw / 128 + CL_WARPS - 1) / CL_WARPS) * 128;
+    s.sb = ((sw / 128 + CL_SPB - 1) / CL_SPB) * 128;
     s.nsb = (s.b - s.a + s.sb - 1) / s.sb;
     return s;
 }
@@ -177,34 +180,43 @@ __device__ u64 block_excl_scan_u64(u64 v, u64 *red) {
     return base + inc - v;
 }
 
-// Sum of w4's weights over each draw sub-block of this CTA's slice: warp j
-// takes sub-block j, lane l the quads at s0 + 128 q + 4 l.  w4(v, end, w)
+// Sum of w4's weights over each draw sub-block of this CTA's slice: warp w
+// takes sub-blocks w, w + CL_WARPS, ... (CL_SPW of them, summed side by side
+// for loads in flight), lane l the quads at s0 + 128 q + 4 l.  w4(v, end, w)
 // writes the weights of elements v..v+3 (0 at or past end).
 template <class W4>
 __device__ __forceinline__ void slice_sub_sums(const Slice &sl, W4 w4, u64 *sub) {
-    const int j = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (j < sl.nsb) {
-        const int s0 = sl.a + j * sl.sb, s1 = min(sl.b, s0 + sl.sb);
-        u64 acc = 0;
-#pragma unroll 4
-        for (int q = s0 + 4 * lane; q < s1; q += 128) {
-            u64 w[4];
-            w4(q, s1, w);
-            acc += w[0] + w[1] + w[2] + w[3];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    u64 acc[CL_SPW];
+#pragma unroll
+    for (int t = 0; t < CL_SPW; t++) {
+        const int j = w + t * CL_WARPS;
+        acc[t] = 0;
+        if (j < sl.nsb) {
+            const int s0 = sl.a + j * sl.sb, s1 = min(sl.b, s0 + sl.sb);
+            for (int q = s0 + 4 * lane; q < s1; q += 128) {
+                u64 x[4];
+                w4(q, s1, x);
+                acc[t] += x[0] + x[1] + x[2] + x[3];
+            }
         }
-        acc = warp_sum_u64(acc);
-        if (lane == 0) sub[j] = acc;
+    }
+#pragma unroll
+    for (int t = 0; t < CL_SPW; t++) {
+        const int j = w + t * CL_WARPS;
+        const u64 a = warp_sum_u64(acc[t]);
+        if (lane == 0 && j < sl.nsb) sub[j] = a;
     }
 }
 
 // The cluster leader's entry of the row's sub-block table: thread t <
-// CL_SUBS reads sub-block t % CL_WARPS of CTA t / CL_WARPS (0 where that
-// slice has fewer sub-blocks), so threads 0..CL_SUBS-1 hold the table in
-// element order.  Call between two cluster barriers.
+// CL_SUBS reads sub-block t % CL_SPB of CTA t / CL_SPB (0 where that slice
+// has fewer sub-blocks), so threads 0..CL_SUBS-1 hold the table in element
+// order.  Call between two cluster barriers.
 __device__ __forceinline__ u64 cl_table_entry(cg::cluster_group &cl, int V, u64 *sub) {
     u64 e = 0;
     if (threadIdx.x < CL_SUBS) {
-        const int c = threadIdx.x / CL_WARPS, j = threadIdx.x % CL_WARPS;
+        const int c = threadIdx.x / CL_SPB, j = threadIdx.x % CL_SPB;
         if (j < cl_slice(V, c).nsb) e = *cl.map_shared_rank(sub + j, c);
     }
     return e;
@@ -228,8 +240,8 @@ __device__ int cl_draw(int V, u64 e, u64 thr, W4 w4, u64 *red, int *s_sub, u64 *
     int res = V - 1;
     if (f >= 0 && threadIdx.x < 32) {
         const int lane = threadIdx.x;
-        const Slice sl = cl_slice(V, f / CL_WARPS);
-        const int s0 = sl.a + (f % CL_WARPS) * sl.sb, s1 = min(sl.b, s0 + sl.sb);
+        const Slice sl = cl_slice(V, f / CL_SPB);
+        const int s0 = sl.a + (f % CL_SPB) * sl.sb, s1 = min(sl.b, s0 + sl.sb);
         u64 base = *s_base;
         for (int q = s0; q < s1; q += 128) {
             const int v = q + 4 * lane;
@@ -277,7 +289,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(CL_THREADS)
     __shared__ MaxIdx red_m[CL_WARPS];
     __shared__ MaxIdx part_m, g_m;
     __shared__ u64 red_u[32];
-    __shared__ u64 sub[CL_WARPS];
+    __shared__ u64 sub[CL_SPB];
     __shared__ int s_sub;
     __shared__ u64 s_base;
     const int c = blockIdx.x, r = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -379,7 +391,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(CL_THREADS, 4)
     __shared__ u64 red_s[ACC_MAX_ROWS][CL_WARPS];
     __shared__ MaxIdx part_m[ACC_MAX_ROWS], g_m[ACC_MAX_ROWS];
     __shared__ u64 part_s[ACC_MAX_ROWS], g_s[ACC_MAX_ROWS];
-    __shared__ u64 sub[CL_WARPS];
+    __shared__ u64 sub[CL_SPB];
     __shared__ u64 red_u[32];
     __shared__ int first_rej, s_sub;
     __shared__ u64 s_base;
