@@ -1,9 +1,10 @@
-"""GPU parity: quantised GEMV (tcgen05 kernel and the exact CUDA-core kernel)
-against the CPU oracle, through the C-ABI (vxc_qgemv / vxc_qgemv_simt).
+"""GPU parity: quantised GEMV against the CPU oracle, through the C-ABI.
+vxc_qgemv runs the streaming CUDA-core kernel for M <= 2 and the tcgen05
+kernel above; vxc_qgemv_simt is the plain CUDA-core cross-check.
 
-Tolerance: both kernels accumulate in fp32 from exact integer weights and a
+Tolerance: the kernels accumulate in fp32 from exact integer weights and a
 22-bit activation split (tensor-core path) or fp32 activations (CUDA-core
-path); they differ from the reference only in summation order, so
+paths); they differ from the reference only in summation order, so
 max|y_gpu - y_oracle| <= 2e-5 * max|y_oracle| (K <= 11008).
 """
 import ctypes
@@ -84,3 +85,25 @@ def test_zero_and_large_activations(cuda):
     assert np.all(y[0] == 0)
     for m in (1, 2, 3):
         assert np.max(np.abs(y[m] - yo[m])) <= TOL * np.max(np.abs(yo[m]))
+
+
+def test_skinny_rows_do_not_depend_on_m(cuda):
+    """One and two activation rows share one accumulation order: row 0 of a
+    two-row call equals the one-row call bit for bit."""
+    import vxb200
+    torch = cuda
+    rng = np.random.default_rng(21)
+    for qt, rows, cols in ((2, 4096, 4096), (8, 2560, 2048)):
+        blk = (q4_0_blocks if qt == 2 else q8_0_blocks)(rows, cols, rng)
+        W = vxb200.QMat(qt, blk, rows, cols)
+        x = torch.from_numpy(rng.standard_normal((2, cols)).astype(np.float32)).cuda()
+        ys = []
+        for M in (1, 2):
+            wsb = max(W.workspace_bytes(M), 4)
+            ws = torch.empty(wsb // 4 + 1, device="cuda")
+            y = torch.empty((M, rows), device="cuda")
+            W.gemv(x.data_ptr(), M, y.data_ptr(), ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            ys.append(y.cpu().numpy())
+        W.close()
+        assert np.array_equal(ys[0][0], ys[1][0]), qt

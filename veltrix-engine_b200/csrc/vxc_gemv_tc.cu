@@ -604,9 +604,15 @@ extern "C" size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M) {
         size_t t = chunk_ws_bytes(w, M % 64);
         if (t > b) b = t;
     }
-    // the same scratch also serves vxc_qgemv_simt
+    // the same scratch also serves vxc_qgemv_simt and the skinny GEMV's partials
     const size_t simt = vxc_qgemv_simt_ws(w, M);
-    return b > simt ? b : simt;
+    if (simt > b) b = simt;
+    if (vxc_skinny_ok(w, M)) {
+        const int ks = vxc_skinny_slices(w);
+        const size_t sk = ks > 1 ? (size_t)ks * M * w->rows * sizeof(float) : 0;
+        if (sk > b) b = sk;
+    }
+    return b;
 }
 
 extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, void *workspace,
@@ -616,6 +622,18 @@ extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, voi
     if (((uintptr_t)workspace & 15) != 0) { vxc_set_error("vxc_qgemv: workspace must be 16-byte aligned"); return -4; }
     cudaStream_t st = (cudaStream_t)stream;
     if (vxc_is_kquant(w->type)) return vxc_kquant_gemv(w, x, M, y, st);   // no workspace
+    if (vxc_skinny_ok(w, M)) {   // few rows: CUDA-core kernel, HBM-bound
+        const int ks = vxc_skinny_slices(w);
+        const size_t need = ks > 1 ? (size_t)ks * M * w->rows * sizeof(float) : 0;
+        if ((need && !workspace) || need > workspace_bytes) {
+            vxc_set_error("vxc_qgemv: workspace %zu < %zu bytes", workspace_bytes, need);
+            return -4;
+        }
+        float *part = ks > 1 ? (float *)workspace : y;
+        int rc = vxc_skinny_run(w, x, w->cols, M, part, st);
+        if (rc == 0 && ks > 1) rc = vxc_launch_splitk_reduce(part, ks, M, w->rows, y, st);
+        return rc;
+    }
     for (int m0 = 0; m0 < M; m0 += 64) {
         const int mc = M - m0 < 64 ? M - m0 : 64;
         VxcGemvPlan p;

@@ -55,6 +55,17 @@ bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p);
 int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, float *part,
                  const VxcGemvPlan &p, cudaStream_t st, const float *x = NULL);
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
+
+// CUDA-core GEMV for few activation rows (vxc_gemv_skinny.cu): Q4_0 / Q8_0,
+// 1 <= M <= VXC_SKINNY_MAX_M, x rows of ldx floats (16-byte aligned).
+// Writes partials [ks][M][R] (the result itself when ks == 1), ks =
+// vxc_skinny_slices(w), which depends on the shape only.  Up to 2 rows it is
+// faster than the tensor-core kernel on every measured shape (HBM-bound
+// streaming); from 5 rows on the tensor cores win (M FMAs per weight).
+#define VXC_SKINNY_MAX_M 2
+int vxc_skinny_ok(const vxc_qmat *w, int M);
+int vxc_skinny_slices(const vxc_qmat *w);
+int vxc_skinny_run(const vxc_qmat *w, const float *x, int ldx, int M, float *out, cudaStream_t st);
 // The calling thread's current CUDA context (driver handle), or NULL.
 void *vxc_current_context(void);
 // Library-wide count of kernel launches (a CUDA-graph replay adds its kernels).
