@@ -585,6 +585,12 @@ def run_spec7b_gpu(args, ws, rank, local):
                           "rounds": st.rounds, "decode_ms": st.decode_ms}
         agree.close()
         progress("batch-1 verify and full-acceptance runs done")
+    if TP and dist:
+        # the verify's exchanges at the engine's message sizes (every rank, same order)
+        rows = S * (k + 1)
+        extra["collectives"] = measure_collectives(torch, dist, ws, rows * SPEC_TARGET[0],
+                                                   rows * (SPEC_TARGET[5] // ws))
+        progress("collective timing done")
     t, n = reduce_over_ranks(dist, [dec_ms, pre_ms, wall_s, v_ms, d_ms, a_ms],
                              [emitted, accepted, drafted, rounds, launches], "cuda")
     dec_ms, pre_ms, wall_s, v_ms_max, d_ms_max, a_ms_max = t
@@ -604,6 +610,44 @@ def run_spec7b_gpu(args, ws, rank, local):
         dist.barrier()
         dist.destroy_process_group()
     return res
+
+
+def measure_collectives(torch, dist, ws, n_sum, n_gather_per_rank, reps=20):
+    """Device time of the tensor-parallel verify's two exchanges, through
+    torch.distributed's NCCL (the library the engine's vxc_tp.cu calls too) at
+    the engine's message sizes: the fp32 all-reduce of one row-split
+    projection's output (two per layer) and the all-gather of the
+    vocabulary-split logits (one per forward).  CUDA events over `reps`
+    back-to-back calls after 3 warm-ups; max over ranks."""
+    a = torch.ones(n_sum, device="cuda")
+    g_in = torch.ones(n_gather_per_rank, device="cuda")
+    g_out = torch.empty(n_gather_per_rank * ws, device="cuda")
+    for _ in range(3):
+        dist.all_reduce(a)
+        dist.all_gather_into_tensor(g_out, g_in)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
+    for _ in range(reps):
+        dist.all_reduce(a)
+    ev[1].record()
+    for _ in range(reps):
+        dist.all_gather_into_tensor(g_out, g_in)
+    ev[2].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([ev[0].elapsed_time(ev[1]) * 1e3 / reps, ev[1].elapsed_time(ev[2]) * 1e3 / reps],
+                     device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ar_us, ag_us = float(t[0]), float(t[1])
+    ar_b, ag_b = n_sum * 4, n_gather_per_rank * ws * 4
+    return {"allreduce_bytes": ar_b, "allreduce_us": round(ar_us, 2),
+            "allreduce_busbw_gbs": round(2 * (ws - 1) / ws * ar_b / (ar_us * 1e-6) / 1e9, 1),
+            "gather_bytes": ag_b, "gather_us": round(ag_us, 2),
+            "gather_busbw_gbs": round((ws - 1) / ws * ag_b / (ag_us * 1e-6) / 1e9, 1),
+            "note": "torch.distributed NCCL at the engine's sizes: one row-split projection's fp32 output "
+                    "(all-reduced twice per layer) and the vocabulary-split logits (gathered once per forward); "
+                    "CUDA events, max over ranks"}
 
 
 def cpu_spec7b_reference(threads, reps=2):
@@ -869,6 +913,12 @@ def main_spec7b(args, ws, rank, threads):
             "rate": round(g["accepted"] / max(1, g["drafted"]), 4),
             "note": "the same engine and sequences, 32 new tokens, greedy, with the target drafting for itself "
                     "(every draft accepted: k + 1 tokens per round; each draft step is a 7B forward)"}
+    if "collectives" in ex:
+        c = dict(ex["collectives"])
+        per_verify = 2 * SPEC_TARGET[1] * c["allreduce_us"] + c["gather_us"]
+        c["per_verify_us"] = round(per_verify, 1)
+        c["share_of_verify"] = round(per_verify * 1e-3 / r["v_ms"], 4)
+        out["collectives"] = c
     out.update(subs)
     if not TP and not TINY:
         out["dtype"] = "f32 (tensor-core GEMV: exact weights, fp32 activations split into fp16 hi + lo, 22 bits)"
