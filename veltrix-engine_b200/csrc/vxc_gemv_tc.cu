@@ -26,8 +26,10 @@
 // of different threads overlap, so one issuer cannot keep up with HBM at
 // these sizes; several threads issuing into separate accumulators can.  The image
 // stacks [x_hi; x_lo] as 2N rows of B, so per K step two MMAs (A = w_hi, then
-// A = w_lo) give all four hi/lo products in one 2N-column accumulator; the
-// epilogue adds column m and N + m.
+// A = w_lo) give the hi/lo products in one 2N-column accumulator; the
+// epilogue adds column m and N + m.  With GM_LO_HALF_N (the default) the w_lo
+// MMA covers the x_hi rows only, dropping w_lo * x_lo (at most 2^-22 of the
+// product).
 //
 // Warp roles (448 threads, one CTA per SM):
 //   warp 0      producer: cp.async.bulk of KB weight records per stage into
@@ -82,8 +84,9 @@
 #define GM_RING_BLOCKS 24   // Q4_0 blocks in flight per CTA (Q8_0: two thirds)
 #endif
 #ifndef GM_LO_HALF_N
-#define GM_LO_HALF_N 0      // 1: the w_lo MMA over the x_hi rows only (drops w_lo*x_lo, <= 2^-22 of a
-                            // product): 3N instead of 4N accumulator columns of tensor work per K step
+#define GM_LO_HALF_N 1      // 1: the w_lo MMA over the x_hi rows only (drops w_lo*x_lo, <= 2^-22 of a
+                            // product): 3N instead of 4N accumulator columns of tensor work per K step;
+                            // measured 0-3% faster on B200 (the kernel is issue-bound), parity unchanged
 #endif
 template <int QT, int NT>
 struct GmCfg {

@@ -75,6 +75,7 @@ struct vxc_seqs {
     float *xs;               // [chunks * 64] image prescales
     float *part;             // GEMV partial sums, one slot per chunk
     size_t part_slot;        // floats per chunk slot
+    float *xf;               // [VXC_SKINNY_MAX_M][K] fp32 rows for the CUDA-core GEMV of 1-2 rows
     float *attn_part;
     int attn_sl, attn_splits;
     float *ar;               // [max_rows][E] all-reduced projection output (tensor parallel)
@@ -475,6 +476,10 @@ __device__ __forceinline__ void image_cols(uint8_t *img, size_t chunk_bytes, int
     }
 }
 
+// The row kernels below write their output for the next GEMV either as its
+// tensor-core image (img != NULL, with the row prescale xs) or, when that GEMV
+// runs on the CUDA cores (1-2 rows), as fp32 rows xf[m][K] (img == NULL).
+
 // Residual update and RMSNorm into the next GEMV's image:
 //   x[src] += sum of the previous GEMV's partials (when add.base != NULL)
 //   h = w * (x[src] * (1/sqrt(sum(x^2)/E + 1e-5)))        (src/tensor.c:132-140)
@@ -484,7 +489,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_image(float *__restrict__ 
                                                               const float *__restrict__ w, int E,
                                                               const int *__restrict__ rows, int write_x, int M_out,
                                                               uint8_t *__restrict__ img, size_t chunk_bytes,
-                                                              float *__restrict__ xs) {
+                                                              float *__restrict__ xs, float *__restrict__ xf) {
     extern __shared__ float v[];   // local columns
     __shared__ float red[32], slots[2];
     cg::cluster_group cl = cg::this_cluster();
@@ -510,20 +515,24 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_image(float *__restrict__ 
     for (int i = k0 + threadIdx.x; i < k1; i += blockDim.x) {
         const float h = rms < 1e-10f ? 0.0f : __fmul_rn(w[i], __fmul_rn(v[i - k0], inv));
         v[i - k0] = h;
+        if (!img) xf[(size_t)m * E + i] = h;
         mx = fmaxf(mx, fabsf(h));
     }
-    mx = cluster_reduce(cl, block_max(mx, red), &slots[1], 1);
-    const float s = vxc_prescale(mx);
-    if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
-    __syncthreads();
-    image_cols(img, chunk_bytes, m, M_out, k0, k1, s, [&](int k) { return v[k - k0]; });
+    if (img) {
+        mx = cluster_reduce(cl, block_max(mx, red), &slots[1], 1);
+        const float s = vxc_prescale(mx);
+        if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
+        __syncthreads();
+        image_cols(img, chunk_bytes, m, M_out, k0, k1, s, [&](int k) { return v[k - k0]; });
+    }
     cl.sync();   // peers have read this CTA's slots
 }
 
 // f = |silu(g)| < 0.01 ? 0 : silu(g) * u  (src/model.c:580-585, src/tensor.c:71-88, :277)
 // from the fused gate/up GEMV's partials, then the image for the down GEMV.
 __global__ void __launch_bounds__(ROW_THREADS) k_swiglu_image(Part gu, int F, int M, uint8_t *__restrict__ img,
-                                                                size_t chunk_bytes, float *__restrict__ xs) {
+                                                                size_t chunk_bytes, float *__restrict__ xs,
+                                                                float *__restrict__ xf) {
     extern __shared__ float v[];
     __shared__ float red[32], slots[1];
     cg::cluster_group cl = cg::this_cluster();
@@ -538,13 +547,16 @@ __global__ void __launch_bounds__(ROW_THREADS) k_swiglu_image(Part gu, int F, in
         const float sl = g / (1.0f + expf(-g));
         const float f = (fabsf(sl) < 0.01f) ? __fmul_rn(sl, 0.0f) : __fmul_rn(sl, u);
         v[j - k0] = f;
+        if (!img) xf[(size_t)m * F + j] = f;
         mx = fmaxf(mx, fabsf(f));
     }
-    mx = cluster_reduce(cl, block_max(mx, red), &slots[0], 1);
-    const float s = vxc_prescale(mx);
-    if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
-    __syncthreads();
-    image_cols(img, chunk_bytes, m, M, k0, k1, s, [&](int k) { return v[k - k0]; });
+    if (img) {
+        mx = cluster_reduce(cl, block_max(mx, red), &slots[0], 1);
+        const float s = vxc_prescale(mx);
+        if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
+        __syncthreads();
+        image_cols(img, chunk_bytes, m, M, k0, k1, s, [&](int k) { return v[k - k0]; });
+    }
     cl.sync();
 }
 
@@ -554,7 +566,8 @@ __global__ void __launch_bounds__(ROW_THREADS) k_swiglu_image(Part gu, int F, in
 // One warp per head; lane s holds split s's weight e^{m_s-M}.
 __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__restrict__ part, int T, int H, int KH,
                                                                  int hd, int nsplit, int M, uint8_t *__restrict__ img,
-                                                                 size_t chunk_bytes, float *__restrict__ xs) {
+                                                                 size_t chunk_bytes, float *__restrict__ xs,
+                                                                 float *__restrict__ xf) {
     extern __shared__ float v[];
     __shared__ float red[32], slots[1];
     cg::cluster_group cl = cg::this_cluster();
@@ -588,14 +601,17 @@ __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__re
             }
             const float val = o * inv;
             v[(h - h0) * hd + d] = val;
+            if (!img) xf[(size_t)m * H * hd + h * hd + d] = val;
             mx = fmaxf(mx, fabsf(val));
         }
     }
-    mx = cluster_reduce(cl, block_max(mx, red), &slots[0], 1);
-    const float s = vxc_prescale(mx);
-    if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
-    __syncthreads();
-    image_cols(img, chunk_bytes, m, M, h0 * hd, h1 * hd, s, [&](int k) { return v[k - h0 * hd]; });
+    if (img) {
+        mx = cluster_reduce(cl, block_max(mx, red), &slots[0], 1);
+        const float s = vxc_prescale(mx);
+        if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
+        __syncthreads();
+        image_cols(img, chunk_bytes, m, M, h0 * hd, h1 * hd, s, [&](int k) { return v[k - h0 * hd]; });
+    }
     cl.sync();
 }
 
@@ -1181,6 +1197,11 @@ static size_t part_slot_floats(const vxc_net *n) {
                 if (f > best) best = f;
             }
         }
+        for (int m = 1; m <= VXC_SKINNY_MAX_M; m++)   // the CUDA-core GEMV of 1-2 rows
+            if (vxc_skinny_ok(w, m)) {
+                const size_t f = (size_t)vxc_skinny_slices(w) * m * w->rows;
+                if (f > best) best = f;
+            }
     };
     for (int l = 0; l < n->cfg.n_layers; l++) {
         consider(n->layers[l].wqkv);
@@ -1229,6 +1250,11 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     ALLOC(s->img, (size_t)nch * s->img_chunk);
     ALLOC(s->xs, (size_t)nch * 64 * 4);
     ALLOC(s->part, (size_t)nch * s->part_slot * 4);
+    {
+        size_t kmax = (size_t)(E > F ? E : F);
+        if ((size_t)net->Hl * hd > kmax) kmax = (size_t)net->Hl * hd;
+        ALLOC(s->xf, (size_t)VXC_SKINNY_MAX_M * kmax * 4);
+    }
     ALLOC(s->attn_part, part * 4);
     if (net->tp) {
         ALLOC(s->ar, (size_t)max_rows * E * 4);
@@ -1275,7 +1301,8 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
 
 extern "C" void vxc_seqs_destroy(vxc_seqs *s) {
     if (!s) return;
-    void *ptrs[] = {s->k, s->v, s->x, s->qbuf, s->img, s->xs, s->part, s->attn_part, s->ar, s->lg_local, s->lg_all};
+    void *ptrs[] = {s->k, s->v, s->x, s->qbuf, s->img, s->xs, s->part, s->xf, s->attn_part, s->ar, s->lg_local,
+                    s->lg_all};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     free(s);
@@ -1329,8 +1356,12 @@ extern "C" int vxc_profile_read(double *ms, int n) {
     return VXC_N_STAGES;
 }
 
-// GEMV over M rows in chunks of 64 (image chunks -> partial slots); returns
-// the Part view of its output.
+// Whether the GEMV of w over M rows runs on the CUDA cores from the fp32 rows
+// s->xf (1-2 rows of a Q4_0 / Q8_0 matrix) rather than from the image.
+static bool skinny(const vxc_qmat *w, int M) { return vxc_skinny_ok(w, M) != 0; }
+
+// GEMV over M rows in chunks of 64 (image chunks -> partial slots), or on the
+// CUDA cores from s->xf when skinny(w, M); returns the Part view of its output.
 static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStream_t st) {
     Part p;
     p.base = s->part;
@@ -1338,6 +1369,17 @@ static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStrea
     p.R = w->rows;
     p.M = M;
     p.ks_full = p.ks_last = 1;
+    if (skinny(w, M)) {
+        const int ks = vxc_skinny_slices(w);
+        if ((size_t)ks * M * w->rows > s->part_slot) {
+            vxc_set_error("vxc_forward: partial slot too small");
+            return -4;
+        }
+        if (int rc = vxc_skinny_run(w, s->xf, w->cols, M, s->part, st)) return rc;
+        p.ks_full = p.ks_last = ks;
+        *out = p;
+        return 0;
+    }
     if (vxc_is_kquant(w->type) || w->type == VXC_QMAT_STACK) {   // CUDA-core K-quant GEMV, one slice
         for (int c = 0; c * 64 < M; c++) {
             const int Mc = M - c * 64 < 64 ? M - c * 64 : 64;
@@ -1439,7 +1481,8 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         float *vc = s->v + (size_t)l * s->n_slots * s->max_ctx * kvd;
         pe = prof_begin(st);
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, prev,
-                               d->attn_norm, E, (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+                               d->attn_norm, E, (const int *)NULL, 1, M, skinny(d->wqkv, M) ? NULL : s->img,
+                               s->img_chunk, s->xs, s->xf);
         prof_end(1, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
@@ -1458,8 +1501,8 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         e = launch_pdl_cluster(k_combine_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL,
-                               (const float *)s->attn_part, T, H, KH, hd, s->attn_splits, M, s->img, s->img_chunk,
-                               s->xs);
+                               (const float *)s->attn_part, T, H, KH, hd, s->attn_splits, M,
+                               skinny(d->wo, M) ? NULL : s->img, s->img_chunk, s->xs, s->xf);
         prof_end(5, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
@@ -1468,7 +1511,8 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         prof_end(6, pe, st);
         pe = prof_begin(st);
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, pp,
-                               d->ffn_norm, E, (const int *)NULL, 1, M, s->img, s->img_chunk, s->xs);
+                               d->ffn_norm, E, (const int *)NULL, 1, M, skinny(d->wgu, M) ? NULL : s->img,
+                               s->img_chunk, s->xs, s->xf);
         prof_end(7, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
@@ -1476,7 +1520,7 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         prof_end(8, pe, st);
         pe = prof_begin(st);
         e = launch_pdl_cluster(k_swiglu_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, pp, F, M,
-                               s->img, s->img_chunk, s->xs);
+                               skinny(d->wd, M) ? NULL : s->img, s->img_chunk, s->xs, s->xf);
         prof_end(9, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
@@ -1489,8 +1533,8 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         const int V = c.n_vocab;
         // last residual update fused with the final norm, for the requested rows only
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, n_logit_rows), dim3(ROW_THREADS), row_smem, st, ROW_CL,
-                               s->x, prev, n->out_norm, E, d_logit_rows, 0, n_logit_rows, s->img, s->img_chunk,
-                               s->xs);
+                               s->x, prev, n->out_norm, E, d_logit_rows, 0, n_logit_rows,
+                               skinny(n->out, n_logit_rows) ? NULL : s->img, s->img_chunk, s->xs, s->xf);
         if (e == cudaSuccess) {
             if ((rc = gemv_rows(s, n->out, n_logit_rows, &pp, st))) return rc;
             const size_t tot = (size_t)n_logit_rows * n->Vl;
