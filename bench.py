@@ -33,7 +33,9 @@ Workload `q4matvec` (benchmark configuration 2): Q4_0 verify matmuls 4096x4096 a
 11008x4096 at M = 1, 2, 5, 8 activation rows, fp32 activations and
 accumulation.  One step = one GEMV over every rotated weight copy for each of
 the 8 (shape, M) cases; the copies of each shape exceed 2x the 126 MB L2, so
-every step streams its weights from HBM.
+every step streams its weights from HBM.  The device-side numbers replay a
+CUDA graph of the public vxc_qgemv calls (the host's per-call launch cost is
+not GPU time); `e2e` calls vxc_qgemv one by one with host buffers.
 
 Workload `spec_tiny` (benchmark configuration 1): the tiny Q8_0 target and
 draft of the parity tests, batch 1, k = 4, greedy, 32-id prompt, 128 new
@@ -250,24 +252,35 @@ def run_q4matvec_gpu(args, ws, rank, local):
     wsb = max(mats[s][0].workspace_bytes(M) for s in SHAPES for M in MS)
     wsp = torch.empty(max(wsb, 4) // 4 + 1, device="cuda")
     cases = [(s, M) for s in SHAPES for M in MS]
+    # The device-side numbers replay CUDA graphs of the public vxc_qgemv calls, so the
+    # host's per-call launch cost (ctypes) does not hide the GPU time; e2e below keeps it.
+    gs = torch.cuda.Stream()
 
-    def step(ev=None):
-        for (s, M) in cases:
-            for i, W in enumerate(mats[s]):
-                if ev is not None:
-                    ev[(s, M)][i][0].record(stream)
-                W.gemv(xs[M].data_ptr(), M, ys[(s[0], M)].data_ptr(), wsp.data_ptr(), wsb, sp)
-                if ev is not None:
-                    ev[(s, M)][i][1].record(stream)
+    def calls(case_list, st):
+        for (s, M) in case_list:
+            for W in mats[s]:
+                W.gemv(xs[M].data_ptr(), M, ys[(s[0], M)].data_ptr(), wsp.data_ptr(), wsb, st)
 
-    for _ in range(args.warmup):
-        step()
+    def capture(case_list):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=gs):
+            calls(case_list, gs.cuda_stream)
+        return g
+
+    with torch.cuda.stream(gs):
+        for _ in range(max(args.warmup, 1)):
+            calls(cases, gs.cuda_stream)
+    torch.cuda.synchronize()
+    l0 = vxb200.lib().vxc_launch_count()
+    g_step = capture(cases)
+    launches_per_step = vxb200.lib().vxc_launch_count() - l0
+    g_case = {c: capture([c]) for c in cases}
+    with torch.cuda.stream(gs):
+        for _ in range(max(args.warmup, 3)):
+            g_step.replay()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    # per-call events (one pair per GEMV) for the roofline of the kernel
-    evs = [{c: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                for _ in mats[c[0]]] for c in cases} for _ in range(args.steps)]
     clk = ClockSampler(local)
     clk.start()
     torch.cuda.synchronize()
@@ -275,29 +288,39 @@ def run_q4matvec_gpu(args, ws, rank, local):
         dist.barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    l0 = vxb200.lib().vxc_launch_count()
-    t0.record(stream)
-    for k in range(args.steps):
-        step(evs[k])
-    t1.record(stream)
+    with torch.cuda.stream(gs):
+        t0.record()
+        for k in range(args.steps):
+            g_step.replay()
+        t1.record()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    n_launch = vxb200.lib().vxc_launch_count() - l0
+    n_launch = launches_per_step * args.steps
     clocks = clk.stop()
     ms_total = t0.elapsed_time(t1)
+    # per case: its calls alone, replayed 3 times (one GEMV and, for split-K shapes, its reduction per call)
     per_case = {}
     kern_ms, kern_bytes, kern_wbytes, kern_launches = 0.0, 0, 0, 0
     for c in cases:
         (R, K), M = c
-        tms = [evs[k][c][i][0].elapsed_time(evs[k][c][i][1]) for k in range(args.steps) for i in range(len(mats[c[0]]))]
-        avg = sum(tms) / len(tms)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(gs):
+            g_case[c].replay()
+            e0.record()
+            for _ in range(3):
+                g_case[c].replay()
+            e1.record()
+        torch.cuda.synchronize()
+        n = 3 * len(mats[c[0]])
+        avg = e0.elapsed_time(e1) / n
         b = q4_bytes(R, K, M)
         per_case[f"{R}x{K}_M{M}"] = round(b / (avg * 1e-3) / 1e9, 1)
-        kern_ms += sum(tms)
-        kern_bytes += b * len(tms)
-        kern_wbytes += R * (K // 32) * 18 * len(tms)
-        kern_launches += len(tms)
+        kern_ms += avg * n
+        kern_bytes += b * n
+        kern_wbytes += R * (K // 32) * 18 * n
+        kern_launches += n
+    del g_step, g_case
     step_bytes = sum(q4_bytes(s[0], s[1], M) * len(mats[s]) for (s, M) in cases)
     # e2e through the C-ABI with host buffers: pinned x in, y out, each call
     hx = {M: torch.randn(M, 4096).pin_memory() for M in MS}
@@ -730,10 +753,14 @@ def main_q4matvec(args, ws, rank, threads):
            "per_case_gbs": r["per_case"],
            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(achieved / peak, 4),
-                        "traffic": int(TRAFFIC_Q4_PER_WEIGHT_BYTE * r["kern_wbytes"] / r["kern_launches"]),
-                        "traffic_note": "per GEMV launch: mean weight bytes x the ncu-measured 1.033 DRAM ratio",
+                        "traffic": int(0.5 * (TRAFFIC_Q4_PER_WEIGHT_BYTE + TRAFFIC_Q4_SKINNY_PER_WEIGHT_BYTE)
+                                       * r["kern_wbytes"] / r["kern_launches"]),
+                        "traffic_note": "per GEMV call: mean weight bytes x the ncu-measured DRAM ratio, averaged "
+                                        "over the cases' two kernels (CUDA-core M <= 2: 1.004; tensor-core M >= 5: "
+                                        "1.033)",
                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                        "kernel": "vxc_qgemv, per-call CUDA events"},
+                        "kernel": "vxc_qgemv calls (GEMV + split-K reduction where the shape has one), "
+                                  "CUDA-graph replay per case"},
            "cpu_baseline": cpu,
            "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": r["h2d"],
                    "d2h_bytes_per_step": r["d2h"]},
@@ -757,6 +784,10 @@ TRAFFIC_ATTN_PER_KV_BYTE = 0.99
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum --clock-control none \
 #       -k regex:k_qgemv_mma -s 0 -c 4 python bench.py --workload q4matvec --steps 1 --warmup 0 --no-cpu
 TRAFFIC_Q4_PER_WEIGHT_BYTE = 9.745e6 / 9437184
+# The CUDA-core GEMV (M <= 2), 4096x4096 Q4_0 M = 1: 9,471,488 DRAM bytes read, 0 written per launch (1.004x):
+#   ncu --set full --clock-control none -k regex:k_qgemv_skinny -s 2 -c 1 python bench.py --workload q4matvec \
+#       --steps 1 --warmup 0 --no-cpu
+TRAFFIC_Q4_SKINNY_PER_WEIGHT_BYTE = 9471488 / 9437184
 
 
 SPEC70_METRIC = "accepted tok/s (70B-shape Q4_0 tensor-parallel spec decode)"
