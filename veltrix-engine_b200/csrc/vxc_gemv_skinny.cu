@@ -10,12 +10,14 @@
 // fp32; only the summation order differs from the reference.
 //
 // Work split.  The work is cut into units of 32 rows x one K-slice of bps
-// blocks (bps a multiple of SK_WARPS); a persistent CTA of SK_WARPS warps
-// takes units blockIdx.x, blockIdx.x + gridDim.x, ..., and within a unit warp
-// w takes the slice's blocks w, w + SK_WARPS, ...  Each warp streams its
-// blocks through its own ring of shared-memory slots with cp.async (the
-// unit's 32 rows of one record, one contiguous span, plus their 32 scales),
-// so all but one slot stay in flight per warp across unit boundaries.  The
+// blocks (bps a multiple of SK_WARPS * SK_BPS); a persistent CTA of SK_WARPS
+// warps takes units blockIdx.x, blockIdx.x + gridDim.x, ..., and within a
+// unit warp w takes the pairs of consecutive blocks 2w, 2w + 2 SK_WARPS, ...
+// Each warp streams its block pairs through its own ring of shared-memory
+// slots with cp.async (per block the unit's 32 rows of one record, one
+// contiguous span, plus their 32 scales), so all but one slot stay in flight
+// per warp across unit boundaries; two blocks per step halve the per-element
+// cost of the ring and cursor bookkeeping.  The
 // first copies are issued before griddepcontrol.wait: the weights do not
 // depend on the kernel that produces x.  Lane l covers rows rr, rr + 8,
 // rr + 16, rr + 24 of the unit (rr = l / 4) and the element group g = l % 4
@@ -40,6 +42,7 @@
 #include "vxc_internal.h"
 
 #include <stdio.h>
+#include <atomic>
 
 #define SK_WARPS 8
 
@@ -102,31 +105,40 @@ __device__ __forceinline__ void sk_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void sk_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Rows per lane and rows of a unit.
+// Rows per lane, rows of a unit, blocks per pipeline step.
 #define SK_RPL 4
 #define SK_UROWS (8 * SK_RPL)
+#define SK_BPS 2
 
-// Ring slot of one warp: the quants of a unit's rows in one record, then their scales.
-template <int QT>
+// CTAs per SM the kernel is built for (registers).
+template <int MAXM>
+struct SkOcc {
+    static constexpr int CTAS = 4;
+};
+
+// Ring slot of one warp: SK_BPS consecutive blocks, each the quants of the
+// unit's rows in one record followed by their scales.
+template <int QT, int MAXM>
 struct SkSlot {
     static constexpr int QB = QT == 2 ? 16 : 32;
     static constexpr int QBYTES = SK_UROWS * QB;
-    static constexpr int BYTES = QBYTES + SK_UROWS * 2;   // 576 or 1088, multiples of 16
-    static constexpr int STAGES = 45056 / (SK_WARPS * BYTES) < 8 ? 45056 / (SK_WARPS * BYTES) : 8;
+    static constexpr int BLK = QBYTES + SK_UROWS * 2;   // 576 or 1088, multiples of 16
+    static constexpr int BYTES = SK_BPS * BLK;
+    static constexpr int BUDGET = 225 * 1024 / SkOcc<MAXM>::CTAS - 2048 - SK_WARPS * SK_UROWS * MAXM * 4;
+    static constexpr int STAGES = BUDGET / (SK_WARPS * BYTES) < 8 ? BUDGET / (SK_WARPS * BYTES) : 8;
+    static constexpr size_t SMEM = (size_t)SK_WARPS * STAGES * BYTES + (size_t)SK_WARPS * SK_UROWS * MAXM * 4;
 };
 
-#define SK_CTAS 4   // CTAs per SM the kernel is built for (registers)
-
 template <int QT, int MAXM>
-__global__ void __launch_bounds__(SK_WARPS * 32, SK_CTAS)
+__global__ void __launch_bounds__(SK_WARPS * 32, SkOcc<MAXM>::CTAS)
     k_qgemv_skinny(const uint8_t *__restrict__ qs, int R, int nblk, float wscale, const float *__restrict__ x,
                    int ldx, int M, float *__restrict__ out, int bps, int ks) {
-    using Sl = SkSlot<QT>;
+    using Sl = SkSlot<QT, MAXM>;
     constexpr int RPL = SK_RPL, ROWS = SK_UROWS;
     constexpr int QB = Sl::QB, SLOT = Sl::BYTES, S = Sl::STAGES;
     constexpr int REC = VXC_TILE_ROWS * QB + 256;
     constexpr int NW = QT == 2 ? 1 : 2;
-    static_assert(S >= 2, "ring too small");
+    static_assert(S >= 3, "ring too small");
     static_assert(MAXM <= VXC_SKINNY_MAX_M, "activation rows held in registers");
     extern __shared__ __align__(16) uint8_t sk_smem[];     // [SK_WARPS][S][SLOT], then red
     float *red = reinterpret_cast<float *>(sk_smem + SK_WARPS * S * SLOT);   // [SK_WARPS][ROWS * MAXM]
@@ -134,10 +146,11 @@ __global__ void __launch_bounds__(SK_WARPS * 32, SK_CTAS)
     const int G = (R + ROWS - 1) / ROWS;
     const int n_units = G * ks;
     const int my_units = (int)blockIdx.x < n_units ? (n_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int nbw = bps / SK_WARPS;   // steps per unit
+    const int nbw = bps / (SK_WARPS * SK_BPS);   // steps per unit
     uint8_t *ring = sk_smem + (size_t)w * S * SLOT;
     const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
-    // cursor over this warp's steps: unit (uu-th of this CTA), step kb in it, block b
+    // cursor over this warp's steps: unit (uu-th of this CTA), step kb in it,
+    // first block b of the step
     struct Cur {
         int uu, kb, b, rg, sl;
     };
@@ -145,7 +158,7 @@ __global__ void __launch_bounds__(SK_WARPS * 32, SK_CTAS)
         const int u = (int)blockIdx.x + c.uu * (int)gridDim.x;
         c.rg = u / ks;
         c.sl = u - c.rg * ks;
-        c.b = c.sl * bps + w;
+        c.b = c.sl * bps + w * SK_BPS;
         c.kb = 0;
     };
     auto advance = [&](Cur &c) {
@@ -153,7 +166,7 @@ __global__ void __launch_bounds__(SK_WARPS * 32, SK_CTAS)
             c.uu++;
             unit_start(c);
         } else {
-            c.b += SK_WARPS;
+            c.b += SK_WARPS * SK_BPS;
         }
     };
     Cur ic, cc;
@@ -162,17 +175,25 @@ __global__ void __launch_bounds__(SK_WARPS * 32, SK_CTAS)
     unit_start(cc);
     int islot = 0, cslot = 0;
     auto issue = [&]() {
-        if (ic.uu < my_units && ic.b < nblk) {
+        if (ic.uu < my_units) {
             const int r0 = ic.rg * ROWS;
-            const uint8_t *rec = qs + ((size_t)(r0 / VXC_TILE_ROWS) * nblk + ic.b) * REC;
+            const uint8_t *rec0 = qs + ((size_t)(r0 / VXC_TILE_ROWS) * nblk + ic.b) * REC;
             const int tr0 = r0 % VXC_TILE_ROWS;
             const uint32_t dst = ring_s + islot * SLOT;
 #pragma unroll
-            for (int c = lane; c < Sl::QBYTES / 16; c += 32) sk_cp16(dst + 16 * c, rec + tr0 * QB + 16 * c);
-            if (lane < ROWS * 2 / 16) sk_cp16(dst + Sl::QBYTES + 16 * lane, rec + VXC_TILE_ROWS * QB + tr0 * 2 + 16 * lane);
+            for (int k = 0; k < SK_BPS; k++)
+                if (ic.b + k < nblk) {
+                    const uint8_t *rec = rec0 + (size_t)k * REC;
+#pragma unroll
+                    for (int c = lane; c < Sl::QBYTES / 16; c += 32)
+                        sk_cp16(dst + k * Sl::BLK + 16 * c, rec + tr0 * QB + 16 * c);
+                    if (lane < ROWS * 2 / 16)
+                        sk_cp16(dst + k * Sl::BLK + Sl::QBYTES + 16 * lane,
+                                rec + VXC_TILE_ROWS * QB + tr0 * 2 + 16 * lane);
+                }
+            advance(ic);
         }
         sk_commit();   // one group per step, empty or not, so the waits below count steps
-        if (ic.uu < my_units) advance(ic);
         islot = islot + 1 == S ? 0 : islot + 1;
     };
     // packed accumulators (even / odd element halves) for every M: one
@@ -194,37 +215,41 @@ __global__ void __launch_bounds__(SK_WARPS * 32, SK_CTAS)
         issue();
         sk_wait<S - 1>();
         __syncwarp();
-        if (cc.b < nblk) {
-            const uint8_t *slot = ring + cslot * SLOT;
-            const uint16_t *sc = reinterpret_cast<const uint16_t *>(slot + Sl::QBYTES);
-            const float *xb = x + (size_t)cc.b * 32 + g * 8;
-            auto rowq = [&](int i, uint32_t (&q)[NW]) {
-                if constexpr (QT == 2) {
-                    q[0] = reinterpret_cast<const uint32_t *>(slot + (rr + 8 * i) * QB)[g];
-                } else {
-                    const uint2 u2 = reinterpret_cast<const uint2 *>(slot + (rr + 8 * i) * QB)[g];
-                    q[0] = u2.x;
-                    q[NW - 1] = u2.y;
-                }
-            };
-            // every activation row of the block in registers, rows outer
-            float4 xr[MAXM][2];
 #pragma unroll
-            for (int m = 0; m < MAXM; m++)
-                if (m < M) {
-                    xr[m][0] = __ldg(reinterpret_cast<const float4 *>(xb + (size_t)m * ldx));
-                    xr[m][1] = __ldg(reinterpret_cast<const float4 *>(xb + (size_t)m * ldx) + 1);
-                }
-#pragma unroll
-            for (int i = 0; i < RPL; i++) {
-                uint32_t q[NW];
-                rowq(i, q);
-                float2 f[4];
-                sk_dequant<QT>(q, f);
-                const float d = vxc_h2f(sc[rr + 8 * i]);
+        for (int k = 0; k < SK_BPS; k++) {
+            const int b = cc.b + k;
+            if (b < nblk) {
+                const uint8_t *blk = ring + cslot * SLOT + k * Sl::BLK;
+                const uint16_t *sc = reinterpret_cast<const uint16_t *>(blk + Sl::QBYTES);
+                const float *xb = x + (size_t)b * 32 + g * 8;
+                auto rowq = [&](int i, uint32_t (&q)[NW]) {
+                    if constexpr (QT == 2) {
+                        q[0] = reinterpret_cast<const uint32_t *>(blk + (rr + 8 * i) * QB)[g];
+                    } else {
+                        const uint2 u2 = reinterpret_cast<const uint2 *>(blk + (rr + 8 * i) * QB)[g];
+                        q[0] = u2.x;
+                        q[NW - 1] = u2.y;
+                    }
+                };
+                // every activation row of the block in registers, rows outer
+                float4 xr[MAXM][2];
 #pragma unroll
                 for (int m = 0; m < MAXM; m++)
-                    if (m < M) accum(acc[i][m], d, sk_dot8(f, xr[m][0], xr[m][1]));
+                    if (m < M) {
+                        xr[m][0] = __ldg(reinterpret_cast<const float4 *>(xb + (size_t)m * ldx));
+                        xr[m][1] = __ldg(reinterpret_cast<const float4 *>(xb + (size_t)m * ldx) + 1);
+                    }
+#pragma unroll
+                for (int i = 0; i < RPL; i++) {
+                    uint32_t q[NW];
+                    rowq(i, q);
+                    float2 f[4];
+                    sk_dequant<QT>(q, f);
+                    const float d = vxc_h2f(sc[rr + 8 * i]);
+#pragma unroll
+                    for (int m = 0; m < MAXM; m++)
+                        if (m < M) accum(acc[i][m], d, sk_dot8(f, xr[m][0], xr[m][1]));
+                }
             }
         }
         __syncwarp();   // every lane has read the slot before a later step refills it
@@ -269,19 +294,22 @@ static int sk_sms() {
     return sms;
 }
 
+#define SK_CTAS_SPLIT 4   // CTAs per SM assumed when choosing K-slices (the same for every M)
+
 // K-slices: the number of slices ks (bps blocks each, a multiple of
-// SK_WARPS, at least 4 per warp when the matrix is sliced) whose units
-// spread most evenly over the persistent CTAs, from the shape alone.
+// SK_WARPS * SK_BPS, at least 2 steps per warp when the matrix is sliced)
+// whose units spread most evenly over the persistent CTAs, from the shape alone.
 static void sk_split(const vxc_qmat *w, int *ks_out, int *bps_out) {
-    const long slots = (long)sk_sms() * SK_CTAS;
+    const int q = SK_WARPS * SK_BPS;
+    const long slots = (long)sk_sms() * SK_CTAS_SPLIT;
     const long G = (w->rows + SK_UROWS - 1) / SK_UROWS;
-    int best_ks = 1, best_bps = (w->nblk + SK_WARPS - 1) / SK_WARPS * SK_WARPS;
+    int best_ks = 1, best_bps = (w->nblk + q - 1) / q * q;
     double best = -1.0;
     for (int ks = 1; ks <= 16; ks++) {
-        const int bps = ((w->nblk + ks - 1) / ks + SK_WARPS - 1) / SK_WARPS * SK_WARPS;
+        const int bps = ((w->nblk + ks - 1) / ks + q - 1) / q * q;
         const int k = (w->nblk + bps - 1) / bps;
         if (k != ks) continue;
-        if (ks > 1 && bps < 4 * SK_WARPS) break;
+        if (ks > 1 && bps < 2 * q) break;
         const long units = G * k, rounds = (units + slots - 1) / slots;
         const double eff = (double)units / (double)(rounds * slots);
         if (eff > best + 0.02) {   // a clearly better spread; otherwise fewer slices
@@ -307,23 +335,33 @@ int vxc_skinny_slices(const vxc_qmat *w) {
 template <int QT, int MAXM>
 static cudaError_t sk_launch(const vxc_qmat *w, const float *x, int ldx, int M, float *out, int ks, int bps,
                              cudaStream_t st) {
-    using Sl = SkSlot<QT>;
+    using Sl = SkSlot<QT, MAXM>;
+    // the shared-memory limit is a per-kernel, per-device attribute
+    static std::atomic<uint64_t> attr_set{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t)1 << dev : 0;
+    if (!bit || !(attr_set.load(std::memory_order_acquire) & bit)) {
+        e = cudaFuncSetAttribute(k_qgemv_skinny<QT, MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sl::SMEM);
+        if (e != cudaSuccess) return e;
+        if (bit) attr_set.fetch_or(bit, std::memory_order_acq_rel);
+    }
     const long units = (long)((w->rows + SK_UROWS - 1) / SK_UROWS) * ks;
-    const long slots = (long)sk_sms() * SK_CTAS;
+    const long slots = (long)sk_sms() * SkOcc<MAXM>::CTAS;
     const unsigned grid = (unsigned)(units < slots ? units : slots);
-    const size_t smem = (size_t)SK_WARPS * Sl::STAGES * Sl::BYTES + (size_t)SK_WARPS * SK_UROWS * MAXM * 4;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(SK_WARPS * 32);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = Sl::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // may start while the producer of x drains
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_qgemv_skinny<QT, MAXM>, w->qs, w->rows, w->nblk, w->wscale, x,
-                                             ldx, M, out, bps, ks);
+    e = cudaLaunchKernelEx(&cfg, k_qgemv_skinny<QT, MAXM>, w->qs, w->rows, w->nblk, w->wscale, x, ldx, M, out, bps,
+                           ks);
     vxc_count_launches(1);
     return e;
 }

@@ -60,9 +60,12 @@ size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
 // 1 <= M <= VXC_SKINNY_MAX_M, x rows of ldx floats (16-byte aligned).
 // Writes partials [ks][M][R] (the result itself when ks == 1), ks =
 // vxc_skinny_slices(w), which depends on the shape only.  Up to 2 rows it is
-// faster than the tensor-core kernel on every measured shape (HBM-bound
-// streaming); from 5 rows on the tensor cores win (M FMAs per weight).
+// faster than the tensor-core kernel on every measured shape; from 5 rows on
+// the tensor cores win (measured up to 2.2x: M FMAs per weight on the CUDA
+// cores).
+#ifndef VXC_SKINNY_MAX_M
 #define VXC_SKINNY_MAX_M 2
+#endif
 int vxc_skinny_ok(const vxc_qmat *w, int M);
 int vxc_skinny_slices(const vxc_qmat *w);
 int vxc_skinny_run(const vxc_qmat *w, const float *x, int ldx, int M, float *out, cudaStream_t st);
