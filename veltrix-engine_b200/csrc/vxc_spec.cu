@@ -104,12 +104,12 @@ __device__ __forceinline__ void slice_pass(const float *__restrict__ row, int a,
     }
 }
 
-// The same over two rows at once (twice the loads in flight): fa(v, ra[v])
-// and fb(v, rb[v]).
+// The same over two rows at once (twice the loads in flight; a 32000-wide
+// row's slice is four steps, all unrolled): fa(v, ra[v]) and fb(v, rb[v]).
 template <class F, class G>
 __device__ __forceinline__ void slice_pass2(const float *__restrict__ ra, const float *__restrict__ rb, int a, int b,
                                             bool vec, F fa, G fb) {
-#pragma unroll 2
+#pragma unroll 4
     for (int v = a + 4 * (int)threadIdx.x; v < b; v += 4 * CL_THREADS) {
         const float4 x = ld_quad(ra, v, b, vec), y = ld_quad(rb, v, b, vec);
         fa(v, x.x);
