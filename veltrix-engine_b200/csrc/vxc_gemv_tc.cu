@@ -92,8 +92,11 @@ template <int QT, int NT>
 struct GmCfg {
     static constexpr int QB = QT == 2 ? 16 : 32;
     static constexpr int REC = 128 * QB + 256;
-    static constexpr int KB = NT >= 3 ? 2 : GM_KB_SMALL_N;
-    static constexpr int IG = NT == 1 ? (KB == 4 ? 4 : 2) : NT == 4 ? 1 : 2;
+    // above 32 rows one MMA issuer per converter group, so that TMEM holds
+    // 4-block A buffers: half the commits and barrier rounds per weight block
+    // of 2-block stages with two issuers (measured ~10% faster at 40 and 64 rows)
+    static constexpr int KB = NT >= 3 ? 4 : GM_KB_SMALL_N;
+    static constexpr int IG = NT == 1 ? (KB == 4 ? 4 : 2) : NT >= 3 ? 1 : 2;
     static constexpr int STAGE = KB * REC;
     static constexpr int RS = (QT == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / KB;
     static_assert(2 * KB * 32 + 2 * IG * 32 * NT <= 512, "TMEM budget");
@@ -458,7 +461,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static int gm_kb(int nt) { return nt >= 3 ? 2 : GM_KB_SMALL_N; }
+static int gm_kb(int nt) { return nt >= 3 ? 4 : GM_KB_SMALL_N; }
 static int gm_stage(int qt, int nt) { return gm_kb(nt) * (128 * (qt == 2 ? 16 : 32) + 256); }
 static int gm_rs(int qt, int nt) { return (qt == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / gm_kb(nt); }
 
