@@ -88,17 +88,25 @@
                             // product): 3N instead of 4N accumulator columns of tensor work per K step;
                             // measured 0-3% faster on B200 (the kernel is issue-bound), parity unchanged
 #endif
+__host__ __device__ constexpr int gm_kb_of(int qt, int nt) {
+    return nt == 1 ? (qt == 8 ? 6 : GM_KB_SMALL_N) : nt == 2 ? GM_KB_SMALL_N : nt == 3 ? 5 : 4;
+}
+
 template <int QT, int NT>
 struct GmCfg {
     static constexpr int QB = QT == 2 ? 16 : 32;
     static constexpr int REC = 128 * QB + 256;
-    // above 32 rows one MMA issuer per converter group, so that TMEM holds
-    // 4-block A buffers: half the commits and barrier rounds per weight block
-    // of 2-block stages with two issuers (measured ~10% faster at 40 and 64 rows)
-    static constexpr int KB = NT >= 3 ? 4 : GM_KB_SMALL_N;
+    // Blocks per stage and MMA issuers per converter group, as measured best on
+    // B200 within the TMEM budget below: larger stages mean fewer commits and
+    // barrier rounds per weight block, more issuers more MMAs in flight.  Above
+    // 32 rows one issuer per group (stages of 5 blocks at N = 48, 4 at N = 64:
+    // 10-15% faster than 2-block stages with two issuers); up to 16 rows, Q8_0
+    // (the draft's matrices) 6-block stages with two issuers (5-11% faster than
+    // 4 blocks with four), Q4_0 4 blocks with four.
+    static constexpr int KB = gm_kb_of(QT, NT);
     static constexpr int IG = NT == 1 ? (KB == 4 ? 4 : 2) : NT >= 3 ? 1 : 2;
     static constexpr int STAGE = KB * REC;
-    static constexpr int RS = (QT == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / KB;
+    static constexpr int RS = (QT == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / KB / 2 * 2;   // even
     static_assert(2 * KB * 32 + 2 * IG * 32 * NT <= 512, "TMEM budget");
 };
 
@@ -461,9 +469,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_qgemv_mma(const GmArgs a) {
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-static int gm_kb(int nt) { return nt >= 3 ? 4 : GM_KB_SMALL_N; }
-static int gm_stage(int qt, int nt) { return gm_kb(nt) * (128 * (qt == 2 ? 16 : 32) + 256); }
-static int gm_rs(int qt, int nt) { return (qt == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / gm_kb(nt); }
+static int gm_stage(int qt, int nt) { return gm_kb_of(qt, nt) * (128 * (qt == 2 ? 16 : 32) + 256); }
+static int gm_rs(int qt, int nt) {
+    return (qt == 2 ? GM_RING_BLOCKS : GM_RING_BLOCKS * 2 / 3) / gm_kb_of(qt, nt) / 2 * 2;
+}
 
 static size_t gm_smem(int qt, int nt, int nbs) {
     return (size_t)nbs * 128 * 16 * nt + (size_t)gm_rs(qt, nt) * gm_stage(qt, nt);
@@ -473,7 +482,7 @@ static size_t gm_smem(int qt, int nt, int nbs) {
 // partial-sum traffic (served mostly from L2).
 bool vxc_gemv_plan(const vxc_qmat *w, int M, VxcGemvPlan *p) {
     if (!w || M < 1 || M > 64) return false;
-    const int nt = (M + 15) / 16, N = 16 * nt, KB = gm_kb(nt);
+    const int nt = (M + 15) / 16, N = 16 * nt, KB = gm_kb_of(w->type, nt);
     const long avail = GM_SMEM_DYN - (long)gm_rs(w->type, nt) * gm_stage(w->type, nt);
     int nbs_max = (int)(avail / (128L * N));
     if (nbs_max > GM_MAXG * KB) nbs_max = GM_MAXG * KB;
