@@ -675,8 +675,11 @@ struct vxc_spec {
     SpecDev D;
     float *dlog;       // [k][S][V]
     float *vlog;       // [S][k+1][V]
-    int *prefill_meta; // per prompt chunk: sequence slot, first position
+    int *prefill_meta; // per prompt-pass call: the groups' sequence slots, then their first positions
     int prefill_cap;   // ints in prefill_meta
+    int *prefill_tok;  // the prompt-pass calls' token rows, one call after another
+    size_t prefill_tok_cap;
+    int prefill_g;     // sequences per prompt-pass call (full 64-row chunks)
     cudaStream_t st;
     cudaStream_t st2;  // the draft's prompt pass runs here, beside the target's
     cudaGraph_t graph;
@@ -709,9 +712,12 @@ extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int 
     e->k = k;
     e->max_ctx = max_ctx;
     e->V = tc.n_vocab;
-    int trows = n_seq * (k + 1) > 64 ? n_seq * (k + 1) : 64;
-    int drows = 2 * n_seq > 64 ? 2 * n_seq : 64;
+    // the prompt pass runs the full 64-row chunks of up to 8 sequences per call
+    e->prefill_g = n_seq < 8 ? n_seq : 8;
+    int trows = n_seq * (k + 1) > 64 * e->prefill_g ? n_seq * (k + 1) : 64 * e->prefill_g;
+    int drows = 2 * n_seq > 64 * e->prefill_g ? 2 * n_seq : 64 * e->prefill_g;
     e->prefill_cap = 2 * 2 * n_seq * ((max_ctx + 63) / 64);
+    e->prefill_tok_cap = (size_t)2 * n_seq * max_ctx;
     if ((rc = vxc_seqs_create(target, n_seq, max_ctx, trows, &e->ts)) ||
         (rc = vxc_seqs_create(draft, n_seq, max_ctx, drows, &e->ds))) {
         vxc_spec_destroy(e);
@@ -748,6 +754,7 @@ extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int 
     DALLOC(e->dlog, (size_t)k * S * e->V * sizeof(float));
     DALLOC(e->vlog, (size_t)S * (k + 1) * e->V * sizeof(float));
     DALLOC(e->prefill_meta, (size_t)e->prefill_cap * sizeof(int));
+    DALLOC(e->prefill_tok, e->prefill_tok_cap * sizeof(int));
 #undef DALLOC
     if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking);
     if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->st2, cudaStreamNonBlocking);
@@ -775,7 +782,7 @@ extern "C" void vxc_spec_destroy(vxc_spec *e) {
     SpecDev &D = e->D;
     void *ptrs[] = {D.c, D.L, D.gen, D.done, D.seq_id, D.slot, D.out, D.tok0, D.pos0, D.lrow0, D.dpos, D.dtok,
                     D.vtok, D.vpos, D.vrows, D.dseq, D.apos, D.n_acc, D.next, D.ctr, D.n_done, e->dlog, e->vlog,
-                    e->prefill_meta};
+                    e->prefill_meta, e->prefill_tok};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     if (e->h_ndone) cudaFreeHost(e->h_ndone);
@@ -899,24 +906,51 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     }
     cudaEvent_t ev[4];
     for (int i = 0; i < 4; i++) cudaEventCreate(&ev[i]);
-    // ---- prompt pass: target rows 0..L-2, draft rows 0..L-3, in chunks of 64 rows
-    // read straight from the committed tokens; the draft's chunks run on st2
-    // beside the target's, with no host round trip between chunks ----
+    // ---- prompt pass: target rows 0..L-2, draft rows 0..L-3.  The full 64-row
+    // chunks of up to prefill_g sequences go through one forward call (one
+    // group per sequence: every 64-row GEMV chunk is one sequence's chunk, as
+    // in a call of its own, so the arithmetic is the same); each sequence's
+    // last, shorter chunk is a call of its own.  Token rows and group tables
+    // are uploaded once; the draft's calls run on st2 beside the target's,
+    // with no host round trip between calls ----
     cudaEventRecord(ev[0], st);
     {
-        std::vector<int> meta;
-        std::vector<int> which_of, len_of;
-        for (int which = 0; which < 2; which++)
-            for (int sq = 0; sq < S; sq++) {
-                const int n = prompt_len[sq] - (which == 0 ? 1 : 2);
-                for (int done = 0; done < n; done += 64) {
-                    meta.push_back(sq);
-                    meta.push_back(done);
-                    which_of.push_back(which);
-                    len_of.push_back(n - done < 64 ? n - done : 64);
+        struct Call {
+            int which, m0, G, T;
+            size_t t0;
+        };
+        std::vector<int> meta, tok;
+        std::vector<Call> calls;
+        std::vector<size_t> off(S + 1, 0);
+        for (int sq = 0; sq < S; sq++) off[sq + 1] = off[sq] + (size_t)prompt_len[sq];
+        for (int which = 0; which < 2; which++) {
+            auto rows_of = [&](int sq) { return prompt_len[sq] - (which == 0 ? 1 : 2); };
+            for (int ci = 0;; ci++) {
+                std::vector<int> seqs;
+                for (int sq = 0; sq < S; sq++)
+                    if (rows_of(sq) >= 64 * (ci + 1)) seqs.push_back(sq);
+                if (seqs.empty()) break;
+                for (size_t b = 0; b < seqs.size(); b += e->prefill_g) {
+                    const int G = (int)(seqs.size() - b < (size_t)e->prefill_g ? seqs.size() - b : e->prefill_g);
+                    calls.push_back({which, (int)meta.size(), G, 64, tok.size()});
+                    for (int g = 0; g < G; g++) meta.push_back(seqs[b + g]);
+                    for (int g = 0; g < G; g++) meta.push_back(64 * ci);
+                    for (int g = 0; g < G; g++)
+                        tok.insert(tok.end(), prompts + off[seqs[b + g]] + 64 * ci,
+                                   prompts + off[seqs[b + g]] + 64 * ci + 64);
                 }
             }
-        if ((int)meta.size() > e->prefill_cap) {
+            for (int sq = 0; sq < S; sq++) {
+                const int n = rows_of(sq), r = n > 0 ? n % 64 : 0;
+                if (r == 0) continue;
+                const int p = n - r;
+                calls.push_back({which, (int)meta.size(), 1, r, tok.size()});
+                meta.push_back(sq);
+                meta.push_back(p);
+                tok.insert(tok.end(), prompts + off[sq] + p, prompts + off[sq] + p + r);
+            }
+        }
+        if ((int)meta.size() > e->prefill_cap || tok.size() > e->prefill_tok_cap) {
             vxc_set_error("vxc_spec_generate: prompt chunks exceed the engine's context");
             return -4;
         }
@@ -925,14 +959,16 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
         cudaEventCreateWithFlags(&join, cudaEventDisableTiming);
         if (!meta.empty())
             err = cudaMemcpyAsync(e->prefill_meta, meta.data(), meta.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (err == cudaSuccess && !tok.empty())
+            err = cudaMemcpyAsync(e->prefill_tok, tok.data(), tok.size() * sizeof(int), cudaMemcpyHostToDevice, st);
         cudaEventRecord(up, st);
         cudaStreamWaitEvent(e->st2, up, 0);
         int rc = 0;
-        for (size_t i = 0; i < which_of.size() && rc == 0 && err == cudaSuccess; i++) {
-            const int sq = meta[2 * i], done = meta[2 * i + 1];
-            const bool tgt = which_of[i] == 0;
-            rc = vxc_forward(tgt ? e->ts : e->ds, D.c + (size_t)sq * D.cap + done, e->prefill_meta + 2 * i,
-                             e->prefill_meta + 2 * i + 1, 1, len_of[i], NULL, 0, NULL, tgt ? st : e->st2);
+        for (size_t i = 0; i < calls.size() && rc == 0 && err == cudaSuccess; i++) {
+            const Call &cl = calls[i];
+            const bool tgt = cl.which == 0;
+            rc = vxc_forward(tgt ? e->ts : e->ds, e->prefill_tok + cl.t0, e->prefill_meta + cl.m0,
+                             e->prefill_meta + cl.m0 + cl.G, cl.G, cl.T, NULL, 0, NULL, tgt ? st : e->st2);
         }
         cudaEventRecord(join, e->st2);
         cudaStreamWaitEvent(st, join, 0);
