@@ -32,6 +32,9 @@
 #include "vxc_internal.h"
 
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <atomic>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -78,6 +81,7 @@ struct vxc_seqs {
     float *xf;               // [VXC_SKINNY_MAX_M][K] fp32 rows for the CUDA-core GEMV of 1-2 rows
     float *attn_part;
     int attn_sl, attn_splits;
+    uint64_t tmk[16], tmv[16];   // CUtensorMap of the K and V caches as [rows][hd] (copied to an aligned local per launch)
     float *ar;               // [max_rows][E] all-reduced projection output (tensor parallel)
     float *lg_local, *lg_all;   // local logits [rows][Vl], gathered [world][rows][Vl]
 };
@@ -85,7 +89,6 @@ struct vxc_seqs {
 // queries per attention CTA: 8 when a kv head has <= 8 queries (verify rows x
 // heads per kv head), else 16; the predicated query loops then carry little waste
 #define ATTN_QC_MAX 16
-#define ATTN_T 32       // key positions per smem tile
 #ifndef ATTN_SL_MIN
 #define ATTN_SL_MIN 64  // shortest context split
 #endif
@@ -221,70 +224,83 @@ __global__ void k_rope_kv(Part qkv, int T, const int *__restrict__ d_slot, const
 // share the kv head (GQA mapping kv_h = h*KH/H, src/model.c:303), so each K/V
 // byte of the split is read from HBM once for all of them.
 //
-// The cache is head-major ([slot][kv head][pos][hd]), so the split's K (and
-// V) rows are one contiguous span.  Tiles of ATTN_T positions stream through
-// an ATTN_NS-stage cp.async ring: the K tiles, then the V tiles of the split.
-// In shared memory the 16-byte chunk c of tile row p sits at c ^ (p & 7), so
-// both access patterns are free of bank conflicts:
-//   scores  lane = position, loop over chunks (q chunk is a broadcast),
-//   P.V     lane = chunk of the output row, loop over positions.
-// Per query the CTA writes its split's record [m, l, -, -, o[hd]] (16-byte
-// aligned): max m, sum l of exp(s - m) and o = sum exp(s - m) v;
-// k_combine_image merges the splits.
+// The cache is head-major ([layer][slot][kv head][pos][hd]), so a split's K
+// (and V) rows are consecutive rows of one 2-D tensor map [rows][hd].  Tiles
+// of ATTN_T rows arrive by TMA (issued by thread 0) in an ATTN_NS-stage ring,
+// the K tiles then the V tiles of the split, as hd/32 boxes of 32 floats x
+// ATTN_T rows with the 128-byte swizzle (16-byte chunk c of row r stored at
+// c ^ (r & 7)), which keeps both access patterns free of bank conflicts.
+// Each of the 4 warps owns a quarter of the head dim (QW 16-byte chunks):
+//  - scores: lane = position; the warp's partial dot product of every query
+//    over its chunks, in order; the softmax pass adds the four partials in
+//    warp order, scales, applies the causal mask and forms max and sum of
+//    exp(s - max) of the split (one warp per query);
+//  - P.V: lane = (row r of each group of RPW rows, chunk of the warp's
+//    quarter); rows in order per lane, then the RPW row sums in order.
+// So no tile is read twice from shared memory, the warps carry equal work,
+// and each warp writes its own chunks of the split's record
+// [m, l, -, -, o[hd]] (16-byte aligned) per query: max m, sum l of
+// exp(s - m) and o = sum exp(s - m) v.  k_combine_image merges the splits.
+// Every wait is bounded: on a timeout the error word gets
+// VXC_DERR_TIMEOUT_TMA, the threads keep the CTA's barriers without
+// computing, and thread 0 drains the copies in flight.
+// Up to 8 queries per kv head the kernel is instantiated for exactly that
+// many (no predicated query slots); beyond, in chunks of 16.
+#define ATTN_T 32    // cache rows per ring stage
 #ifndef ATTN_NS
-#define ATTN_NS 2
+#define ATTN_NS 2    // ring stages
 #endif
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                 "l"(src)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+// float4 index of chunk c of row r in a ring stage: [hd/32 boxes][ATTN_T rows][8 chunks, swizzled]
+__device__ __forceinline__ int attn_chunk(int r, int c) { return (c >> 3) * (ATTN_T * 8) + r * 8 + ((c & 7) ^ (r & 7)); }
 
 template <int HD, int QC>
-__global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qbuf, int T, const int *__restrict__ d_slot,
-                                                    const int *__restrict__ d_pos, int H, int KH,
-                                                    const float *__restrict__ kc, const float *__restrict__ vc,
-                                                    int n_slots, int max_ctx, int SL, int nqc,
-                                                    float *__restrict__ part) {
-    constexpr int NC = HD / 4;                  // float4 chunks per row
-    constexpr int QPW = 32 / NC;                // query slots per warp in P.V
-    constexpr int QT1 = QC / 4;            // queries per thread in the score pass
-    constexpr int QT3 = (QC + 4 * QPW - 1) / (4 * QPW);   // ... in the P.V pass
-    static_assert(HD % 32 == 0 && HD <= 128, "head dim");
-    extern __shared__ __align__(16) float sm[];
-    float4 *ring = reinterpret_cast<float4 *>(sm);                 // [NS][T][NC]
-    float4 *qs = ring + ATTN_NS * ATTN_T * NC;                      // [QC][NC]
-    float *sc = reinterpret_cast<float *>(qs + QC * NC);       // [QC][SL+1]
+__global__ void __launch_bounds__(128, 4)
+    k_attn(const float *__restrict__ qbuf, int T, const int *__restrict__ d_slot, const int *__restrict__ d_pos,
+           int H, int KH, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, int row0,
+           int n_slots, int max_ctx, int SL, int nqc, float *__restrict__ part, unsigned int *err) {
+    constexpr int NC = HD / 4;                // float4 chunks per row
+    constexpr int QW = NC / 4;                // chunks per warp
+    constexpr int RPW = 32 / QW;              // V rows per warp instruction in P.V
+    constexpr int SEG = HD / 32;              // boxes per tile
+    constexpr int STG = ATTN_T * HD;          // floats per ring stage
+    static_assert(HD % 32 == 0 && HD <= 128 && ATTN_T == 32, "head dim / tile");
+    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    // the swizzled boxes need 1024-byte aligned stages
+    float *ring = reinterpret_cast<float *>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);   // [ATTN_NS][STG]
+    float *qs = ring + ATTN_NS * STG;          // [QC][HD]
+    float *sc = qs + QC * HD;                  // [4][QC][SL + 1] partial scores; exp values in [0]
+    __shared__ __align__(8) uint64_t full[ATTN_NS], qbar;
     __shared__ float qmax[QC], qsum[QC];
-    const int G = H / KH, nq = T * G;
+    __shared__ int abort_flag;
+    const int G = H / KH, nq = T * G, E = H * HD;
     const int bx = blockIdx.x;
     const int qc = bx % nqc;
     const int kvh = (bx / nqc) % KH;
     const int g = bx / (nqc * KH);
     const int split = blockIdx.y, nsplit = gridDim.y;
     const int q0 = qc * QC;
-    const int nql = min(QC, nq - q0);
-    const int E = H * HD;
+    // up to 8 queries per kv head the host picks QC = that count, so the query loops are exact
+    const int nql = QC <= 8 ? QC : min(QC, nq - q0);
+    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < ATTN_NS; s++) mbar_init(smem_u32(&full[s]), 1);
+        mbar_init(smem_u32(&qbar), 1);
+        abort_flag = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
     pdl_trigger();
     pdl_wait();
     const int slot = d_slot[g];
     const int base = d_pos[g];
     const int p0 = split * SL;
-    // exclusive end: causal bound of the group, clamped to the cache (k_rope_kv
-    // flags positions outside it; a bad slot reads nothing)
+    // exclusive end: causal bound of the group, clamped to the cache
+    // (k_rope_kv flags positions outside it; a bad slot reads nothing)
     const int pend = (slot < 0 || slot >= n_slots || base < 0) ? 0 : min(min(p0 + SL, base + T), max_ctx);
-    const int tid = threadIdx.x, w = tid >> 5, lane = tid & 31;
-    const int SLP = SL + 1;
     auto part_ptr = [&](int q) {
         return part + ((((size_t)g * KH + kvh) * (size_t)nq + q) * nsplit + split) * (HD + 4);
     };
-    if (nql <= 0) return;
     if (p0 >= pend) {
         if (tid < nql) {
             float *pp = part_ptr(q0 + tid);
@@ -294,128 +310,162 @@ __global__ void __launch_bounds__(128) k_attn_split(const float *__restrict__ qb
         return;
     }
     const int npos = pend - p0;
-    const int ntile = (npos + ATTN_T - 1) / ATTN_T;
-    const size_t head_off = ((size_t)slot * KH + kvh) * (size_t)max_ctx * HD;
-    const float4 *ksrc = reinterpret_cast<const float4 *>(kc + head_off + (size_t)p0 * HD);
-    const float4 *vsrc = reinterpret_cast<const float4 *>(vc + head_off + (size_t)p0 * HD);
-    // tile i < ntile: K tile i; i >= ntile: V tile i - ntile
+    const int nt = (npos + ATTN_T - 1) / ATTN_T;
+    const int hrow = row0 + (slot * KH + kvh) * max_ctx + p0;   // tensor-map row of the split's first position
+    volatile int *abortp = &abort_flag;
+    // tile i < nt: K tile i; i >= nt: V tile i - nt (whole boxes land: rows past the split are
+    // read, or zero past the tensor)
     auto issue = [&](int i) {
-        if (i < 2 * ntile) {
-            const int t = i < ntile ? i : i - ntile;
-            const float4 *src = (i < ntile ? ksrc : vsrc) + (size_t)t * ATTN_T * NC;
-            const int rows = min(ATTN_T, npos - t * ATTN_T);
-            float4 *dst = ring + (i % ATTN_NS) * ATTN_T * NC;
-            for (int e = tid; e < rows * NC; e += 128) {
-                const int p = e / NC, c = e % NC;
-                cp_async16(dst + p * NC + (c ^ (p & 7)), src + e);
-            }
+        if (i < 2 * nt) {
+            const int s = i % ATTN_NS, t = i < nt ? i : i - nt;
+            const uint32_t bar = smem_u32(&full[s]);
+            mbar_expect_tx(bar, (uint32_t)(STG * 4));
+#pragma unroll
+            for (int b = 0; b < SEG; b++)
+                tma_load_2d(smem_u32(ring + (size_t)s * STG + b * (ATTN_T * 32)), i < nt ? &tmk : &tmv, b * 32,
+                            hrow + t * ATTN_T, bar);
         }
-        cp_async_commit();
     };
-    for (int i = 0; i < ATTN_NS - 1; i++) issue(i);
-    // queries of this CTA (post-RoPE rows of qkv)
-    for (int e = tid; e < nql * NC; e += 128) {
-        const int ql = e / NC, c = e % NC;
-        const int q = q0 + ql, t = q / G, h = kvh * G + q % G;
-        qs[ql * NC + c] = reinterpret_cast<const float4 *>(qbuf + (size_t)(g * T + t) * E + (size_t)h * HD)[c];
+    if (tid == 0) {
+        mbar_expect_tx(smem_u32(&qbar), (uint32_t)(nql * HD * 4));
+        for (int ql = 0; ql < nql; ql++) {
+            const int q = q0 + ql, t = q / G, h = kvh * G + q % G;
+            bulk_g2s(smem_u32(qs + (size_t)ql * HD), qbuf + (size_t)(g * T + t) * E + (size_t)h * HD, HD * 4,
+                     smem_u32(&qbar));
+        }
+        for (int i = 0; i < ATTN_NS - 1; i++) issue(i);
     }
     const float scale = 1.0f / sqrtf((float)HD);
-    float4 acc[QT3];
+    const int SLP = SL + 1;
+    const int r = lane / QW, cc = w * QW + lane % QW;   // P.V lane: row r, chunk cc
+    const float4 *qv4 = reinterpret_cast<const float4 *>(qs);
+    float4 acc[QC];
 #pragma unroll
-    for (int j = 0; j < QT3; j++) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int qslot = lane / NC, cc = lane % NC;
-    for (int i = 0; i < 2 * ntile; i++) {
-        issue(i + ATTN_NS - 1);
-        cp_async_wait<ATTN_NS - 1>();
-        __syncthreads();
-        if (i == ntile) {
-            // softmax pieces of the split: one warp per query
+    for (int jq = 0; jq < QC; jq++) acc[jq] = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool ok = mbar_wait(smem_u32(&qbar), 0, abortp, err, VXC_DERR_TIMEOUT_TMA);
+    int issued = ATTN_NS - 1;
+    for (int i = 0; i < 2 * nt; i++) {
+        if (tid == 0 && !*abortp) {
+            // the stage of tile i - 1 was released by the barrier that ended its iteration
+            fence_proxy_async();
+            issue(i + ATTN_NS - 1);
+            issued = i + ATTN_NS;
+        }
+        const int s = i % ATTN_NS;
+        if (ok) ok = mbar_wait(smem_u32(&full[s]), (i / ATTN_NS) & 1, abortp, err, VXC_DERR_TIMEOUT_TMA);
+        const float4 *tile = reinterpret_cast<const float4 *>(ring + (size_t)s * STG);
+        if (i == nt && ok) {
+            // scores = ((w0 + w1) + w2) + w3, scaled and masked; softmax pieces of the split
             for (int ql = w; ql < nql; ql += 4) {
                 float *row = sc + ql * SLP;
+                const int lim = base + (q0 + ql) / G - p0;   // last visible position of the split
                 float mx = -INFINITY;
-                for (int p = lane; p < npos; p += 32) mx = fmaxf(mx, row[p]);
+                for (int p = lane; p < npos; p += 32) {
+                    float v = row[p];
+#pragma unroll
+                    for (int ww = 1; ww < 4; ww++) v += row[(size_t)ww * QC * SLP + p];
+                    v = p <= lim ? v * scale : -INFINITY;
+                    row[p] = v;
+                    mx = fmaxf(mx, v);
+                }
                 mx = warp_max(mx);
                 float su = 0.0f;
                 for (int p = lane; p < npos; p += 32) {
-                    const float s = row[p];
-                    const float e = (s == -INFINITY) ? 0.0f : expf(s - mx);
+                    const float v = row[p];
+                    const float e = (v == -INFINITY) ? 0.0f : expf(v - mx);
                     row[p] = e;
                     su += e;
                 }
                 su = warp_sum(su);
-                if (lane == 0) { qmax[ql] = mx; qsum[ql] = su; }
+                if (lane == 0) {
+                    qmax[ql] = mx;
+                    qsum[ql] = su;
+                }
             }
-            __syncthreads();
         }
-        const float4 *tile = ring + (i % ATTN_NS) * ATTN_T * NC;
-        if (i < ntile) {
-            // scores: lane = position p of the tile
-            const int t0 = i * ATTN_T, p = lane;
-            const int pos = p0 + t0 + p;
-            float a[QT1];
+        if (i == nt) __syncthreads();
+        if (ok && i < nt) {
+            // partial scores over this warp's chunks: lane = position p of the tile
+            const int pl = i * ATTN_T + lane;
+            if (pl < npos) {
+                float a[QC];
 #pragma unroll
-            for (int j = 0; j < QT1; j++) a[j] = 0.0f;
-            if (t0 + p < npos) {
-                const float4 *krow = tile + p * NC;
-#pragma unroll 4
-                for (int c = 0; c < NC; c++) {
-                    const float4 kv = krow[c ^ (p & 7)];
+                for (int jq = 0; jq < QC; jq++) a[jq] = 0.0f;
+#pragma unroll 2
+                for (int ci = 0; ci < QW; ci++) {
+                    const int c = w * QW + ci;
+                    const float4 kv = tile[attn_chunk(lane, c)];
 #pragma unroll
-                    for (int j = 0; j < QT1; j++) {
-                        const int ql = w + 4 * j;
-                        if (ql < nql) {
-                            const float4 qv = qs[ql * NC + c];
-                            float s = a[j];
-                            s = fmaf(qv.x, kv.x, s);
-                            s = fmaf(qv.y, kv.y, s);
-                            s = fmaf(qv.z, kv.z, s);
-                            s = fmaf(qv.w, kv.w, s);
-                            a[j] = s;
+                    for (int jq = 0; jq < QC; jq++) {
+                        if (jq < nql) {
+                            const float4 qv = qv4[jq * NC + c];
+                            float x = a[jq];
+                            x = fmaf(qv.x, kv.x, x);
+                            x = fmaf(qv.y, kv.y, x);
+                            x = fmaf(qv.z, kv.z, x);
+                            x = fmaf(qv.w, kv.w, x);
+                            a[jq] = x;
                         }
                     }
                 }
+                float *dst = sc + (size_t)w * QC * SLP + pl;
 #pragma unroll
-                for (int j = 0; j < QT1; j++) {
-                    const int ql = w + 4 * j;
-                    if (ql < nql) {
-                        const int tq = (q0 + ql) / G;
-                        sc[ql * SLP + t0 + p] = (pos <= base + tq) ? a[j] * scale : -INFINITY;
-                    }
-                }
+                for (int jq = 0; jq < QC; jq++)
+                    if (jq < nql) dst[jq * SLP] = a[jq];
             }
-        } else if (qslot < QPW) {
-            // P.V: lane = (query slot, output chunk cc)
-            const int t0 = (i - ntile) * ATTN_T;
-            const int nt = min(ATTN_T, npos - t0);
-            for (int p = 0; p < nt; p++) {
-                const float4 vv = tile[p * NC + (cc ^ (p & 7))];
+        } else if (ok && r < RPW) {
+            // P.V over this warp's chunks: lane = (row r, chunk cc)
+            const int t0 = (i - nt) * ATTN_T, ntp = min(ATTN_T, npos - t0);
+            const float *et = sc + t0;
+#pragma unroll 4
+            for (int p = r; p < ntp; p += RPW) {
+                const float4 vv = tile[attn_chunk(p, cc)];
 #pragma unroll
-                for (int j = 0; j < QT3; j++) {
-                    const int ql = (w * QPW + qslot) + j * 4 * QPW;
-                    if (ql < nql) {
-                        const float e = sc[ql * SLP + t0 + p];
-                        acc[j].x = fmaf(e, vv.x, acc[j].x);
-                        acc[j].y = fmaf(e, vv.y, acc[j].y);
-                        acc[j].z = fmaf(e, vv.z, acc[j].z);
-                        acc[j].w = fmaf(e, vv.w, acc[j].w);
+                for (int jq = 0; jq < QC; jq++) {
+                    if (jq < nql) {
+                        const float e = et[jq * SLP + p];
+                        acc[jq].x = fmaf(e, vv.x, acc[jq].x);
+                        acc[jq].y = fmaf(e, vv.y, acc[jq].y);
+                        acc[jq].z = fmaf(e, vv.z, acc[jq].z);
+                        acc[jq].w = fmaf(e, vv.w, acc[jq].w);
                     }
                 }
             }
         }
         __syncthreads();
     }
-    cp_async_wait<0>();
-    if (qslot < QPW) {
+    // row sums in order (lanes of row 0 collect rows 1..RPW-1), then this warp's chunks of the records
+    float4 tot[QC];
 #pragma unroll
-        for (int j = 0; j < QT3; j++) {
-            const int ql = (w * QPW + qslot) + j * 4 * QPW;
-            if (ql < nql) reinterpret_cast<float4 *>(part_ptr(q0 + ql) + 4)[cc] = acc[j];
+    for (int jq = 0; jq < QC; jq++) tot[jq] = acc[jq];
+#pragma unroll
+    for (int k = 1; k < RPW; k++)
+#pragma unroll
+        for (int jq = 0; jq < QC; jq++) {
+            tot[jq].x += __shfl_down_sync(0xffffffffu, acc[jq].x, k * QW);
+            tot[jq].y += __shfl_down_sync(0xffffffffu, acc[jq].y, k * QW);
+            tot[jq].z += __shfl_down_sync(0xffffffffu, acc[jq].z, k * QW);
+            tot[jq].w += __shfl_down_sync(0xffffffffu, acc[jq].w, k * QW);
         }
-    }
-    if (tid < nql) {
-        float *pp = part_ptr(q0 + tid);
-        pp[0] = qmax[tid];
-        pp[1] = qsum[tid];
+    if (!*abortp) {
+        if (r == 0) {
+#pragma unroll
+            for (int jq = 0; jq < QC; jq++)
+                if (jq < nql) reinterpret_cast<float4 *>(part_ptr(q0 + jq) + 4)[cc] = tot[jq];
+        }
+        if (tid < nql) {
+            float *pp = part_ptr(q0 + tid);
+            pp[0] = qmax[tid];
+            pp[1] = qsum[tid];
+        }
+    } else if (tid == 0) {
+        // drain (bounded): the query rows and the tiles issued but not waited for
+        for (int k = max(0, issued - ATTN_NS); k < issued && k < 2 * nt; k++) {
+            const uint64_t t0 = vxc_globaltimer();
+            while (!mbar_try(smem_u32(&full[k % ATTN_NS]), (k / ATTN_NS) & 1) && vxc_globaltimer() - t0 < 100000000ull) {}
+        }
+        const uint64_t t0 = vxc_globaltimer();
+        while (!mbar_try(smem_u32(&qbar), 0) && vxc_globaltimer() - t0 < 100000000ull) {}
     }
 }
 
@@ -1115,28 +1165,76 @@ extern "C" size_t vxc_net_weight_bytes(const vxc_net *n) { return n ? n->weight_
 // ---------------------------------------------------------------------------
 // host: sequences + forward
 // ---------------------------------------------------------------------------
+// Dynamic shared memory of k_attn: ring, query rows, four partial-score rows
+// per query (+ alignment of the ring).
 static size_t attn_smem(int hd, int SL, int qc) {
-    return ((size_t)ATTN_NS * ATTN_T * hd + (size_t)qc * hd + (size_t)qc * (SL + 1)) * sizeof(float);
+    return ((size_t)ATTN_NS * ATTN_T * hd + (size_t)qc * hd + (size_t)4 * qc * (SL + 1)) * sizeof(float) + 1024;
 }
 
-static int attn_qc(int nq) { return nq <= 8 ? 8 : 16; }
+static int attn_qc(int nq) { return nq <= 8 ? nq : 16; }
 
-typedef void (*attn_kernel_t)(const float *, int, const int *, const int *, int, int, const float *, const float *,
-                              int, int, int, int, float *);
+// cuTensorMapEncodeTiled through the runtime's driver entry point table (the
+// library links only the static runtime, not libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+    static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> fn{nullptr};
+    PFN_cuTensorMapEncodeTiled_v12000 f = fn.load(std::memory_order_acquire);
+    if (!f) {
+        void *p = NULL;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !p) {
+            cudaGetLastError();
+            return NULL;
+        }
+        f = (PFN_cuTensorMapEncodeTiled_v12000)p;
+        fn.store(f, std::memory_order_release);
+    }
+    return f;
+}
 
+// A KV cache as the 2-D tensor [rows][hd] of fp32, read in boxes of 32 floats
+// x ATTN_T rows with the 128-byte swizzle (k_attn's ring layout).
+static bool attn_tmap(float *base, int hd, uint64_t rows, uint64_t out[16]) {
+    PFN_cuTensorMapEncodeTiled_v12000 f = tmap_encode_fn();
+    if (!f) return false;
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {(cuuint64_t)hd, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)hd * sizeof(float)};
+    const cuuint32_t box[2] = {32, ATTN_T};
+    const cuuint32_t es[2] = {1, 1};
+    if (f(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return false;
+    static_assert(sizeof(CUtensorMap) == 16 * sizeof(uint64_t), "tensor map size");
+    memcpy(out, &m, sizeof m);
+    return true;
+}
+
+typedef void (*attn_kernel_t)(const float *, int, const int *, const int *, int, int, const CUtensorMap,
+                              const CUtensorMap, int, int, int, int, int, float *, unsigned int *);
+
+#define ATTN_K_QC(HD)                  \
+    case 1: return k_attn<HD, 1>;      \
+    case 2: return k_attn<HD, 2>;      \
+    case 3: return k_attn<HD, 3>;      \
+    case 4: return k_attn<HD, 4>;      \
+    case 5: return k_attn<HD, 5>;      \
+    case 6: return k_attn<HD, 6>;      \
+    case 7: return k_attn<HD, 7>;      \
+    case 8: return k_attn<HD, 8>;      \
+    case 16: return k_attn<HD, 16>;    \
+    default: return NULL;
 static attn_kernel_t attn_kernel(int hd, int qc) {
-    switch (hd * 100 + qc) {
-        case 3208: return k_attn_split<32, 8>;
-        case 3216: return k_attn_split<32, 16>;
-        case 6408: return k_attn_split<64, 8>;
-        case 6416: return k_attn_split<64, 16>;
-        case 9608: return k_attn_split<96, 8>;
-        case 9616: return k_attn_split<96, 16>;
-        case 12808: return k_attn_split<128, 8>;
-        case 12816: return k_attn_split<128, 16>;
+    switch (hd) {
+        case 32: switch (qc) { ATTN_K_QC(32) }
+        case 64: switch (qc) { ATTN_K_QC(64) }
+        case 96: switch (qc) { ATTN_K_QC(96) }
+        case 128: switch (qc) { ATTN_K_QC(128) }
         default: return NULL;
     }
 }
+#undef ATTN_K_QC
 
 // Kernel launch with programmatic dependent launch: the kernel may start while
 // its predecessor finishes; every kernel of the forward calls
@@ -1275,6 +1373,14 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
         vxc_seqs_destroy(s);
         return -4;
     }
+    // the attention kernel addresses cache rows with 32-bit tensor-map coordinates
+    const uint64_t kv_rows = (uint64_t)c.n_layers * n_slots * net->KHl * max_ctx;
+    if (e == cudaSuccess && (kv_rows + ATTN_T >= (1ull << 31) || !attn_tmap(s->k, hd, kv_rows, s->tmk) ||
+                             !attn_tmap(s->v, hd, kv_rows, s->tmv))) {
+        vxc_set_error("vxc_seqs_create: no tensor map for a KV cache of %llu rows of %d", (unsigned long long)kv_rows, hd);
+        vxc_seqs_destroy(s);
+        return -4;
+    }
     if (ROW_CL > 8) {   // clusters above the portable size of 8 must be allowed per kernel
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_norm_image, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_swiglu_image, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -1283,12 +1389,14 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     // The attribute is per kernel (and device), shared by every sequence set of
     // the process, so it is only ever raised: a set with a shorter context
     // must not shrink it under one with a longer context.
-    for (int qc = 8; qc <= 16 && e == cudaSuccess; qc += 8) {
+    static const int attn_qcs[] = {1, 2, 3, 4, 5, 6, 7, 8, 16};
+    for (int qc : attn_qcs) {
+        if (e != cudaSuccess) break;
         cudaFuncAttributes fa;
+        const int need = (int)attn_smem(hd, SL, qc);
         e = cudaFuncGetAttributes(&fa, attn_kernel(hd, qc));
-        if (e == cudaSuccess && fa.maxDynamicSharedSizeBytes < (int)attn_smem(hd, SL, qc))
-            e = cudaFuncSetAttribute(attn_kernel(hd, qc), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)attn_smem(hd, SL, qc));
+        if (e == cudaSuccess && fa.maxDynamicSharedSizeBytes < need)
+            e = cudaFuncSetAttribute(attn_kernel(hd, qc), cudaFuncAttributeMaxDynamicSharedMemorySize, need);
     }
     if (e != cudaSuccess) {
         vxc_set_error("vxc_seqs_create: %s", cudaGetErrorString(e));
@@ -1464,6 +1572,9 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     prof_end(0, pe, st);
     const int G = H / KH, nq = T * G, qcn = attn_qc(nq), nqc = (nq + qcn - 1) / qcn;
     const size_t asm_bytes = attn_smem(hd, s->attn_sl, qcn);
+    CUtensorMap tmk, tmv;
+    memcpy(&tmk, s->tmk, sizeof tmk);
+    memcpy(&tmv, s->tmv, sizeof tmv);
     // local columns of a row kernel's CTA (norm: E / ROW_CL, SwiGLU: F / ROW_CL, merge: heads x hd)
     auto cols8 = [](int K) { return ((K + ROW_CL - 1) / ROW_CL + 7) / 8 * 8; };
     size_t row_smem = (size_t)cols8(E);
@@ -1495,8 +1606,8 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
         e = launch_pdl(attn_kernel(hd, qcn), dim3(n_groups * KH * nqc, s->attn_splits), dim3(128), asm_bytes, st,
-                       (const float *)s->qbuf, T, d_slot, d_pos, H, KH, (const float *)kc, (const float *)vc,
-                       s->n_slots, s->max_ctx, s->attn_sl, nqc, s->attn_part);
+                       (const float *)s->qbuf, T, d_slot, d_pos, H, KH, tmk, tmv, l * s->n_slots * KH * s->max_ctx,
+                       s->n_slots, s->max_ctx, s->attn_sl, nqc, s->attn_part, err);
         prof_end(4, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
