@@ -92,6 +92,9 @@ struct vxc_seqs {
 #ifndef ATTN_SL_MIN
 #define ATTN_SL_MIN 64  // shortest context split
 #endif
+#ifndef ATTN_MAX_SPLITS
+#define ATTN_MAX_SPLITS 16   // context splits at most (before the minimum split lengths below)
+#endif
 #ifndef ATTN_SL_MIN_WIDE
 #define ATTN_SL_MIN_WIDE 128  // ... for head dims >= 128 (fewer splits to merge)
 #endif
@@ -254,8 +257,10 @@ __global__ void k_rope_kv(Part qkv, int T, const int *__restrict__ d_slot, const
 // float4 index of chunk c of row r in a ring stage: [hd/32 boxes][ATTN_T rows][8 chunks, swizzled]
 __device__ __forceinline__ int attn_chunk(int r, int c) { return (c >> 3) * (ATTN_T * 8) + r * 8 + ((c & 7) ^ (r & 7)); }
 
+// 4 CTAs per SM (128 registers) up to 8 queries; the 16-query form (prompt chunks) keeps 3 so
+// that its 16 accumulators per lane stay in registers
 template <int HD, int QC>
-__global__ void __launch_bounds__(128, 4)
+__global__ void __launch_bounds__(128, QC > 8 ? 3 : 4)
     k_attn(const float *__restrict__ qbuf, int T, const int *__restrict__ d_slot, const int *__restrict__ d_pos,
            int H, int KH, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, int row0,
            int n_slots, int max_ctx, int SL, int nqc, float *__restrict__ part, unsigned int *err) {
@@ -264,8 +269,9 @@ __global__ void __launch_bounds__(128, 4)
     constexpr int RPW = 32 / QW;              // V rows per warp instruction in P.V
     constexpr int SEG = HD / 32;              // boxes per tile
     constexpr int STG = ATTN_T * HD;          // floats per ring stage
+    constexpr int PVU = QC > 8 ? 2 : 4;       // P.V rows in flight per lane
     static_assert(HD % 32 == 0 && HD <= 128 && ATTN_T == 32, "head dim / tile");
-    extern __shared__ __align__(1024) unsigned char sm_raw[];
+    extern __shared__ __align__(16) unsigned char sm_raw[];
     // the swizzled boxes need 1024-byte aligned stages
     float *ring = reinterpret_cast<float *>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);   // [ATTN_NS][STG]
     float *qs = ring + ATTN_NS * STG;          // [QC][HD]
@@ -417,7 +423,7 @@ __global__ void __launch_bounds__(128, 4)
             // P.V over this warp's chunks: lane = (row r, chunk cc)
             const int t0 = (i - nt) * ATTN_T, ntp = min(ATTN_T, npos - t0);
             const float *et = sc + t0;
-#pragma unroll 4
+#pragma unroll(PVU)
             for (int p = r; p < ntp; p += RPW) {
                 const float4 vv = tile[attn_chunk(p, cc)];
 #pragma unroll
@@ -434,24 +440,25 @@ __global__ void __launch_bounds__(128, 4)
         }
         __syncthreads();
     }
-    // row sums in order (lanes of row 0 collect rows 1..RPW-1), then this warp's chunks of the records
-    float4 tot[QC];
+    // row sums in order (lanes of row 0 collect rows 1..RPW-1; every lane reads the others' sums
+    // before it overwrites its own), then this warp's chunks of the records
 #pragma unroll
-    for (int jq = 0; jq < QC; jq++) tot[jq] = acc[jq];
+    for (int jq = 0; jq < QC; jq++) {
+        float4 t = acc[jq];
 #pragma unroll
-    for (int k = 1; k < RPW; k++)
-#pragma unroll
-        for (int jq = 0; jq < QC; jq++) {
-            tot[jq].x += __shfl_down_sync(0xffffffffu, acc[jq].x, k * QW);
-            tot[jq].y += __shfl_down_sync(0xffffffffu, acc[jq].y, k * QW);
-            tot[jq].z += __shfl_down_sync(0xffffffffu, acc[jq].z, k * QW);
-            tot[jq].w += __shfl_down_sync(0xffffffffu, acc[jq].w, k * QW);
+        for (int k = 1; k < RPW; k++) {
+            t.x += __shfl_down_sync(0xffffffffu, acc[jq].x, k * QW);
+            t.y += __shfl_down_sync(0xffffffffu, acc[jq].y, k * QW);
+            t.z += __shfl_down_sync(0xffffffffu, acc[jq].z, k * QW);
+            t.w += __shfl_down_sync(0xffffffffu, acc[jq].w, k * QW);
         }
+        acc[jq] = t;
+    }
     if (!*abortp) {
         if (r == 0) {
 #pragma unroll
             for (int jq = 0; jq < QC; jq++)
-                if (jq < nql) reinterpret_cast<float4 *>(part_ptr(q0 + jq) + 4)[cc] = tot[jq];
+                if (jq < nql) reinterpret_cast<float4 *>(part_ptr(q0 + jq) + 4)[cc] = acc[jq];
         }
         if (tid < nql) {
             float *pp = part_ptr(q0 + tid);
@@ -643,11 +650,18 @@ __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__re
         const float e = (ms == -INFINITY) ? 0.0f : expf(ms - Mx);
         const float Ls = warp_sum(lane < nsplit ? e * pp[(size_t)lane * rec + 1] : 0.0f);
         const float inv = 1.0f / (Ls + 1e-10f);
+        // splits past the last one with positions hold no output; the others are read
+        // unconditionally (a select, not a branch, drops the weightless ones), so the
+        // loads of several splits are in flight together
+        const unsigned live = __ballot_sync(0xffffffffu, lane < nsplit && e != 0.0f);
+        const int ns = live ? 32 - __clz(live) : 0;
         for (int d = cpart * 32 + lane; d < hd; d += 32 * P) {
             float o = 0.0f;
-            for (int sp = 0; sp < nsplit; sp++) {
+#pragma unroll 8
+            for (int sp = 0; sp < ns; sp++) {
                 const float es = __shfl_sync(0xffffffffu, e, sp);
-                if (es != 0.0f) o += es * pp[(size_t)sp * rec + 4 + d];
+                const float v = pp[(size_t)sp * rec + 4 + d];
+                o = fmaf(es, es != 0.0f ? v : 0.0f, o);
             }
             const float val = o * inv;
             v[(h - h0) * hd + d] = val;
@@ -1330,7 +1344,7 @@ extern "C" int vxc_seqs_create(const vxc_net *net, int n_slots, int max_ctx, int
     // attention split length: at most 16 splits of >= ATTN_SL_MIN positions (whole
     // tiles).  Short splits and a 2-stage ring keep ~5 CTAs per SM resident, which
     // measured faster on B200 than deeper rings (the kernel is latency-bound per CTA).
-    int SL = (max_ctx + 15) / 16;
+    int SL = (max_ctx + ATTN_MAX_SPLITS - 1) / ATTN_MAX_SPLITS;
     SL = ((SL + ATTN_T - 1) / ATTN_T) * ATTN_T;
     const int sl_min = hd >= 128 ? ATTN_SL_MIN_WIDE : ATTN_SL_MIN;
     if (SL < sl_min) SL = sl_min;
