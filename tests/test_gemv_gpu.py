@@ -1,6 +1,7 @@
 """GPU parity: quantised GEMV against the CPU oracle, through the C-ABI.
-vxc_qgemv runs the streaming CUDA-core kernel for M <= 2 and the tcgen05
-kernel above; vxc_qgemv_simt is the plain CUDA-core cross-check.
+vxc_qgemv runs the streaming CUDA-core kernel for M <= 2, the tcgen05 GEMV
+up to 63 rows and the tcgen05 GEMM (weights converted once per 256-row
+slab) from 64 rows on; vxc_qgemv_simt is the plain CUDA-core cross-check.
 
 Tolerance: the kernels accumulate in fp32 from exact integer weights and a
 22-bit activation split (tensor-core path) or fp32 activations (CUDA-core
@@ -107,3 +108,45 @@ def test_skinny_rows_do_not_depend_on_m(cuda):
             ys.append(y.cpu().numpy())
         W.close()
         assert np.array_equal(ys[0][0], ys[1][0]), qt
+
+
+@pytest.mark.parametrize("qt,rows,cols,M", [(2, 4096, 4096, 96), (8, 2560, 2048, 300), (2, 384, 11008, 64),
+                                            (8, 300, 2048, 520), (2, 32000, 256, 65), (8, 130, 4096, 257),
+                                            (2, 1000, 1024, 1111)])
+def test_gemm_shapes(cuda, qt, rows, cols, M):
+    """The GEMM path: full and ragged 256-row slabs, a single weight tile in
+    the last pair (odd tile counts), ragged weight rows, K up to 11008."""
+    err, mx = run_case(cuda, qt, rows, cols, M, simt=False, seed=3 * rows + M)
+    assert err <= TOL * mx, (err, mx)
+
+
+def test_gemm_rows_do_not_depend_on_m(cuda):
+    """A row's GEMM result depends on that row only: the same rows give the
+    same bits whether the call has 64, 300 or 600 rows (other slabs, another
+    slab position, other rows beside them)."""
+    import vxb200
+    torch = cuda
+    rng = np.random.default_rng(33)
+    for qt, rows, cols in ((2, 4096, 4096), (8, 2560, 2048)):
+        blk = (q4_0_blocks if qt == 2 else q8_0_blocks)(rows, cols, rng)
+        W = vxb200.QMat(qt, blk, rows, cols)
+        x = torch.from_numpy(rng.standard_normal((600, cols)).astype(np.float32)).cuda()
+        ys = {}
+        for M in (64, 300, 600):
+            wsb = max(W.workspace_bytes(M), 4)
+            ws = torch.empty(wsb // 4 + 1, device="cuda")
+            y = torch.empty((M, rows), device="cuda")
+            W.gemv(x.data_ptr(), M, y.data_ptr(), ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            ys[M] = y.cpu().numpy()
+        # a call whose first row is row 100 of x: every row sits at another place in its slab
+        wsb = max(W.workspace_bytes(300), 4)
+        ws = torch.empty(wsb // 4 + 1, device="cuda")
+        y = torch.empty((300, rows), device="cuda")
+        W.gemv(x[100:400].data_ptr(), 300, y.data_ptr(), ws.data_ptr(), wsb, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        shifted = y.cpu().numpy()
+        W.close()
+        assert np.array_equal(ys[64], ys[300][:64]), qt
+        assert np.array_equal(ys[300], ys[600][:300]), qt
+        assert np.array_equal(ys[600][100:400], shifted), qt

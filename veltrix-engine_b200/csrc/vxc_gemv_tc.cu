@@ -611,8 +611,25 @@ static size_t chunk_ws_bytes(const vxc_qmat *w, int M) {
     return img_bytes(w, M) + (p.ks > 1 ? (size_t)p.ks * M * w->rows * sizeof(float) : 0);
 }
 
+// Workspace of the GEMM path (M >= VXC_GEMM_MIN_ROWS): the image in slabs,
+// then the M prescales (each 256-byte aligned), then the K-slices' partial
+// sums [ks][M][R] when ks > 1 (one slice is written to y directly).
+static size_t gemm_img_bytes(const vxc_qmat *w, int M) {
+    return (vxc_gemm_image_bytes(w->cols, M) + 255) & ~(size_t)255;
+}
+static size_t gemm_ws_bytes(const vxc_qmat *w, int M) {
+    const int ks = vxc_gemm_slices(w);
+    return gemm_img_bytes(w, M) + (((size_t)M * sizeof(float) + 255) & ~(size_t)255) +
+           (ks > 1 ? (size_t)ks * M * w->rows * sizeof(float) : 0);
+}
+
 extern "C" size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M) {
     if (!w || M <= 0 || vxc_is_kquant(w->type)) return 0;
+    if (M >= VXC_GEMM_MIN_ROWS && vxc_gemm_ok(w)) {
+        const size_t g = gemm_ws_bytes(w, M);
+        const size_t simt = vxc_qgemv_simt_ws(w, M);
+        return g > simt ? g : simt;
+    }
     const int mc = M < 64 ? M : 64;
     size_t b = chunk_ws_bytes(w, mc);
     if (M > 64 && M % 64) {
@@ -647,6 +664,28 @@ extern "C" int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, voi
         float *part = ks > 1 ? (float *)workspace : y;
         int rc = vxc_skinny_run(w, x, w->cols, M, part, st);
         if (rc == 0 && ks > 1) rc = vxc_launch_splitk_reduce(part, ks, M, w->rows, y, st);
+        return rc;
+    }
+    if (M >= VXC_GEMM_MIN_ROWS && vxc_gemm_ok(w)) {   // many rows: the tensor-core GEMM, weights read once per slab
+        const size_t ib = gemm_img_bytes(w, M), need = gemm_ws_bytes(w, M);
+        if (!workspace || need > workspace_bytes) {
+            vxc_set_error("vxc_qgemv: workspace %zu < %zu bytes", workspace_bytes, need);
+            return -4;
+        }
+        uint8_t *img = (uint8_t *)workspace;
+        float *xs = (float *)(img + ib);
+        float *part = (float *)(img + ib + (((size_t)M * sizeof(float) + 255) & ~(size_t)255));
+        const int ks = vxc_gemm_slices(w);
+        const size_t slab = (size_t)w->nblk * 128 * VXC_GEMM_SLAB;
+        for (int m0 = 0; m0 < M; m0 += VXC_GEMM_SLAB) {
+            const int ms = M - m0 < VXC_GEMM_SLAB ? M - m0 : VXC_GEMM_SLAB;
+            const int rc = vxc_launch_act_image(x + (size_t)m0 * w->cols, ms, w->cols,
+                                                img + (size_t)(m0 / VXC_GEMM_SLAB) * slab, xs + m0, st);
+            if (rc) return rc;
+        }
+        if (ks == 1) return vxc_gemm_run(w, img, slab, xs, M, y, (size_t)64 * w->rows, 0, st);
+        int rc = vxc_gemm_run(w, img, slab, xs, M, part, (size_t)64 * w->rows, (size_t)M * w->rows, st);
+        if (rc == 0) rc = vxc_launch_splitk_reduce(part, ks, M, w->rows, y, st);
         return rc;
     }
     for (int m0 = 0; m0 < M; m0 += 64) {

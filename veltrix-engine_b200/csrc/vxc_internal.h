@@ -56,6 +56,29 @@ int vxc_gemv_run(const vxc_qmat *w, const uint8_t *img, const float *xs, int M, 
                  const VxcGemvPlan &p, cudaStream_t st, const float *x = NULL);
 size_t vxc_qgemv_simt_ws(const vxc_qmat *w, int M);
 
+// Tensor-core GEMM for many activation rows (vxc_gemm_tc.cu), Q4_0 / Q8_0.
+// The activation image is cut into slabs of VXC_GEMM_SLAB rows, slab s at
+// img + s * slab_bytes in the vxc_qmat.cuh layout with N = padded rows of
+// that slab (slab_bytes >= K/32 * 128 * VXC_GEMM_SLAB); prescales xs[M].
+// K is cut into vxc_gemm_slices(w) slices (a function of K only); slice s of
+// row m goes to out[(m >> 6) * slot + s * sst + (m & 63) * R + r] with
+// sst = sstride, or (rows of m's 64-row chunk) * R when sstride == 0 (the
+// forward's partial-sum slots).  The consumer adds the slices in order.  A
+// row's result does not depend on the other rows of the call.  Programmatic
+// dependent launch.
+#define VXC_GEMM_SLAB 256
+// Rows from which vxc_qgemv and vxc_forward use the GEMM.
+#define VXC_GEMM_MIN_ROWS 64
+int vxc_gemm_ok(const vxc_qmat *w);
+int vxc_gemm_slices(const vxc_qmat *w);
+size_t vxc_gemm_image_bytes(int K, int M);   // image of M rows in slabs of full size
+int vxc_gemm_run(const vxc_qmat *w, const uint8_t *img, size_t slab_bytes, const float *xs, int M, float *out,
+                 size_t slot, size_t sstride, cudaStream_t st);
+// vxc_forward without logits for the speculative engine's prompt pass: every
+// Q4_0 / Q8_0 matrix runs on the GEMM whatever the row count (vxc_model.cu).
+int vxc_forward_prompt(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
+                       int rows_per_group, void *stream);
+
 // CUDA-core GEMV for few activation rows (vxc_gemv_skinny.cu): Q4_0 / Q8_0,
 // 1 <= M <= VXC_SKINNY_MAX_M, x rows of ldx floats (16-byte aligned).
 // Writes partials [ks][M][R] (the result itself when ks == 1), ks =

@@ -65,7 +65,7 @@ struct vxc_net {
 
 namespace cg = cooperative_groups;
 
-#define VXC_MAX_CHUNKS 16   // row chunks of 64 per forward (max_rows <= 1024)
+#define VXC_MAX_CHUNKS 64   // row chunks of 64 per forward (max_rows <= 4096)
 
 struct vxc_seqs {
     const vxc_net *net;
@@ -73,8 +73,8 @@ struct vxc_seqs {
     float *k, *v;            // [L][slot][kv head][pos][hd]
     float *x;                // [max_rows][E] residual stream
     float *qbuf;             // [max_rows][E] rotated queries
-    uint8_t *img;            // activation images, one 64-row chunk per img_chunk bytes
-    size_t img_chunk;
+    uint8_t *img;            // activation images, one 64-row chunk per img_chunk bytes (GEMV), or
+    size_t img_chunk;        // one slab of VXC_GEMM_SLAB rows per (VXC_GEMM_SLAB / 64) * img_chunk (GEMM)
     float *xs;               // [chunks * 64] image prescales
     float *part;             // GEMV partial sums, one slot per chunk
     size_t part_slot;        // floats per chunk slot
@@ -513,12 +513,13 @@ __device__ __forceinline__ void col_range(int K, int align, int *k0, int *k1) {
     *k1 = min(K, *k0 + cw);
 }
 
-// Image columns [k0, k1) of row m (chunks of 64 rows, vxc_qmat.cuh).
+// Image columns [k0, k1) of row m (vxc_qmat.cuh layout) in chunks of 2^csh
+// rows: 64 for the GEMV, VXC_GEMM_SLAB for the GEMM (vxc_gemm_tc.cu).
 template <class F>
-__device__ __forceinline__ void image_cols(uint8_t *img, size_t chunk_bytes, int m, int M, int k0, int k1, float s,
-                                           F val) {
-    const int c = m >> 6;
-    const int N = vxc_img_rows(min(64, M - (c << 6)));
+__device__ __forceinline__ void image_cols(uint8_t *img, size_t chunk_bytes, int csh, int m, int M, int k0, int k1,
+                                           float s, F val) {
+    const int c = m >> csh, cr = 1 << csh, ml = m & (cr - 1);
+    const int N = vxc_img_rows(min(cr, M - (c << csh)));
     uint8_t *base = img + c * chunk_bytes;
     for (int ch = k0 / 8 + threadIdx.x; ch < k1 / 8; ch += blockDim.x) {
         const int b = ch >> 2, cc = ch & 3;
@@ -528,8 +529,8 @@ __device__ __forceinline__ void image_cols(uint8_t *img, size_t chunk_bytes, int
         uint4 hi, lo;
         vxc_hilo8(v, s, hi, lo);
         uint8_t *chunk = base + (size_t)(b * 4 + cc) * 2 * N * 16;
-        *reinterpret_cast<uint4 *>(chunk + (size_t)(m & 63) * 16) = hi;
-        *reinterpret_cast<uint4 *>(chunk + (size_t)(N + (m & 63)) * 16) = lo;
+        *reinterpret_cast<uint4 *>(chunk + (size_t)ml * 16) = hi;
+        *reinterpret_cast<uint4 *>(chunk + (size_t)(N + ml) * 16) = lo;
     }
 }
 
@@ -545,7 +546,7 @@ __device__ __forceinline__ void image_cols(uint8_t *img, size_t chunk_bytes, int
 __global__ void __launch_bounds__(ROW_THREADS) k_norm_image(float *__restrict__ x, Part add,
                                                               const float *__restrict__ w, int E,
                                                               const int *__restrict__ rows, int write_x, int M_out,
-                                                              uint8_t *__restrict__ img, size_t chunk_bytes,
+                                                              uint8_t *__restrict__ img, size_t chunk_bytes, int csh,
                                                               float *__restrict__ xs, float *__restrict__ xf) {
     extern __shared__ float v[];   // local columns
     __shared__ float red[32], slots[2];
@@ -580,7 +581,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_image(float *__restrict__ 
         const float s = vxc_prescale(mx);
         if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
         __syncthreads();
-        image_cols(img, chunk_bytes, m, M_out, k0, k1, s, [&](int k) { return v[k - k0]; });
+        image_cols(img, chunk_bytes, csh, m, M_out, k0, k1, s, [&](int k) { return v[k - k0]; });
     }
     cl.sync();   // peers have read this CTA's slots
 }
@@ -588,7 +589,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_norm_image(float *__restrict__ 
 // f = |silu(g)| < 0.01 ? 0 : silu(g) * u  (src/model.c:580-585, src/tensor.c:71-88, :277)
 // from the fused gate/up GEMV's partials, then the image for the down GEMV.
 __global__ void __launch_bounds__(ROW_THREADS) k_swiglu_image(Part gu, int F, int M, uint8_t *__restrict__ img,
-                                                                size_t chunk_bytes, float *__restrict__ xs,
+                                                                size_t chunk_bytes, int csh, float *__restrict__ xs,
                                                                 float *__restrict__ xf) {
     extern __shared__ float v[];
     __shared__ float red[32], slots[1];
@@ -612,7 +613,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_swiglu_image(Part gu, int F, in
         const float s = vxc_prescale(mx);
         if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
         __syncthreads();
-        image_cols(img, chunk_bytes, m, M, k0, k1, s, [&](int k) { return v[k - k0]; });
+        image_cols(img, chunk_bytes, csh, m, M, k0, k1, s, [&](int k) { return v[k - k0]; });
     }
     cl.sync();
 }
@@ -623,7 +624,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_swiglu_image(Part gu, int F, in
 // One warp per head; lane s holds split s's weight e^{m_s-M}.
 __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__restrict__ part, int T, int H, int KH,
                                                                  int hd, int nsplit, int M, uint8_t *__restrict__ img,
-                                                                 size_t chunk_bytes, float *__restrict__ xs,
+                                                                 size_t chunk_bytes, int csh, float *__restrict__ xs,
                                                                  float *__restrict__ xf) {
     extern __shared__ float v[];
     __shared__ float red[32], slots[1];
@@ -674,7 +675,7 @@ __global__ void __launch_bounds__(ROW_THREADS) k_combine_image(const float *__re
         const float s = vxc_prescale(mx);
         if (blockIdx.x == 0 && threadIdx.x == 0) xs[m] = s;
         __syncthreads();
-        image_cols(img, chunk_bytes, m, M, h0 * hd, h1 * hd, s, [&](int k) { return v[k - h0 * hd]; });
+        image_cols(img, chunk_bytes, csh, m, M, h0 * hd, h1 * hd, s, [&](int k) { return v[k - h0 * hd]; });
     }
     cl.sync();
 }
@@ -1309,6 +1310,10 @@ static size_t part_slot_floats(const vxc_net *n) {
                 if (f > best) best = f;
             }
         }
+        if (vxc_gemm_ok(w)) {   // the GEMM's K-slices of a 64-row chunk
+            const size_t f = (size_t)vxc_gemm_slices(w) * 64 * w->rows;
+            if (f > best) best = f;
+        }
         for (int m = 1; m <= VXC_SKINNY_MAX_M; m++)   // the CUDA-core GEMV of 1-2 rows
             if (vxc_skinny_ok(w, m)) {
                 const size_t f = (size_t)vxc_skinny_slices(w) * m * w->rows;
@@ -1482,16 +1487,41 @@ extern "C" int vxc_profile_read(double *ms, int n) {
 // s->xf (1-2 rows of a Q4_0 / Q8_0 matrix) rather than from the image.
 static bool skinny(const vxc_qmat *w, int M) { return vxc_skinny_ok(w, M) != 0; }
 
-// GEMV over M rows in chunks of 64 (image chunks -> partial slots), or on the
-// CUDA cores from s->xf when skinny(w, M); returns the Part view of its output.
-static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStream_t st) {
+// How a matrix multiplies M rows in a forward whose GEMM threshold is
+// gemm_min: the tensor-core GEMM (one launch for all rows, image in slabs),
+// the CUDA-core GEMV (1-2 rows, fp32 rows in s->xf), or the tensor-core GEMV
+// (64-row chunks).  The producer of the rows writes the operand that mode reads.
+enum GemvMode { GM_GEMV = 0, GM_SKINNY = 1, GM_GEMM = 2 };
+static GemvMode gemv_mode(const vxc_qmat *w, int M, int gemm_min) {
+    if (M >= gemm_min && vxc_gemm_ok(w)) return GM_GEMM;
+    return skinny(w, M) ? GM_SKINNY : GM_GEMV;
+}
+
+// GEMM over all M rows, or GEMV over M rows in chunks of 64 (image chunks ->
+// partial slots), or on the CUDA cores from s->xf; returns the Part view of
+// its output.
+static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStream_t st, int gemm_min) {
     Part p;
     p.base = s->part;
     p.slot = s->part_slot;
     p.R = w->rows;
     p.M = M;
     p.ks_full = p.ks_last = 1;
-    if (skinny(w, M)) {
+    const GemvMode mode = gemv_mode(w, M, gemm_min);
+    if (mode == GM_GEMM) {
+        const int ks = vxc_gemm_slices(w);
+        if (s->part_slot < (size_t)ks * 64 * w->rows) {
+            vxc_set_error("vxc_forward: partial slot too small");
+            return -4;
+        }
+        if (int rc = vxc_gemm_run(w, s->img, (VXC_GEMM_SLAB / 64) * s->img_chunk, s->xs, M, s->part, s->part_slot,
+                                  0, st))
+            return rc;
+        p.ks_full = p.ks_last = ks;
+        *out = p;
+        return 0;
+    }
+    if (mode == GM_SKINNY) {
         const int ks = vxc_skinny_slices(w);
         if ((size_t)ks * M * w->rows > s->part_slot) {
             vxc_set_error("vxc_forward: partial slot too small");
@@ -1532,9 +1562,10 @@ static int gemv_rows(vxc_seqs *s, const vxc_qmat *w, int M, Part *out, cudaStrea
     return 0;
 }
 
-extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
-                           int rows_per_group, const int *d_logit_rows, int n_logit_rows, float *d_logits,
-                           void *stream) {
+// The forward of vxc_forward; matrices multiply M >= gemm_min rows on the GEMM.
+static int forward_impl(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
+                        int rows_per_group, const int *d_logit_rows, int n_logit_rows, float *d_logits,
+                        void *stream, int gemm_min) {
     if (!s || !d_tokens || !d_slot || !d_pos || n_groups <= 0 || rows_per_group <= 0) {
         vxc_set_error("vxc_forward: bad arguments");
         return -4;
@@ -1600,18 +1631,32 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     prev.slot = 0;
     prev.R = prev.M = prev.ks_full = prev.ks_last = 0;
     Part pp;
+    // where a row kernel writes the operand of the GEMV/GEMM that reads it
+    struct ImgOut {
+        uint8_t *img;
+        size_t bytes;
+        int csh;
+    };
+    auto img_for = [&](const vxc_qmat *w, int rows) -> ImgOut {
+        switch (gemv_mode(w, rows, gemm_min)) {
+            case GM_GEMM: return {s->img, (VXC_GEMM_SLAB / 64) * s->img_chunk, 8};
+            case GM_SKINNY: return {NULL, s->img_chunk, 6};
+            default: return {s->img, s->img_chunk, 6};
+        }
+    };
+    static_assert(VXC_GEMM_SLAB == 256, "slab rows = 2^8");
     for (int l = 0; l < c.n_layers && e == cudaSuccess; l++) {
         const vxc_layer_dev *d = &n->layers[l];
         float *kc = s->k + (size_t)l * s->n_slots * s->max_ctx * kvd;
         float *vc = s->v + (size_t)l * s->n_slots * s->max_ctx * kvd;
         pe = prof_begin(st);
+        ImgOut io = img_for(d->wqkv, M);
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, prev,
-                               d->attn_norm, E, (const int *)NULL, 1, M, skinny(d->wqkv, M) ? NULL : s->img,
-                               s->img_chunk, s->xs, s->xf);
+                               d->attn_norm, E, (const int *)NULL, 1, M, io.img, io.bytes, io.csh, s->xs, s->xf);
         prof_end(1, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
-        if ((rc = gemv_rows(s, d->wqkv, M, &pp, st))) return rc;
+        if ((rc = gemv_rows(s, d->wqkv, M, &pp, st, gemm_min))) return rc;
         prof_end(2, pe, st);
         pe = prof_begin(st);
         e = launch_pdl(k_rope_kv, dim3(H + 2 * KH, M), dim3(((hd / 2) + 31) / 32 * 32), 0, st, pp, T, d_slot, d_pos, (const float2 *)n->rope,
@@ -1625,31 +1670,33 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         prof_end(4, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
+        io = img_for(d->wo, M);
         e = launch_pdl_cluster(k_combine_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL,
-                               (const float *)s->attn_part, T, H, KH, hd, s->attn_splits, M,
-                               skinny(d->wo, M) ? NULL : s->img, s->img_chunk, s->xs, s->xf);
+                               (const float *)s->attn_part, T, H, KH, hd, s->attn_splits, M, io.img, io.bytes,
+                               io.csh, s->xs, s->xf);
         prof_end(5, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
-        if ((rc = gemv_rows(s, d->wo, M, &pp, st))) return rc;
+        if ((rc = gemv_rows(s, d->wo, M, &pp, st, gemm_min))) return rc;
         if (n->tp && (rc = tp_sum(pp))) return rc;
         prof_end(6, pe, st);
         pe = prof_begin(st);
+        io = img_for(d->wgu, M);
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, s->x, pp,
-                               d->ffn_norm, E, (const int *)NULL, 1, M, skinny(d->wgu, M) ? NULL : s->img,
-                               s->img_chunk, s->xs, s->xf);
+                               d->ffn_norm, E, (const int *)NULL, 1, M, io.img, io.bytes, io.csh, s->xs, s->xf);
         prof_end(7, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
-        if ((rc = gemv_rows(s, d->wgu, M, &pp, st))) return rc;
+        if ((rc = gemv_rows(s, d->wgu, M, &pp, st, gemm_min))) return rc;
         prof_end(8, pe, st);
         pe = prof_begin(st);
+        io = img_for(d->wd, M);
         e = launch_pdl_cluster(k_swiglu_image, dim3(ROW_CL, M), dim3(ROW_THREADS), row_smem, st, ROW_CL, pp, F, M,
-                               skinny(d->wd, M) ? NULL : s->img, s->img_chunk, s->xs, s->xf);
+                               io.img, io.bytes, io.csh, s->xs, s->xf);
         prof_end(9, pe, st);
         if (e != cudaSuccess) break;
         pe = prof_begin(st);
-        if ((rc = gemv_rows(s, d->wd, M, &prev, st))) return rc;
+        if ((rc = gemv_rows(s, d->wd, M, &prev, st, gemm_min))) return rc;
         if (n->tp && (rc = tp_sum(prev))) return rc;
         prof_end(10, pe, st);
     }
@@ -1657,11 +1704,12 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
         pe = prof_begin(st);
         const int V = c.n_vocab;
         // last residual update fused with the final norm, for the requested rows only
+        const ImgOut lo = img_for(n->out, n_logit_rows);
         e = launch_pdl_cluster(k_norm_image, dim3(ROW_CL, n_logit_rows), dim3(ROW_THREADS), row_smem, st, ROW_CL,
-                               s->x, prev, n->out_norm, E, d_logit_rows, 0, n_logit_rows,
-                               skinny(n->out, n_logit_rows) ? NULL : s->img, s->img_chunk, s->xs, s->xf);
+                               s->x, prev, n->out_norm, E, d_logit_rows, 0, n_logit_rows, lo.img, lo.bytes, lo.csh,
+                               s->xs, s->xf);
         if (e == cudaSuccess) {
-            if ((rc = gemv_rows(s, n->out, n_logit_rows, &pp, st))) return rc;
+            if ((rc = gemv_rows(s, n->out, n_logit_rows, &pp, st, gemm_min))) return rc;
             const size_t tot = (size_t)n_logit_rows * n->Vl;
             e = launch_pdl(k_part_out, dim3(nblk(tot, 256) < 1184 ? nblk(tot, 256) : 1184), dim3(256), 0, st, pp,
                            n_logit_rows, n->tp ? s->lg_local : d_logits);
@@ -1678,6 +1726,21 @@ extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, 
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) { vxc_set_error("vxc_forward: %s", cudaGetErrorString(e)); return -3; }
     return 0;
+}
+
+extern "C" int vxc_forward(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
+                           int rows_per_group, const int *d_logit_rows, int n_logit_rows, float *d_logits,
+                           void *stream) {
+    return forward_impl(s, d_tokens, d_slot, d_pos, n_groups, rows_per_group, d_logit_rows, n_logit_rows, d_logits,
+                        stream, VXC_GEMM_MIN_ROWS);
+}
+
+// The prompt pass of the speculative engine: every Q4_0 / Q8_0 matrix runs on
+// the GEMM whatever the row count, so a prompt row's numbers do not depend on
+// how the prompts were batched (a row's GEMM result depends on that row only).
+int vxc_forward_prompt(vxc_seqs *s, const int *d_tokens, const int *d_slot, const int *d_pos, int n_groups,
+                       int rows_per_group, void *stream) {
+    return forward_impl(s, d_tokens, d_slot, d_pos, n_groups, rows_per_group, NULL, 0, NULL, stream, 1);
 }
 
 // ---------------------------------------------------------------------------

@@ -23,6 +23,8 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <algorithm>
+#include <utility>
 #include <vector>
 
 namespace cg = cooperative_groups;
@@ -379,6 +381,9 @@ extern "C" int vxc_sample_rows(const float *logits, int n_rows, int V, float tem
 // Greedy (temp <= 0) stops after 1: the first j with d_j != argmax P_j.
 // ---------------------------------------------------------------------------
 #define ACC_MAX_K 64
+// Prompt pass: rows of one sequence per forward group, and rows per forward call.
+#define PREFILL_PIECE 512
+#define PREFILL_ROWS 4096
 #define ACC_MAX_ROWS (2 * ACC_MAX_K + 1)
 
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(CL_THREADS, 4)
@@ -679,7 +684,7 @@ struct vxc_spec {
     int prefill_cap;   // ints in prefill_meta
     int *prefill_tok;  // the prompt-pass calls' token rows, one call after another
     size_t prefill_tok_cap;
-    int prefill_g;     // sequences per prompt-pass call (full 64-row chunks)
+    int prefill_rows;  // rows per prompt-pass call (pieces of up to PREFILL_PIECE rows of several sequences)
     cudaStream_t st;
     cudaStream_t st2;  // the draft's prompt pass runs here, beside the target's
     cudaGraph_t graph;
@@ -712,10 +717,15 @@ extern "C" int vxc_spec_create(const vxc_net *target, const vxc_net *draft, int 
     e->k = k;
     e->max_ctx = max_ctx;
     e->V = tc.n_vocab;
-    // the prompt pass runs the full 64-row chunks of up to 8 sequences per call
-    e->prefill_g = n_seq < 8 ? n_seq : 8;
-    int trows = n_seq * (k + 1) > 64 * e->prefill_g ? n_seq * (k + 1) : 64 * e->prefill_g;
-    int drows = 2 * n_seq > 64 * e->prefill_g ? 2 * n_seq : 64 * e->prefill_g;
+    // the prompt pass runs pieces of up to PREFILL_PIECE rows of many sequences per call, up to
+    // PREFILL_ROWS rows per call, so the GEMM reads the weights once per VXC_GEMM_SLAB rows
+    {
+        const long piece = max_ctx < PREFILL_PIECE ? max_ctx : PREFILL_PIECE;
+        const long want = (long)n_seq * piece;
+        e->prefill_rows = (int)(want < PREFILL_ROWS ? want : PREFILL_ROWS);
+    }
+    int trows = n_seq * (k + 1) > e->prefill_rows ? n_seq * (k + 1) : e->prefill_rows;
+    int drows = 2 * n_seq > e->prefill_rows ? 2 * n_seq : e->prefill_rows;
     e->prefill_cap = 2 * 2 * n_seq * ((max_ctx + 63) / 64);
     e->prefill_tok_cap = (size_t)2 * n_seq * max_ctx;
     if ((rc = vxc_seqs_create(target, n_seq, max_ctx, trows, &e->ts)) ||
@@ -906,13 +916,14 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
     }
     cudaEvent_t ev[4];
     for (int i = 0; i < 4; i++) cudaEventCreate(&ev[i]);
-    // ---- prompt pass: target rows 0..L-2, draft rows 0..L-3.  The full 64-row
-    // chunks of up to prefill_g sequences go through one forward call (one
-    // group per sequence: every 64-row GEMV chunk is one sequence's chunk, as
-    // in a call of its own, so the arithmetic is the same); each sequence's
-    // last, shorter chunk is a call of its own.  Token rows and group tables
-    // are uploaded once; the draft's calls run on st2 beside the target's,
-    // with no host round trip between calls ----
+    // ---- prompt pass: target rows 0..L-2, draft rows 0..L-3.  Each sequence's
+    // rows are cut into pieces of PREFILL_PIECE; piece i of every sequence
+    // comes after piece i-1 of all of them, and pieces of equal length go
+    // through one forward call, one group per sequence, up to prefill_rows
+    // rows.  Every matrix runs on the GEMM (vxc_forward_prompt), whose result
+    // for a row depends on that row only, so batching changes no number.
+    // Token rows and group tables are uploaded once; the draft's calls run on
+    // st2 beside the target's, with no host round trip between calls ----
     cudaEventRecord(ev[0], st);
     {
         struct Call {
@@ -926,28 +937,30 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
         for (int which = 0; which < 2; which++) {
             auto rows_of = [&](int sq) { return prompt_len[sq] - (which == 0 ? 1 : 2); };
             for (int ci = 0;; ci++) {
-                std::vector<int> seqs;
-                for (int sq = 0; sq < S; sq++)
-                    if (rows_of(sq) >= 64 * (ci + 1)) seqs.push_back(sq);
-                if (seqs.empty()) break;
-                for (size_t b = 0; b < seqs.size(); b += e->prefill_g) {
-                    const int G = (int)(seqs.size() - b < (size_t)e->prefill_g ? seqs.size() - b : e->prefill_g);
-                    calls.push_back({which, (int)meta.size(), G, 64, tok.size()});
-                    for (int g = 0; g < G; g++) meta.push_back(seqs[b + g]);
-                    for (int g = 0; g < G; g++) meta.push_back(64 * ci);
-                    for (int g = 0; g < G; g++)
-                        tok.insert(tok.end(), prompts + off[seqs[b + g]] + 64 * ci,
-                                   prompts + off[seqs[b + g]] + 64 * ci + 64);
+                // piece ci of every sequence that has one, grouped by length (ascending)
+                std::vector<std::pair<int, int>> pcs;   // (length, sequence)
+                for (int sq = 0; sq < S; sq++) {
+                    const int n = rows_of(sq) - PREFILL_PIECE * ci;
+                    if (n > 0) pcs.push_back({n < PREFILL_PIECE ? n : PREFILL_PIECE, sq});
                 }
-            }
-            for (int sq = 0; sq < S; sq++) {
-                const int n = rows_of(sq), r = n > 0 ? n % 64 : 0;
-                if (r == 0) continue;
-                const int p = n - r;
-                calls.push_back({which, (int)meta.size(), 1, r, tok.size()});
-                meta.push_back(sq);
-                meta.push_back(p);
-                tok.insert(tok.end(), prompts + off[sq] + p, prompts + off[sq] + p + r);
+                if (pcs.empty()) break;
+                std::stable_sort(pcs.begin(), pcs.end(),
+                                 [](const std::pair<int, int> &a, const std::pair<int, int> &b) { return a.first < b.first; });
+                for (size_t b = 0; b < pcs.size();) {
+                    const int T = pcs[b].first;
+                    const int gmax = e->prefill_rows / T > 0 ? e->prefill_rows / T : 1;
+                    size_t end = b;
+                    while (end < pcs.size() && pcs[end].first == T && (int)(end - b) < gmax) end++;
+                    const int G = (int)(end - b);
+                    calls.push_back({which, (int)meta.size(), G, T, tok.size()});
+                    for (size_t g = b; g < end; g++) meta.push_back(pcs[g].second);
+                    for (size_t g = b; g < end; g++) meta.push_back(PREFILL_PIECE * ci);
+                    for (size_t g = b; g < end; g++) {
+                        const int *src = prompts + off[pcs[g].second] + (size_t)PREFILL_PIECE * ci;
+                        tok.insert(tok.end(), src, src + T);
+                    }
+                    b = end;
+                }
             }
         }
         if ((int)meta.size() > e->prefill_cap || tok.size() > e->prefill_tok_cap) {
@@ -967,8 +980,8 @@ extern "C" int vxc_spec_generate(vxc_spec *e, const int *prompts, const int *pro
         for (size_t i = 0; i < calls.size() && rc == 0 && err == cudaSuccess; i++) {
             const Call &cl = calls[i];
             const bool tgt = cl.which == 0;
-            rc = vxc_forward(tgt ? e->ts : e->ds, e->prefill_tok + cl.t0, e->prefill_meta + cl.m0,
-                             e->prefill_meta + cl.m0 + cl.G, cl.G, cl.T, NULL, 0, NULL, tgt ? st : e->st2);
+            rc = vxc_forward_prompt(tgt ? e->ts : e->ds, e->prefill_tok + cl.t0, e->prefill_meta + cl.m0,
+                                    e->prefill_meta + cl.m0 + cl.G, cl.G, cl.T, tgt ? st : e->st2);
         }
         cudaEventRecord(join, e->st2);
         cudaStreamWaitEvent(st, join, 0);
