@@ -82,15 +82,19 @@ def peaks():
 
 
 def verify_mma_flops(rows, weights):
-    """Tensor-pipe work of one verify forward under the exact GEMV scheme:
-    rows go in chunks of <= 64, each padded to N = 16 * ceil(rows / 16)
-    image rows; per K16 step two MMAs (A = w_hi, A = w_lo) against the
-    2N-row stacked [x_hi; x_lo], i.e. 8 N flop per weight and chunk."""
+    """Tensor-pipe work of one forward of `rows` rows under the exact scheme.
+    Below 64 rows the GEMV pads the rows to N = 16 * ceil(rows / 16) and per
+    K16 step multiplies A = w_hi by the 2N-row stacked [x_hi; x_lo] and
+    A = w_lo by the N rows of x_hi: 6 N flop per weight.  From 64 rows the
+    GEMM takes slabs of 256 rows, each padded to N = 16 * ceil(rows / 16), with
+    three N-row MMAs per K16 step (w_hi x_hi, w_hi x_lo, w_lo x_hi): again
+    6 N flop per weight."""
+    step = 64 if rows < 64 else 256
     n = 0
-    for c0 in range(0, rows, 64):
-        c = min(64, rows - c0)
+    for c0 in range(0, rows, step):
+        c = min(step, rows - c0)
         n += 16 * ((c + 15) // 16)
-    return 8 * n * weights
+    return 6 * n * weights
 
 
 def target_weights(cfg):
@@ -225,6 +229,92 @@ def matvec_records(torch, reps=3):
             for W in mats:
                 W.close()
     return out
+
+
+# The GEMM (64+ rows): the 7B target's Q4_0 matrices at prompt-pass row counts.
+GEMM_SHAPES = [(12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008)]
+GEMM_ROWS = 4096
+
+
+def gemm_records(torch, cases=None, reps=3):
+    """The tensor-core GEMM through the public vxc_qgemv (activation image,
+    GEMM, and the ordered sum of its K-slices, as the entry point launches
+    them), per (shape, rows): microseconds per call from CUDA events around
+    `reps` back-to-back calls after two warm-up calls; algorithmic TFLOP/s
+    (2 M R K) and the exact scheme's tensor work (6 x padded rows x weights,
+    three fp16 products per weight x activation) against the measured dense
+    bf16 peak.  Every call writes K-slice partials and an output far larger
+    than L2."""
+    import vxb200
+    from qgen import q4_0_blocks
+    rng = np.random.default_rng(4321)
+    tpk, tkind = tensor_peak()
+    out = {}
+    stream = torch.cuda.current_stream()
+    for (R, K, M) in (cases or [(r, k, GEMM_ROWS) for (r, k) in GEMM_SHAPES]):
+        W = vxb200.QMat(2, q4_0_blocks(R, K, rng), R, K)
+        x = torch.randn(M, K, device="cuda")
+        y = torch.empty(M, R, device="cuda")
+        wsb = max(W.workspace_bytes(M), 16)
+        wsp = torch.empty(wsb // 4 + 4, device="cuda")
+        for _ in range(2):
+            W.gemv(x.data_ptr(), M, y.data_ptr(), wsp.data_ptr(), wsb, stream.cuda_stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            W.gemv(x.data_ptr(), M, y.data_ptr(), wsp.data_ptr(), wsb, stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        alg = 2.0 * M * R * K / (us * 1e-6) / 1e12
+        mma = verify_mma_flops(M, R * K) / (us * 1e-6) / 1e12
+        out[f"q4_0 {R}x{K} M={M}"] = {"us": round(us, 1), "tflops": round(alg, 1), "mma_tflops": round(mma, 1),
+                                      "mma_frac": round(mma / tpk, 4)}
+        W.close()
+        del x, y, wsp
+    code = ctypes.c_uint(0)
+    vxb200.check(vxb200.lib().vxc_check_device_error(ctypes.byref(code)), "device error check")
+    out["peak"] = {"tflops": tpk, "source": tkind + " (MEASURED_PEAKS.json bf16; fallback if absent)"}
+    return out
+
+
+def main_q4gemm(args, ws, rank, threads):
+    """The tensor-core GEMM alone (the prompt pass's and wide verifies' kernel):
+    one line, value = algorithmic TFLOP/s over GEMM_SHAPES at --gemm-rows rows
+    (or the single case --gemm-case R,K,M)."""
+    import torch
+    import vxb200
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    vxb200.check(vxb200.lib().vxc_device_init(local), "vxc_device_init")
+    if args.gemm_case:
+        R, K, M = (int(v) for v in args.gemm_case.split(","))
+        cases = [(R, K, M)]
+    else:
+        cases = [(r, k, args.gemm_rows) for (r, k) in GEMM_SHAPES]
+    clk = ClockSampler(local)
+    clk.start()
+    rec = gemm_records(torch, cases, reps=max(args.steps, 1))
+    clocks = clk.stop()
+    tot_us = sum(v["us"] for k, v in rec.items() if k != "peak")
+    flop = sum(2.0 * M * R * K for (R, K, M) in cases)
+    mma = sum(verify_mma_flops(M, R * K) for (R, K, M) in cases)
+    tpk, tkind = tensor_peak()
+    if rank == 0:
+        print(json.dumps({"metric": "Q4_0 GEMM TFLOP/s (7B target matrices, prompt-pass rows)",
+                          "value": round(flop / (tot_us * 1e-6) / 1e12, 1), "unit": "TFLOP/s", "n_gpus": 1,
+                          "steps": args.steps, "warmup": 2, "ms_per_step": round(tot_us / 1e3, 3),
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "f32 (exact fp16 hi/lo products, fp32 accumulation)", "data": "synthetic",
+                          "config": {"workload": "q4gemm: " + ", ".join(f"{R}x{K} M={M}" for (R, K, M) in cases),
+                                     "l2": "no flush: each call writes K-slice partials and outputs far above L2"},
+                          "roofline": {"bound": "tensor", "achieved": round(mma / (tot_us * 1e-6) / 1e12, 1),
+                                       "peak": tpk, "unit": "TFLOP/s",
+                                       "frac": round(mma / (tot_us * 1e-6) / 1e12 / tpk, 4), "traffic": None,
+                                       "peak_source": tkind,
+                                       "note": "achieved = the exact scheme's tensor work (3 fp16 products per "
+                                               "weight x activation) over whole vxc_qgemv calls"},
+                          "cases": rec, "clocks": clocks, "cpu_baseline": None, "e2e": None}))
 
 
 def run_q4matvec_gpu(args, ws, rank, local):
@@ -847,6 +937,7 @@ def main_spec7b(args, ws, rank, threads):
         # configurations 2 and 3 on the same GPU, so the driver's run records them too
         import torch
         subs["q4matvec"] = matvec_records(torch)
+        subs["q4gemm"] = gemm_records(torch)
         a = argparse.Namespace(**vars(args))
         a.steps, a.warmup = 3, 3
         ra = run_accept_gpu(a, 1, 0, int(os.environ.get("LOCAL_RANK", "0")))
@@ -888,7 +979,7 @@ def main_spec7b(args, ws, rank, threads):
             "algorithmic_bytes": int(v_bytes), "weight_bytes": tw // (ws if TP else 1),
             "kv_bytes": int(r["v_kv"] / (ws if TP else 1)),
             "verify_ms": round(r["v_ms"], 4)}
-    # the same verify seen from the tensor pipe: the exact GEMV's MMA work (4 fp16 products per
+    # the same verify seen from the tensor pipe: the exact scheme's MMA work (3 fp16 products per
     # weight x activation product, padded rows included) over the sustained bf16 peak
     rows = SPEC["seqs_per_gpu"] * (SPEC["k"] + 1)
     flops = verify_mma_flops(rows, target_weights(SPEC_TARGET)) / (ws if TP else 1)
@@ -896,7 +987,7 @@ def main_spec7b(args, ws, rank, threads):
     ach = flops / (r["v_ms"] * 1e-3) / 1e12
     tview = {"achieved": round(ach, 1), "peak": tpk, "unit": "TFLOP/s", "frac": round(ach / tpk, 4),
              "mma_flops": int(flops), "peak_source": f"{tpk_kind} (MEASURED_PEAKS.json bf16_tflops_sustained)",
-             "note": "8 x padded rows x weights of this GPU per verify: the exact hi/lo scheme's MMA work"}
+             "note": "6 x padded rows x weights of this GPU per verify: the exact hi/lo scheme's MMA work (3 fp16 products per weight x activation)"}
     if TP:
         # 224 rows: the tensor work takes several times the weight streaming (HBM view kept)
         roof = {"bound": "tensor", "achieved": tview["achieved"], "peak": tpk, "unit": "TFLOP/s",
@@ -1187,7 +1278,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="spec7b",
-                    choices=["spec7b", "spec2l", "spec70b", "spec_tiny", "q4matvec", "accept"],
+                    choices=["spec7b", "spec2l", "spec70b", "spec_tiny", "q4matvec", "q4gemm", "accept"],
                     help="spec2l: spec7b with 2-layer models, the small case for profilers; "
                          "spec70b: configuration 5, the 70B-shape target tensor-parallel over --gpus")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
@@ -1196,6 +1287,8 @@ def main():
     ap.add_argument("--layers", type=int, default=None,
                     help="spec70b: target layers (fewer than 80 = a small functional/profiling case)")
     ap.add_argument("--prompt", type=int, default=None, help="spec70b: prompt ids per sequence")
+    ap.add_argument("--gemm-rows", type=int, default=GEMM_ROWS, help="q4gemm: activation rows")
+    ap.add_argument("--gemm-case", default=None, help="q4gemm: one case R,K,M (a small case for profilers)")
     args = ap.parse_args()
     global SPEC_TARGET, SPEC_DRAFT, TP, TINY
     if args.workload == "spec_tiny":
@@ -1222,6 +1315,8 @@ def main():
         main_spec7b(args, ws, rank, threads)
     elif args.workload == "accept":
         main_accept(args, ws, rank, threads)
+    elif args.workload == "q4gemm":
+        main_q4gemm(args, ws, rank, threads)
     else:
         main_q4matvec(args, ws, rank, threads)
 

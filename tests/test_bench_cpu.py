@@ -56,15 +56,17 @@ def test_accept_and_tiny_reference_arms_print_their_lines():
 def test_roofline_arithmetic_matches_the_configuration_figures():
     """Bytes and flops the bench divides by: 70B target 69.50 G weights and
     39.09 GB of Q4_0 (LM head included, embedding excluded), 3.11e13 flop per
-    224-row verify (2 x rows x weights; the exact scheme's MMA work is 4x
-    that, no padding at 224 rows), 7B target 3.7165 GB, acceptance 90.1 MB."""
+    224-row verify (2 x rows x weights; the exact scheme's MMA work is 3x
+    that, three fp16 products per weight x activation, no padding at 224
+    rows), 7B target 3.7165 GB, acceptance 90.1 MB."""
     sys.path.insert(0, ROOT)
     import bench
     w70 = bench.target_weights(bench.SPEC70_TARGET)
     assert abs(w70 - 69.50e9) < 0.01e9
     assert abs(bench.model_bytes(bench.SPEC70_TARGET) - 39.09e9) < 0.01e9
     assert abs(2 * 224 * w70 - 3.11e13) < 0.01e13
-    assert bench.verify_mma_flops(224, w70) == 4 * 2 * 224 * w70
-    assert bench.verify_mma_flops(40, 1) == 8 * 48          # 40 rows pad to N = 48
+    assert bench.verify_mma_flops(224, w70) == 3 * 2 * 224 * w70
+    assert bench.verify_mma_flops(40, 1) == 6 * 48          # 40 rows pad to N = 48 (GEMV)
+    assert bench.verify_mma_flops(300, 1) == 6 * (256 + 48)  # GEMM slabs of 256 rows, each padded
     assert abs(bench.model_bytes(bench.SPEC_TARGET) - 3.7165e9) < 0.001e9
     assert abs(bench.accept_bytes() - 90.1e6) < 0.1e6
