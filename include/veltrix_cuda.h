@@ -79,7 +79,9 @@ int vxc_qmat_shape(const vxc_qmat *w, int *type, int *rows, int *cols);
 
 /* Bytes of scratch vxc_qgemv (and vxc_qgemv_simt) needs for M activation
  * rows: the split-K partial sums and, above 16 rows, the activation image
- * and its prescales.  Nothing in it has to be initialised. */
+ * and its prescales (from 64 rows: the image in slabs of 256 rows, the
+ * prescales and the GEMM's K-slice sums).  Nothing in it has to be
+ * initialised. */
 size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M);
 
 /* y[m][r] = sum_k W[r][k] * x[m][k] for m < M (fp32 in, fp32 out, device
@@ -87,6 +89,9 @@ size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M);
  * the reference's interleaved nibble order.  Replaces vx_gemv_q4_0
  * (src/quantize.c:728-750), vx_gemv_q4_0_avx2 (src/simd/avx2.c:311-370) and
  * apply_gemv's Q8_0 path (src/model.c:234-244), batched over M rows.
+ * 1-2 rows run on the CUDA cores, up to 63 on the tensor-core GEMV, from 64
+ * on the tensor-core GEMM (weights converted once per 256-row slab; a row's
+ * result does not depend on the other rows). */
  * `workspace` must hold vxc_qgemv_workspace_bytes(w, M) bytes (may be NULL
  * when that is 0). */
 int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, void *workspace,
