@@ -5,16 +5,20 @@ reference's CLI, src/main.c:283-324, one CUDA-graph replay per token).
   (tests/golden) wherever the reference's top-2 margin exceeds 1e-3, the
   same rule as test_model_gpu.py.
 - At 7B width it emits exactly the tokens of a host loop over
-  vx_model_forward with the reference's first-max argmax.
+  vx_model_forward with the reference's first-max argmax, and the tokens of
+  the CPU oracle's greedy loop (oracle/vxo_fwd.c, the reference's scalar
+  forward) wherever the oracle's top-2 margin exceeds 1e-3.
 - eos_id stops the loop without emitting it; cache_len counts every
   forwarded token, so a forward of the last emitted token continues the
   stream.
 """
+import ctypes
 import os
 
 import numpy as np
 import pytest
 
+from _paths import oracle
 import fixtures
 
 pytestmark = pytest.mark.gpu
@@ -30,6 +34,26 @@ def host_loop(m, prompt, n):
         out.append(t)
         lg = m.forward(np.array([t], np.int32))
     return np.array(out, np.int32)
+
+
+def oracle_greedy(path, prompt, n, V=32000):
+    """The oracle's greedy stream (first-max argmax after every forward) and
+    each step's top-2 logit margin."""
+    O = oracle()
+    f32p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    om = O.vxo_model_load(path.encode(), 0)
+    ref = np.zeros(V, np.float32)
+    assert O.vxo_forward(om, f32p(prompt), len(prompt), f32p(ref)) == 0
+    toks, margins = [], []
+    for _ in range(n):
+        top2 = np.partition(ref, -2)[-2:]
+        t = int(np.argmax(ref))
+        toks.append(t)
+        margins.append(float(top2[1] - top2[0]))
+        one = np.array([t], np.int32)
+        assert O.vxo_forward(om, f32p(one), 1, f32p(ref)) == 0
+    O.vxo_model_free(om)
+    return toks, margins
 
 
 def test_greedy_matches_reference_golden(cuda):
@@ -55,6 +79,12 @@ def test_greedy_equals_host_loop_7b_width(cuda):
     got = m.generate_greedy(prompt, 20)
     assert np.array_equal(got, want)
     m.close()
+    # the reference's arithmetic: equal up to the first near-tie of the oracle's logits
+    toks, margins = oracle_greedy(fixtures.path("l7b_2layer"), prompt, 20)
+    for i in range(20):
+        if int(got[i]) != toks[i]:
+            assert margins[i] <= 1e-3, (i, int(got[i]), toks[i], margins[i])
+            break
 
 
 def test_eos_and_continuation(cuda):
