@@ -22,6 +22,8 @@ import vxb200  # noqa: E402
 
 PROMPT70 = np.array([1, 17, 4242, 99, 128000, 31337], np.int32)
 NEXT70 = np.array([777], np.int32)
+# 70 ids: one 64-row chunk on the tensor-core GEMM, then 6 rows on the GEMV
+PROMPT70_LONG = np.random.default_rng(70).integers(0, 128256, 70).astype(np.int32)
 PROMPT_TINY = np.random.default_rng(2024).integers(0, 4096, 32).astype(np.int32)
 
 
@@ -51,6 +53,8 @@ def main():
     m = vxb200.Model(fixtures.path("l70b_2layer"), tp=(rank, world, uid70))
     res["l70_prefill"] = m.forward(PROMPT70)
     res["l70_decode"] = m.forward(NEXT70)
+    m.cache_len = 0
+    res["l70_long_prefill"] = m.forward(PROMPT70_LONG)
     m.close()
     # the same shard generated on the device instead of read from the file
     m = vxb200.Model(None, tp=(rank, world, uids), synth=fixtures.CONFIGS["l70b_2layer"])
