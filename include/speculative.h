@@ -11,7 +11,11 @@
  *     a bonus token from the target when all drafts are accepted.  Uniforms
  *     come from Philox4x32-10 keyed by (seed, token position, sequence id).
  *     top_p is recorded but sampling always uses the full distribution
- *     (top_p = 1).
+ *     (top_p = 1).  The reference applies top_p to the draft side only
+ *     (src/speculative.c:164); with the standard procedure the output
+ *     follows the target's tempered distribution for any draft
+ *     distribution, so the cut would change acceptance rates, not the
+ *     distribution of the output.
  *   - The state keeps its own device KV caches for both models; the models'
  *     own cache_len fields are not modified.
  * Functions return the number of generated tokens (0 on failure) like the
