@@ -91,7 +91,7 @@ size_t vxc_qgemv_workspace_bytes(const vxc_qmat *w, int M);
  * apply_gemv's Q8_0 path (src/model.c:234-244), batched over M rows.
  * 1-2 rows run on the CUDA cores, up to 63 on the tensor-core GEMV, from 64
  * on the tensor-core GEMM (weights converted once per 256-row slab; a row's
- * result does not depend on the other rows). */
+ * result does not depend on the other rows).
  * `workspace` must hold vxc_qgemv_workspace_bytes(w, M) bytes (may be NULL
  * when that is 0). */
 int vxc_qgemv(const vxc_qmat *w, const float *x, int M, float *y, void *workspace,
