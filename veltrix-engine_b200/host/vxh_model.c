@@ -274,7 +274,7 @@ vx_error vx_model_forward(vx_model *model, const int *tokens, int n_tokens, floa
     if (e) return e;
     model->cache_len = keep;
     if (model->cache_len < 0) model->cache_len = 0;
-    if (model->cache_len + n_tokens > m->seqs_ctx) return VX_ERR_PARAM;
+    if ((long long)model->cache_len + n_tokens > m->seqs_ctx) return VX_ERR_PARAM;
     if (vxc_device_current() != m->device) vxc_device_init(m->device);
     double t0 = g_timing ? now_us() : 0.0;
     int rc = vxc_forward_host(m->seqs, 0, model->cache_len, tokens, n_tokens, logits);
