@@ -510,6 +510,41 @@ SPEC_TARGET_2L = (4096, 2, 32, 32, 11008, 32000, 2, 13)
 SPEC_DRAFT_2L = (2048, 2, 32, 4, 5632, 32000, 8, 14)
 
 
+GOLDEN_SEQ0 = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "spec7b_seq0.npz")
+
+
+def first_tokens_vs_golden(first):
+    """Sequence 0's first emitted tokens against the committed CPU greedy stream
+    of the same target and prompt (tests/golden/spec7b_seq0.npz, written by
+    tests/golden/make_spec7b_golden.py from the oracle's scalar forward).  At
+    temperature 0 speculative decoding emits the target's greedy stream, so the
+    benchmark's rule applies: identical up to the first step whose CPU top-2
+    logit margin is at most 1e-3.  Only the full spec7b workload has a golden;
+    None elsewhere, when the file is absent or when it was made for another
+    model or prompt."""
+    try:
+        if TP or TINY or SPEC_TARGET != (4096, 32, 32, 32, 11008, 32000, 2, 11) or SPEC["temp"] != 0.0:
+            return None
+        if not os.path.exists(GOLDEN_SEQ0):
+            return None
+        g = np.load(GOLDEN_SEQ0)
+        if not np.array_equal(g["prompt"], spec_prompts(0, 1)[0]):
+            return None
+        want, marg = g["greedy"], g["margins"]
+        n = min(len(first), len(want))
+        same, ok = 0, True
+        for i in range(n):
+            if int(first[i]) != int(want[i]):
+                ok = bool(marg[i] <= 1e-3)
+                break
+            same += 1
+        return {"match": ok, "identical_prefix": same, "compared": n,
+                "golden": "tests/golden/spec7b_seq0.npz (CPU oracle greedy stream of sequence 0)",
+                "rule": "identical until the first step whose CPU top-2 margin is <= 1e-3"}
+    except Exception as e:   # a report field only: never fail the benchmark over it
+        return {"match": None, "error": repr(e)[:200]}
+
+
 def q_bytes(rows, cols, wtype):
     return rows * (cols // 32) * (18 if wtype == 2 else 34)
 
@@ -1027,6 +1062,9 @@ def main_spec7b(args, ws, rank, threads):
                    "d2h_bytes_per_step": r["d2h"] * ws,
                    "note": "wall time of the vx_speculative_generate_batch calls, prompt pass included"},
            "gpu_launches": r["launches"], "clocks": r["clocks"], "first_tokens_seq0": r["first"]}
+    chk = first_tokens_vs_golden(r["first"])
+    if chk is not None:
+        out["first_tokens_vs_oracle"] = chk
     if "agree" in ex:
         g = ex["agree"]
         out["acceptance"]["full_acceptance"] = {

@@ -70,3 +70,28 @@ def test_roofline_arithmetic_matches_the_configuration_figures():
     assert bench.verify_mma_flops(300, 1) == 6 * (256 + 48)  # GEMM slabs of 256 rows, each padded
     assert abs(bench.model_bytes(bench.SPEC_TARGET) - 3.7165e9) < 0.001e9
     assert abs(bench.accept_bytes() - 90.1e6) < 0.1e6
+
+
+def test_first_tokens_check_against_the_committed_golden():
+    """The spec7b line's `first_tokens_vs_oracle` field: sequence 0's first
+    tokens against tests/golden/spec7b_seq0.npz under the margin rule."""
+    import numpy as np
+    sys.path.insert(0, ROOT)
+    import bench
+    g = np.load(bench.GOLDEN_SEQ0)
+    assert np.array_equal(g["prompt"], bench.spec_prompts(0, 1)[0])
+    want = [int(t) for t in g["greedy"][:8]]
+    ok = bench.first_tokens_vs_golden(want)
+    assert ok["match"] is True and ok["identical_prefix"] == 8 and ok["compared"] == 8
+    # a different token where the CPU margin is clear fails the check
+    i = int(np.argmax(g["margins"][:8] > 1e-3))
+    bad = list(want)
+    bad[i] = (bad[i] + 1) % 32000
+    r = bench.first_tokens_vs_golden(bad)
+    assert r["match"] is False and r["identical_prefix"] == i
+    # other workloads have no golden
+    bench.TINY = True
+    try:
+        assert bench.first_tokens_vs_golden(want) is None
+    finally:
+        bench.TINY = False
