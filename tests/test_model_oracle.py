@@ -57,3 +57,26 @@ def test_forward_bit_exact_vs_reference(name):
     R.vx_model_destroy(h)
     ora = oracle_logits(name, toks)
     assert np.array_equal(ora.view(np.uint32), ref_out.view(np.uint32))
+
+
+@pytest.mark.skipif(not ref_available(), reason="reference build not available")
+@pytest.mark.parametrize("name,n", [("l7b_2layer", 6), ("d11b_2layer", 12), ("l70b_2layer", 3)])
+def test_forward_bit_exact_vs_reference_at_benchmark_widths(name, n):
+    """The same pin at the widths the GPU tests compare against the oracle:
+    7B width (32 heads of 128), the 1.1B draft shape (GQA 32/4, heads of 64)
+    and the 70B width (GQA 64/8, theta 5e5, vocabulary 128256), 2 layers each
+    (reference src/model.c:391-628, GQA map :303)."""
+    R = ref()
+    h = ctypes.c_void_p()
+    assert R.vx_model_create(fixtures.path(name).encode(), ctypes.byref(h)) == 0
+    cfg = (ctypes.c_int * 8)()
+    R.vxref_config(h, cfg)
+    e, L, H, KH, F, V = fixtures.CONFIGS[name][:6]
+    assert list(cfg)[:7] == [L, H, KH, e, e // H, F, V]
+    toks = np.random.default_rng(12345).integers(0, V, n).astype(np.int32)
+    ref_out = np.zeros((n, V), np.float32)
+    for i, t in enumerate(toks):
+        assert R.vx_model_forward(h, f32p(np.array([t], np.int32)), 1, f32p(ref_out[i])) == 0
+    R.vx_model_destroy(h)
+    ora = oracle_logits(name, toks)
+    assert np.array_equal(ora.view(np.uint32), ref_out.view(np.uint32))
